@@ -1,0 +1,318 @@
+"""Benchmark of the dendritic matrix tick (one JSON line on stdout).
+
+Workload (BASELINE.json metric): N=166,000 neurons, M=24,988,875 edges
+(``random_topology(166000, 25_000_000, seed=0)``, the reference generator's
+stream), B=1, fp32 weights, constant drives 0.2 / 0.1.  A step is one tick.
+
+* ``value``     synapse-updates/s = M*B / tick time, inputs resident in HBM,
+                ticks replayed from a captured CUDA graph (the multi-tick path).
+* ``e2e``       the same metric through the public API: every step copies the
+                step's drive [B,N] from pinned host memory to the device, calls
+                ``NativeDendriticMatrixRuntime.step`` and copies the new state
+                back to pinned host memory.
+* ``roofline``  HBM roofline of the tick kernel: algorithmic bytes
+                M*(w+4) + 4*(N+1) + 24*B*N per launch over the measured launch
+                duration, against MEASURED_PEAKS.json's hbm_gbs.
+* ``cpu_baseline``  the CPU oracle (a C restatement of the reference tick,
+                OpenMP over all host cores) on a bounded sample of the same ticks.
+
+``--impl reference`` times that CPU implementation alone (the reference path
+is Python/PyTorch-CPU and cannot run on the GPU box; its arithmetic is the
+oracle's).  ``--gpus N`` under torchrun shards destination rows across ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from neurosim_gpu_b200 import (DendriticDynamics, Dynamics,  # noqa: E402
+                               NativeDendriticMatrixRuntime, random_topology)
+
+WORKLOADS = {
+    # name: (neurons, candidate edges, batch, precision)
+    "matrix_n166k_m25M_b1_fp32": (166_000, 25_000_000, 1, "fp32"),
+    "matrix_n166k_m25M_b1_nvfp4": (166_000, 25_000_000, 1, "nvfp4"),
+    "matrix_n166k_m10M_b1_fp32": (166_000, 10_000_000, 1, "fp32"),
+    "matrix_n166k_m10M_b1_fp16": (166_000, 10_000_000, 1, "fp16"),
+    "matrix_n166k_m10M_b1_fp8": (166_000, 10_000_000, 1, "fp8"),
+    "matrix_n166k_m10M_b1_nvfp4": (166_000, 10_000_000, 1, "nvfp4"),
+    "matrix_n166k_m25M_b8_fp32": (166_000, 25_000_000, 8, "fp32"),
+    "matrix_n50k_m1M_b8_fp32": (50_000, 1_000_000, 8, "fp32"),
+    "matrix_n4096_m65k_b1_fp32": (4096, 65_536, 1, "fp32"),
+    "matrix_n1330k_m200M_b1_fp32": (1_330_000, 200_000_000, 1, "fp32"),
+}
+DEFAULT_WORKLOAD = "matrix_n166k_m25M_b1_fp32"
+WEIGHT_BYTES = {"fp32": 4.0, "fp16": 2.0, "fp8": 1.0, "nvfp4": 0.5 + 1.0 / 16.0}
+FALLBACK_HBM_GBS = 6650.0
+
+
+def algorithmic_bytes(neurons: int, edges: int, batch: int, precision: str) -> float:
+    """M*(w + 4) + 4*(N+1) + 24*B*N (+4 B of global scale for fp8 / nvfp4)."""
+    extra = 4 if precision in ("fp8", "nvfp4") else 0
+    return edges * (WEIGHT_BYTES[precision] + 4) + 4 * (neurons + 1) + 24 * batch * neurons + extra
+
+
+def hbm_peak() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(workload: str) -> float | None:
+    """DRAM bytes per launch recorded from an ncu capture (profiles/traffic.txt)."""
+    path = ROOT / "profiles" / "traffic.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == workload and not line.startswith("#"):
+            return float(parts[1])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the GPU works."""
+
+    QUERY = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.samples: list[list[str]] = []
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}",
+                                      f"--query-gpu={self.QUERY}",
+                                      "--format=csv,noheader,nounits"],
+                                     capture_output=True, text=True, timeout=5).stdout
+                row = [v.strip() for v in out.strip().split(",")]
+                if len(row) == 7:
+                    self.samples.append(row)
+            except (OSError, subprocess.SubprocessError):
+                pass
+            self._stop.wait(0.1)
+
+    def __enter__(self):
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self._stop.set()
+        self._thread.join()
+
+    def summary(self) -> dict:
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[0]) for r in self.samples if r[0].replace(".", "").isdigit()]
+        reasons = sorted({names[i] for r in self.samples for i in range(4)
+                          if r[3 + i].lower() in ("active", "1")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(self.samples[0][1]) if self.samples[0][1].isdigit() else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def bench_model(neurons: int, device) -> DendriticDynamics:
+    soma = Dynamics(torch.full((neurons,), 0.72, device=device),
+                    torch.full((neurons,), 0.8, device=device))
+    return DendriticDynamics.from_time_constants(soma, dt=1.0, tau_dendrite=4.0,
+                                                 tau_adaptation=25.0, coupling=0.5,
+                                                 adaptation_strength=0.2)
+
+
+def cpu_oracle_rate(graph, batch: int, seconds: float, max_ticks: int | None = None):
+    """Synapse-updates/s of the C oracle tick over all host cores, bounded by time."""
+    import numpy as np
+
+    import oracle
+    n = graph.n_neurons
+    csr = oracle.CSR.make(n, graph.in_rowptr.cpu().numpy(), graph.in_col.cpu().numpy(),
+                          graph.in_weight.detach().cpu().numpy())
+    model = bench_model(n, "cpu")
+    params = [p.numpy() for p in model.parameters()]
+    s = np.zeros((batch, n), np.float32)
+    d, a = np.zeros_like(s), np.zeros_like(s)
+    u, v = np.full_like(s, 0.2), np.full_like(s, 0.1)
+    s, d, a = oracle.matrix_tick(csr, s, d, a, params, u, v)  # warm caches / threads
+    ticks, start = 0, time.perf_counter()
+    while True:
+        s, d, a = oracle.matrix_tick(csr, s, d, a, params, u, v)
+        ticks += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= seconds or (max_ticks is not None and ticks >= max_ticks):
+            break
+    per_tick = elapsed / ticks
+    return graph.n_edges * batch / per_tick, per_tick, ticks, oracle.max_threads()
+
+
+def build_graph(neurons: int, edges: int, device):
+    # CPU draws (the reference's random stream), canonicalised on the GPU.
+    return random_topology(neurons, edges, device="cpu", seed=0, build_device=device)
+
+
+def run_reference(args, workload: str) -> dict:
+    neurons, edges, batch, precision = WORKLOADS[workload]
+    graph = random_topology(neurons, edges, device="cpu", seed=0)
+    for _ in range(args.warmup):
+        pass
+    rate, per_tick, ticks, cores = cpu_oracle_rate(graph, batch, seconds=1e9,
+                                                   max_ticks=max(args.steps, 1))
+    return {
+        "metric": "synapse-updates/s (M*B/tick)", "value": rate, "unit": "synapse-updates/s",
+        "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_tick * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference random_topology stream, seed 0)",
+        "config": {"workload": workload, "neurons": neurons, "edges": graph.n_edges,
+                   "batch": batch, "weights": "fp32"},
+        "cpu_baseline": {"value": rate, "unit": "synapse-updates/s", "cores": cores,
+                         "kind": "port", "sample": f"{ticks} ticks of the full graph"},
+        "e2e": {"value": rate, "unit": "synapse-updates/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def run_native(args, workload: str) -> dict:
+    neurons, edges, batch, precision = WORKLOADS[workload]
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    graph = build_graph(neurons, edges, device)
+    model = bench_model(neurons, device)
+    runtime = NativeDendriticMatrixRuntime(graph, model, torch.zeros(batch, neurons, device=device),
+                                           precision=precision)
+    chunk = 64
+    with torch.inference_mode():
+        # Warm-up (includes graph capture and weight packing).
+        runtime.run(max(args.warmup, 1) * 1, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
+        steps = max(args.steps - args.steps % chunk, chunk)
+        runtime.run(chunk, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
+        torch.cuda.synchronize()
+        sampler = ClockSampler(torch.cuda.current_device())
+        with sampler:
+            # Busy pre-roll so the first samples already see the loaded clock.
+            pre = time.perf_counter()
+            while time.perf_counter() - pre < 0.3:
+                runtime.run(chunk * 4, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
+                torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            start.record()
+            runtime.run(steps, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
+            end.record()
+            end.synchronize()
+            post = time.perf_counter()
+            while time.perf_counter() - post < 0.3:
+                runtime.run(chunk * 4, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
+                torch.cuda.synchronize()
+        total_ms = start.elapsed_time(end)
+        tick_ms = total_ms / steps
+
+        # Launch durations bracketed one by one (eager ticks).
+        events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(50)]
+        for e0, e1 in events:
+            e0.record()
+            runtime.step(0.2, dendritic_drive=0.1)
+            e1.record()
+        torch.cuda.synchronize()
+        launch_ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in events)
+
+        # End to end through the public API with host buffers.
+        e2e_steps = min(steps, 2000)
+        host_drive = torch.full((batch, neurons), 0.2).pin_memory()
+        host_state = torch.empty((batch, neurons)).pin_memory()
+        dev_drive = torch.empty((batch, neurons), device=device)
+        for _ in range(3):
+            dev_drive.copy_(host_drive, non_blocking=True)
+            host_state.copy_(runtime.step(dev_drive, dendritic_drive=0.1), non_blocking=True)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        wall = time.perf_counter()
+        e0.record()
+        for _ in range(e2e_steps):
+            dev_drive.copy_(host_drive, non_blocking=True)
+            host_state.copy_(runtime.step(dev_drive, dendritic_drive=0.1), non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        wall = time.perf_counter() - wall
+        e2e_ms = max(e0.elapsed_time(e1), wall * 1e3) / e2e_steps
+
+    m = graph.n_edges
+    rate = m * batch / (tick_ms * 1e-3)
+    peak, peak_kind = hbm_peak()
+    algo = algorithmic_bytes(neurons, m, batch, precision)
+    achieved = algo / (tick_ms * 1e-3) / 1e9
+    result = {
+        "metric": "synapse-updates/s (M*B/tick)", "value": rate, "unit": "synapse-updates/s",
+        "n_gpus": 1, "steps": steps, "warmup": args.warmup, "ms_per_step": tick_ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (reference random_topology stream, seed 0; drives 0.2/0.1)",
+        "config": {"workload": workload, "neurons": neurons, "edges": m, "batch": batch,
+                   "weights": precision, "parallelism": "single GPU",
+                   "l2": "inputs larger than L2 (edge stream %.0f MB vs 126 MB)" % (algo / 1e6),
+                   "ticks_per_graph": chunk},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": ncu_traffic(workload),
+                     "algorithmic_bytes_per_launch": algo, "peak_source": peak_kind,
+                     "launch_ms_graph": tick_ms, "launch_ms_eager_median": launch_ms},
+        "e2e": {"value": m * batch / (e2e_ms * 1e-3), "unit": "synapse-updates/s",
+                "h2d_bytes_per_step": 4 * batch * neurons, "d2h_bytes_per_step": 4 * batch * neurons,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": steps,
+        "clocks": sampler.summary(),
+    }
+    if not args.skip_cpu_baseline:
+        rate_cpu, per_tick, ticks, cores = cpu_oracle_rate(graph, batch, seconds=args.cpu_seconds)
+        result["cpu_baseline"] = {"value": rate_cpu, "unit": "synapse-updates/s", "cores": cores,
+                                  "kind": "port",
+                                  "sample": f"{ticks} ticks of the full graph "
+                                            f"({per_tick * 1e3:.2f} ms/tick)"}
+    return result
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=4096)
+    parser.add_argument("--warmup", type=int, default=64)
+    parser.add_argument("--impl", choices=("native", "reference"), default="native")
+    parser.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--skip-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args, args.workload)))
+        return
+    if world > 1 or args.gpus > 1:
+        from neurosim_gpu_b200.sharded import bench_sharded
+        result = bench_sharded(args, WORKLOADS[args.workload], args.workload)
+        if result is not None and rank == 0:
+            print(json.dumps(result))
+        return
+    print(json.dumps(run_native(args, args.workload)))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,182 @@
+/*
+ * neurosim_b200.h -- C ABI of the B200 dendritic tick library (libneurosim_b200.so).
+ *
+ * The library replaces the native extension of NeuroSim-GPU for the dendritic
+ * hot path.  Its entry points are the FFI a host binds instead of the
+ * reference's pybind11 module `neurosim_gpu_native`:
+ *
+ *   nsb_dendritic_step   <- dendritic_step   (csrc/bindings.cpp:137-142,
+ *                                             csrc/compartmental.cu:176-236)
+ *   nsb_dendritic_event  <- dendritic_event  (csrc/bindings.cpp:143,
+ *                                             csrc/compartmental.cu:238-273)
+ *   nsb_csr_propagate    <- the j = W @ x product the runtime needs for its
+ *                           persistent current (runtime.py:217-223, which the
+ *                           reference computes with cuSPARSE via torch.sparse.mm)
+ *
+ * Conventions
+ *  - Every pointer is a device pointer unless stated otherwise.  Nothing is
+ *    retained after a call returns; nothing is allocated by the library.
+ *  - A [B,N] operand is an nsb_view: element (b, n) lives at
+ *    data[b * batch_stride + n * neuron_stride] (strides in elements, any
+ *    sign-free value, 0 for broadcast).  A view whose data is NULL reads as the
+ *    constant `scalar` everywhere (the reference's `input=None, input_scalar=x`).
+ *  - Outputs are nsb_out views; they must not overlap any input.
+ *  - All work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *    stream).  No call synchronises the host or allocates, so every call can be
+ *    captured into a CUDA graph.
+ *  - Return value: NSB_OK, or a negative code after which nothing was
+ *    enqueued; nsb_last_error() then returns the message (thread-local).
+ *    Invalid arguments are rejected before any launch (the reference raises
+ *    RuntimeError from TORCH_CHECK at the same points).
+ */
+#ifndef NEUROSIM_B200_H
+#define NEUROSIM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define NSB_API __attribute__((visibility("default")))
+#else
+#define NSB_API
+#endif
+
+#define NSB_ABI_VERSION 1
+
+enum nsb_status {
+  NSB_OK = 0,
+  NSB_ERR_ARGUMENT = -1, /* invalid shape, stride, geometry or null pointer   */
+  NSB_ERR_CUDA = -2,     /* a CUDA runtime call failed (message says which)  */
+  NSB_ERR_WORKSPACE = -3 /* workspace missing, misaligned or too small        */
+};
+
+/* Weight storage of the destination-major CSR (csrc/compartmental.cu:92-119). */
+enum nsb_weight_format {
+  NSB_WEIGHT_F32 = 0,   /* float[M]                                            */
+  NSB_WEIGHT_F16 = 1,   /* IEEE half[M]                                        */
+  NSB_WEIGHT_E4M3 = 2,  /* uint8 E4M3FN codes[M] x *global_scale               */
+  NSB_WEIGHT_NVFP4 = 3  /* uint8[(M+1)/2]: E2M1 codes, edge 2i in the low
+                           nibble of byte i; block_scales[(M+15)/16] E4M3 per
+                           16 consecutive edges; x *global_scale               */
+};
+
+typedef struct nsb_view {
+  const float* data;     /* NULL -> constant `scalar`                          */
+  int64_t batch_stride;  /* elements between (b, n) and (b+1, n)              */
+  int64_t neuron_stride; /* elements between (b, n) and (b, n+1)              */
+  float scalar;
+} nsb_view;
+
+typedef struct nsb_out {
+  float* data;
+  int64_t batch_stride;
+  int64_t neuron_stride;
+} nsb_out;
+
+/* The six per-neuron parameter vectors, in this order:
+ * alpha, gain, dendrite_decay, adaptation_decay, coupling, adaptation_strength
+ * (native_compartmental.py:20-23).  stride[i] is in elements. */
+typedef struct nsb_params {
+  const float* data[6];
+  int64_t stride[6];
+} nsb_params;
+
+/* Everything one tick reads besides the synaptic current. */
+typedef struct nsb_tick {
+  int64_t batch;   /* B >= 0                                                    */
+  int64_t neurons; /* N >= 1                                                    */
+  nsb_view state, dendrite, adaptation; /* s_t, d_t, a_t                        */
+  nsb_view input;           /* soma drive u_t (added inside the soma tanh)      */
+  nsb_view dendritic_input; /* dendritic drive v_t (added inside the dendrite tanh) */
+  nsb_params params;
+} nsb_tick;
+
+/* s_{t+1}, d_{t+1}, a_{t+1}. */
+typedef struct nsb_tick_out {
+  nsb_out state, dendrite, adaptation;
+} nsb_tick_out;
+
+/* Destination-major CSR W[dst, src]: the reference's in_rowptr / in_col /
+ * in_weight (topology.py:85-93), optionally in a packed weight format. */
+typedef struct nsb_csr {
+  int64_t n_edges;        /* M                                                 */
+  const int32_t* rowptr;  /* [N+1], rowptr[0] = 0, rowptr[N] = M               */
+  const int32_t* col;     /* [M] source neuron of each edge                    */
+  const void* weight;     /* see nsb_weight_format                             */
+  int32_t format;         /* enum nsb_weight_format                            */
+  const uint8_t* block_scales; /* NVFP4 only                                   */
+  const float* global_scale;   /* E4M3 / NVFP4 only: one float on the device  */
+} nsb_csr;
+
+/* Source-major CSR of the same edges for the event scatter: out_rowptr / dst
+ * (topology.py:83, 105-115) and a weight per edge.  With weight_index NULL,
+ * weight[e] is the weight of source-major edge e (the reference's
+ * topology.weight, read coalesced); otherwise weight is the destination-major
+ * in_weight and edge e uses weight[weight_index[e]] (the reference call,
+ * native_compartmental.py:171-172). */
+typedef struct nsb_out_csr {
+  int64_t n_edges;
+  const int32_t* rowptr;       /* [N+1] */
+  const int32_t* dst;          /* [M]   */
+  const int32_t* weight_index; /* [M] or NULL */
+  const float* weight;         /* [M]   */
+} nsb_out_csr;
+
+/* Matrix tick (replaces dendritic_step): j = W @ s_t, then
+ *   d' = rd*d + (1-rd)*tanh(j + v)
+ *   s' = clamp(alpha*s + (1-alpha)*gain*tanh((1-c)*j + c*d' - k*a + u), 0, 1)
+ *   a' = ra*a + (1-ra)*s'
+ * `width` is the number of lanes that share one destination row: 4, 8, 16 or 32
+ * (the reference accepts 8/16/32), or 0 to let the library choose from the
+ * mean degree.  One launch; edges are streamed once for every 8 batch rows. */
+NSB_API int nsb_dendritic_step(const nsb_tick* tick, const nsb_csr* csr, int32_t width,
+                       const nsb_tick_out* out, void* stream);
+
+/* result[b, n] = sum over in-edges of n of w[e] * source[b, col[e]]
+ * (one launch, no state update), for any weight format.  Used for the PELS
+ * persistent current; with one edge per row and source = 1 it returns the
+ * decoded weights themselves. */
+NSB_API int nsb_csr_propagate(int64_t batch, int64_t neurons, const nsb_csr* csr,
+                      const nsb_view* source, const nsb_out* result, void* stream);
+
+/* Workspace of nsb_dendritic_event, in bytes, for B x N (256-byte aligned,
+ * caller-owned device memory; contents need not be initialised). */
+NSB_API size_t nsb_dendritic_event_workspace_size(int64_t batch, int64_t neurons);
+
+/* Layout of the workspace head after nsb_dendritic_event has run: */
+typedef struct nsb_event_counters {
+  uint32_t emitted_sources;   /* (b, n) pairs queued for the scatter            */
+  uint32_t reserved;
+  uint64_t active_neurons;    /* (b, n) pairs with |s' - emitted| >= theta      */
+  uint64_t active_edges;      /* sum of out-degree over active pairs            */
+  uint64_t reserved2;
+} nsb_event_counters;
+
+/* PELS tick (replaces dendritic_event):
+ *   s', d', a' = the matrix-tick update with j = current
+ *   active     = |s' - emitted| >= theta[n]
+ *   emitted'   = active ? s' : emitted
+ *   current   += W @ (active ? s' - emitted : 0)     (in place, float atomics)
+ * `current` is a contiguous [B,N] array.  Two launches plus one 32-byte
+ * memset; the scatter only visits the out-edges of active sources. */
+NSB_API int nsb_dendritic_event(const nsb_tick* tick, float* current, const nsb_view* emitted,
+                        const float* theta, int64_t theta_stride,
+                        const nsb_out_csr* out_csr, const nsb_tick_out* out,
+                        const nsb_out* out_emitted, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* Thread-local message of the last failing call ("" if none). */
+NSB_API const char* nsb_last_error(void);
+
+/* NSB_ABI_VERSION of the loaded library. */
+NSB_API int nsb_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NEUROSIM_B200_H */

@@ -1,0 +1,194 @@
+// capi.cu -- extern "C" entry points of libneurosim_b200.so (see include/neurosim_b200.h).
+//
+// Each entry point validates its arguments completely before it enqueues
+// anything, mirroring the TORCH_CHECKs of the reference extension
+// (csrc/compartmental.cu:29-70, 182-210, 244-256): on failure it returns a
+// negative status, leaves the stream untouched and records a message for
+// nsb_last_error().
+#include <cstdio>
+#include <string>
+
+#include "nsb_launch.h"
+
+namespace nsb {
+size_t event_workspace_bytes(int64_t batch, int64_t neurons);
+}  // namespace nsb
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const std::string& message) {
+  g_error = message;
+  return code;
+}
+
+int cuda_fail(cudaError_t err, const char* where) {
+  return fail(NSB_ERR_CUDA, std::string(where) + ": " + cudaGetErrorName(err) + " (" +
+                                cudaGetErrorString(err) + ")");
+}
+
+nsb::View to_view(const nsb_view& v) { return {v.data, v.batch_stride, v.neuron_stride, v.scalar}; }
+nsb::Out to_out(const nsb_out& o) { return {o.data, o.batch_stride, o.neuron_stride}; }
+
+// Shared checks of the tick operands; fills `t`.
+bool check_tick(const nsb_tick* tick, nsb::TickArgs* t) {
+  if (!tick) return fail(NSB_ERR_ARGUMENT, "tick arguments are required"), false;
+  if (tick->batch < 0 || tick->neurons <= 0)
+    return fail(NSB_ERR_ARGUMENT, "state must be [B,N], N > 0"), false;
+  if (tick->batch > 0 && (!tick->state.data || !tick->dendrite.data || !tick->adaptation.data))
+    return fail(NSB_ERR_ARGUMENT, "state, dendrite and adaptation must be arrays"), false;
+  for (int i = 0; i < 6; ++i)
+    if (!tick->params.data[i])
+      return fail(NSB_ERR_ARGUMENT, "six neuron parameter vectors are required"), false;
+  if (tick->batch * tick->neurons >= (int64_t(1) << 32))
+    return fail(NSB_ERR_ARGUMENT, "B*N must be below 2^32"), false;
+  t->batch = tick->batch;
+  t->neurons = tick->neurons;
+  t->s = to_view(tick->state);
+  t->d = to_view(tick->dendrite);
+  t->a = to_view(tick->adaptation);
+  t->u = to_view(tick->input);
+  t->v = to_view(tick->dendritic_input);
+  for (int i = 0; i < 6; ++i) {
+    t->p.data[i] = tick->params.data[i];
+    t->p.stride[i] = tick->params.stride[i];
+  }
+  return true;
+}
+
+bool check_out(const nsb_out& o, const char* name) {
+  if (!o.data) return fail(NSB_ERR_ARGUMENT, std::string(name) + " output is required"), false;
+  return true;
+}
+
+bool check_csr(const nsb_csr* csr, nsb::Csr* c) {
+  if (!csr) return fail(NSB_ERR_ARGUMENT, "CSR arguments are required"), false;
+  if (csr->n_edges < 0 || csr->n_edges >= (int64_t(1) << 31))
+    return fail(NSB_ERR_ARGUMENT, "invalid CSR geometry: edge count must be in [0, 2^31)"), false;
+  if (!csr->rowptr) return fail(NSB_ERR_ARGUMENT, "invalid CSR geometry: rowptr is required"), false;
+  if (csr->n_edges > 0 && (!csr->col || !csr->weight))
+    return fail(NSB_ERR_ARGUMENT, "invalid CSR geometry: col and weight are required"), false;
+  switch (csr->format) {
+    case NSB_WEIGHT_F32:
+    case NSB_WEIGHT_F16:
+      if (csr->block_scales || csr->global_scale)
+        return fail(NSB_ERR_ARGUMENT, "invalid floating-point CSR weights: scales given"), false;
+      break;
+    case NSB_WEIGHT_E4M3:
+      if (!csr->global_scale)
+        return fail(NSB_ERR_ARGUMENT, "quantized CSR weights require a global scale"), false;
+      if (csr->block_scales)
+        return fail(NSB_ERR_ARGUMENT, "E4M3 CSR weights take no block scales"), false;
+      break;
+    case NSB_WEIGHT_NVFP4:
+      if (!csr->global_scale)
+        return fail(NSB_ERR_ARGUMENT, "quantized CSR weights require a global scale"), false;
+      if (csr->n_edges > 0 && !csr->block_scales)
+        return fail(NSB_ERR_ARGUMENT, "invalid NVFP4 block scales"), false;
+      break;
+    default:
+      return fail(NSB_ERR_ARGUMENT, "unknown CSR weight format"), false;
+  }
+  *c = {csr->n_edges, csr->rowptr, csr->col, csr->weight, csr->format, csr->block_scales,
+        csr->global_scale};
+  return true;
+}
+
+bool check_width(int32_t width) {
+  if (width == 0 || width == 4 || width == 8 || width == 16 || width == 32) return true;
+  fail(NSB_ERR_ARGUMENT, "width must be 4, 8, 16 or 32 (0 = automatic)");
+  return false;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* nsb_last_error(void) { return g_error.c_str(); }
+
+int nsb_abi_version(void) { return NSB_ABI_VERSION; }
+
+int nsb_dendritic_step(const nsb_tick* tick, const nsb_csr* csr, int32_t width,
+                       const nsb_tick_out* out, void* stream) {
+  nsb::TickArgs t;
+  nsb::Csr c;
+  if (!check_tick(tick, &t) || !check_csr(csr, &c) || !check_width(width)) return NSB_ERR_ARGUMENT;
+  if (!out) return fail(NSB_ERR_ARGUMENT, "outputs are required");
+  if (!check_out(out->state, "state") || !check_out(out->dendrite, "dendrite") ||
+      !check_out(out->adaptation, "adaptation"))
+    return NSB_ERR_ARGUMENT;
+  g_error.clear();
+  if (t.batch == 0) return NSB_OK;
+  const nsb::TickOut o{to_out(out->state), to_out(out->dendrite), to_out(out->adaptation)};
+  const cudaError_t err = nsb::launch_csr(t, t.s, c, width, true, o, nsb::Out{nullptr, 0, 0},
+                                          static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_step launch");
+  return NSB_OK;
+}
+
+int nsb_csr_propagate(int64_t batch, int64_t neurons, const nsb_csr* csr,
+                      const nsb_view* source, const nsb_out* result, void* stream) {
+  nsb::Csr c;
+  if (batch < 0 || neurons <= 0) return fail(NSB_ERR_ARGUMENT, "source must be [B,N], N > 0");
+  if (!check_csr(csr, &c)) return NSB_ERR_ARGUMENT;
+  if (!source || !result || (batch > 0 && (!source->data || !result->data)))
+    return fail(NSB_ERR_ARGUMENT, "source and result arrays are required");
+  g_error.clear();
+  if (batch == 0) return NSB_OK;
+  nsb::TickArgs t{};
+  t.batch = batch;
+  t.neurons = neurons;
+  const nsb::TickOut none{};
+  const cudaError_t err = nsb::launch_csr(t, to_view(*source), c, 0, false, none,
+                                          to_out(*result), static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_csr_propagate launch");
+  return NSB_OK;
+}
+
+size_t nsb_dendritic_event_workspace_size(int64_t batch, int64_t neurons) {
+  if (batch < 0 || neurons < 0) return 0;
+  return nsb::event_workspace_bytes(batch, neurons);
+}
+
+int nsb_dendritic_event(const nsb_tick* tick, float* current, const nsb_view* emitted,
+                        const float* theta, int64_t theta_stride, const nsb_out_csr* out_csr,
+                        const nsb_tick_out* out, const nsb_out* out_emitted, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  nsb::TickArgs t;
+  if (!check_tick(tick, &t)) return NSB_ERR_ARGUMENT;
+  if (t.batch > 0 && (!current || !emitted || !emitted->data))
+    return fail(NSB_ERR_ARGUMENT, "persistent current and emitted state are required");
+  if (!theta) return fail(NSB_ERR_ARGUMENT, "theta must have N values");
+  if (!out_csr || !out_csr->rowptr || out_csr->n_edges < 0 || out_csr->n_edges >= (int64_t(1) << 31) ||
+      (out_csr->n_edges > 0 && (!out_csr->dst || !out_csr->weight)))
+    return fail(NSB_ERR_ARGUMENT, "invalid event topology geometry");
+  if (!out || !out_emitted) return fail(NSB_ERR_ARGUMENT, "outputs are required");
+  if (!check_out(out->state, "state") || !check_out(out->dendrite, "dendrite") ||
+      !check_out(out->adaptation, "adaptation") || !check_out(*out_emitted, "emitted"))
+    return NSB_ERR_ARGUMENT;
+  const size_t need = nsb::event_workspace_bytes(t.batch, t.neurons);
+  if (!workspace || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+    return fail(NSB_ERR_WORKSPACE, "event workspace must be 256-byte aligned and at least " +
+                                       std::to_string(need) + " bytes");
+  g_error.clear();
+  if (t.batch == 0) return NSB_OK;
+  nsb::EventArgs e;
+  e.current = current;
+  e.current_out = current;
+  e.emitted = to_view(*emitted);
+  e.theta = theta;
+  e.theta_stride = theta_stride;
+  e.out_rowptr = out_csr->rowptr;
+  e.dst = out_csr->dst;
+  e.weight_index = out_csr->weight_index;
+  e.weight = out_csr->weight;
+  e.n_edges = out_csr->n_edges;
+  const nsb::TickOut o{to_out(out->state), to_out(out->dendrite), to_out(out->adaptation)};
+  const cudaError_t err = nsb::launch_event(t, e, o, to_out(*out_emitted), workspace,
+                                            static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_event launch");
+  return NSB_OK;
+}
+
+}  // extern "C"

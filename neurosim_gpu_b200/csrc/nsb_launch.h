@@ -1,0 +1,53 @@
+// nsb_launch.h -- host-side launchers shared by the C ABI (capi.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "nsb_device.cuh"
+
+namespace nsb {
+
+// Destination-major CSR as the kernels see it.
+struct Csr {
+  int64_t n_edges;
+  const int32_t* rowptr;
+  const int32_t* col;
+  const void* weight;
+  int32_t format;
+  const uint8_t* block_scales;
+  const float* global_scale;
+};
+
+// Per-device facts, queried once per device.
+struct DeviceInfo {
+  int sm_count;
+};
+cudaError_t device_info(DeviceInfo* info);
+
+// Lanes that share one row, chosen from the mean degree (width == 0) or given.
+int choose_group_width(int64_t n_edges, int64_t neurons);
+
+// Matrix tick (update = true) or plain product j = W @ x (update = false,
+// written to `product`).  `x` is the gathered operand (the state for a tick).
+cudaError_t launch_csr(const TickArgs& t, const View& x, const Csr& csr, int width,
+                       bool update, const TickOut& out, const Out& product,
+                       cudaStream_t stream);
+
+struct EventArgs {
+  const float* current;  // contiguous [B,N]; updated in place by the scatter
+  float* current_out;
+  View emitted;
+  const float* theta;
+  int64_t theta_stride;
+  const int32_t* out_rowptr;
+  const int32_t* dst;
+  const int32_t* weight_index;  // nullptr: weight is source-major
+  const float* weight;
+  int64_t n_edges;
+};
+
+cudaError_t launch_event(const TickArgs& t, const EventArgs& e, const TickOut& out,
+                         const Out& out_emitted, void* workspace, cudaStream_t stream);
+
+}  // namespace nsb

@@ -1,0 +1,347 @@
+"""ctypes binding of ``libneurosim_b200.so`` and the drop-in extension object.
+
+``load_native_extension()`` returns an object with the hot-path functions of
+the reference's pybind11 module ``neurosim_gpu_native``
+(csrc/bindings.cpp:137-143):
+
+* ``dendritic_step(state, dendrite, adaptation, params, rowptr, source, weight,
+  input, input_scalar, dendritic_input, dendritic_scalar, width,
+  block_scales=None, global_scale=None) -> [s, d, a]``
+* ``dendritic_event(state, dendrite, adaptation, params, current, emitted,
+  theta, out_rowptr, dst, out_weight_index, weight, input, input_scalar,
+  dendritic_input, dendritic_scalar) -> [s, d, a, emitted]`` (updates
+  ``current`` in place)
+
+with the same argument meaning, the same ownership (inputs borrowed; outputs
+are fresh views of one allocation) and the same errors (``RuntimeError``
+before any launch, csrc/compartmental.cu:29-70, 182-210, 244-256).  Calls go
+to the C ABI on the caller's current CUDA stream, so they can be captured in
+CUDA graphs.  ``dendritic_event`` also accepts ``out_weight_index=None`` with
+the source-major ``topology.weight``, which the scatter reads coalesced.
+
+There is no fallback: if the library is missing or the tensors are not CUDA
+float32, the call fails.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import functools
+from pathlib import Path
+
+import torch
+
+LIBRARY_PATH = Path(__file__).resolve().parent / "libneurosim_b200.so"
+
+F32, F16, E4M3, NVFP4 = 0, 1, 2, 3
+
+
+class _View(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("batch_stride", ctypes.c_int64),
+                ("neuron_stride", ctypes.c_int64), ("scalar", ctypes.c_float)]
+
+
+class _Out(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("batch_stride", ctypes.c_int64),
+                ("neuron_stride", ctypes.c_int64)]
+
+
+class _Params(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p * 6), ("stride", ctypes.c_int64 * 6)]
+
+
+class _Tick(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int64), ("neurons", ctypes.c_int64),
+                ("state", _View), ("dendrite", _View), ("adaptation", _View),
+                ("input", _View), ("dendritic_input", _View), ("params", _Params)]
+
+
+class _TickOut(ctypes.Structure):
+    _fields_ = [("state", _Out), ("dendrite", _Out), ("adaptation", _Out)]
+
+
+class _Csr(ctypes.Structure):
+    _fields_ = [("n_edges", ctypes.c_int64), ("rowptr", ctypes.c_void_p),
+                ("col", ctypes.c_void_p), ("weight", ctypes.c_void_p),
+                ("format", ctypes.c_int32), ("block_scales", ctypes.c_void_p),
+                ("global_scale", ctypes.c_void_p)]
+
+
+class _OutCsr(ctypes.Structure):
+    _fields_ = [("n_edges", ctypes.c_int64), ("rowptr", ctypes.c_void_p),
+                ("dst", ctypes.c_void_p), ("weight_index", ctypes.c_void_p),
+                ("weight", ctypes.c_void_p)]
+
+
+class EventCounters(ctypes.Structure):
+    """Head of the nsb_dendritic_event workspace (nsb_event_counters)."""
+
+    _fields_ = [("emitted_sources", ctypes.c_uint32), ("reserved", ctypes.c_uint32),
+                ("active_neurons", ctypes.c_uint64), ("active_edges", ctypes.c_uint64),
+                ("reserved2", ctypes.c_uint64)]
+
+
+EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
+                    "nsb_dendritic_event_workspace_size", "nsb_dendritic_event",
+                    "nsb_last_error", "nsb_abi_version")
+
+
+@functools.lru_cache(maxsize=1)
+def load_library() -> ctypes.CDLL:
+    """Open the in-tree library (no JIT, no fallback)."""
+    if not LIBRARY_PATH.exists():
+        raise RuntimeError(
+            f"{LIBRARY_PATH.name} is missing: build it with `python -m neurosim_gpu_b200.build` "
+            "(nvcc, sm_100a).  The native runtimes have no CPU or PyTorch fallback.")
+    lib = ctypes.CDLL(str(LIBRARY_PATH))
+    p = ctypes.POINTER
+    lib.nsb_dendritic_step.argtypes = [p(_Tick), p(_Csr), ctypes.c_int32, p(_TickOut),
+                                       ctypes.c_void_p]
+    lib.nsb_csr_propagate.argtypes = [ctypes.c_int64, ctypes.c_int64, p(_Csr), p(_View),
+                                      p(_Out), ctypes.c_void_p]
+    lib.nsb_dendritic_event_workspace_size.argtypes = [ctypes.c_int64, ctypes.c_int64]
+    lib.nsb_dendritic_event_workspace_size.restype = ctypes.c_size_t
+    lib.nsb_dendritic_event.argtypes = [p(_Tick), ctypes.c_void_p, p(_View), ctypes.c_void_p,
+                                        ctypes.c_int64, p(_OutCsr), p(_TickOut), p(_Out),
+                                        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.nsb_last_error.restype = ctypes.c_char_p
+    lib.nsb_abi_version.restype = ctypes.c_int
+    for name in EXPORTED_SYMBOLS:
+        getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
+    if lib.nsb_abi_version() != 1:
+        raise RuntimeError("libneurosim_b200.so ABI version mismatch")
+    return lib
+
+
+def _check(ok: bool, message: str) -> None:
+    if not ok:
+        raise RuntimeError(message)
+
+
+def _raise_on_status(lib: ctypes.CDLL, status: int) -> None:
+    if status != 0:
+        raise RuntimeError(lib.nsb_last_error().decode() or f"libneurosim_b200 status {status}")
+
+
+def _float_on(value: torch.Tensor, state: torch.Tensor) -> None:
+    _check(value.is_cuda and value.device == state.device,
+           "all tensors must be on the state's CUDA device")
+    _check(value.dtype == torch.float32, "all values must be float32")
+
+
+def _view(value: torch.Tensor, state: torch.Tensor) -> _View:
+    _float_on(value, state)
+    _check(value.shape == state.shape, "state/current/drive shape mismatch")
+    return _View(value.data_ptr(), value.stride(0), value.stride(1), 0.0)
+
+
+def _drive(value: torch.Tensor | None, scalar: float, state: torch.Tensor) -> _View:
+    if value is not None:
+        return _view(value, state)
+    return _View(None, 0, 0, float(scalar))
+
+
+def _params(values, state: torch.Tensor) -> _Params:
+    _check(len(values) == 6, "six neuron parameter vectors are required")
+    result = _Params()
+    for i, value in enumerate(values):
+        _float_on(value, state)
+        _check(value.dim() == 1 and value.numel() == state.size(1),
+               "parameters must have one value per neuron")
+        result.data[i] = value.data_ptr()
+        result.stride[i] = value.stride(0)
+    return result
+
+
+def _index(value: torch.Tensor, state: torch.Tensor) -> None:
+    _check(value.device == state.device and value.dtype == torch.int32
+           and value.is_contiguous() and value.dim() == 1,
+           "indices must be contiguous int32 vectors on the state device")
+
+
+def _check_state(state: torch.Tensor) -> None:
+    _check(state.is_cuda and state.dtype == torch.float32, "state must be CUDA float32")
+    _check(state.dim() == 2 and state.size(1) > 0, "state must be [B,N], N > 0")
+
+
+def _outputs(planes: int, state: torch.Tensor, neuron_major: bool = True
+             ) -> tuple[torch.Tensor, list[torch.Tensor]]:
+    """One fresh block holding `planes` [B,N] outputs.
+
+    With B > 1 and ``neuron_major`` the block is [planes, N, B] and the
+    returned [B,N] views have strides (1, B): the next matrix tick then
+    gathers all batch rows of a source neuron from one 32-byte sector.
+    """
+    batch, neurons = state.shape
+    if batch > 1 and neuron_major:
+        block = torch.empty((planes, neurons, batch), device=state.device, dtype=torch.float32)
+        return block, [block[i].t() for i in range(planes)]
+    block = torch.empty((planes, batch, neurons), device=state.device, dtype=torch.float32)
+    return block, [block[i] for i in range(planes)]
+
+
+def _out(view: torch.Tensor) -> _Out:
+    return _Out(view.data_ptr(), view.stride(0), view.stride(1))
+
+
+def _tick(state, dendrite, adaptation, params, input, input_scalar, dendritic_input,
+          dendritic_scalar) -> _Tick:
+    return _Tick(state.size(0), state.size(1), _view(state, state), _view(dendrite, state),
+                 _view(adaptation, state), _drive(input, input_scalar, state),
+                 _drive(dendritic_input, dendritic_scalar, state), _params(params, state))
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def csr_arguments(rowptr: torch.Tensor, source: torch.Tensor, weight: torch.Tensor,
+                  block_scales: torch.Tensor | None, global_scale: torch.Tensor | None,
+                  state: torch.Tensor) -> _Csr:
+    """Validate a destination-major CSR (compartmental.cu:187-209) into the C struct."""
+    _index(rowptr, state)
+    _index(source, state)
+    edges = source.numel()
+    quantized = weight.dtype == torch.uint8
+    _check(weight.device == state.device and weight.is_contiguous() and weight.dim() == 1,
+           "CSR weights must be a contiguous vector on the state device")
+    _check(rowptr.numel() == state.size(1) + 1, "invalid CSR geometry")
+    scale_ptr = scales_ptr = None
+    if quantized:
+        _check(global_scale is not None, "quantized CSR weights require a global scale")
+        _float_on(global_scale, state)
+        _check(global_scale.numel() == 1, "global scale must have one value")
+        _check(weight.numel() == ((edges + 1) // 2 if block_scales is not None else edges),
+               "invalid quantized CSR weight count")
+        if block_scales is not None:
+            _check(block_scales.device == state.device and block_scales.dtype == torch.uint8
+                   and block_scales.is_contiguous() and block_scales.dim() == 1
+                   and block_scales.numel() == (edges + 15) // 16,
+                   "invalid NVFP4 block scales")
+            scales_ptr = block_scales.data_ptr() if block_scales.numel() else None
+            fmt = NVFP4
+        else:
+            fmt = E4M3
+        scale_ptr = global_scale.data_ptr()
+    else:
+        _check(block_scales is None and global_scale is None and weight.numel() == edges
+               and weight.dtype in (torch.float32, torch.float16),
+               "invalid floating-point CSR weights")
+        fmt = F32 if weight.dtype == torch.float32 else F16
+    return _Csr(edges, rowptr.data_ptr(), source.data_ptr() if edges else None,
+                weight.data_ptr() if edges else None, fmt, scales_ptr, scale_ptr)
+
+
+class DendriticExtension:
+    """The hot-path subset of the reference's ``neurosim_gpu_native`` module."""
+
+    def __init__(self) -> None:
+        self.lib = load_library()
+
+    # -- matrix tick ---------------------------------------------------------
+    def prepare_step(self, state, dendrite, adaptation, params, rowptr, source, weight,
+                     input, input_scalar, dendritic_input, dendritic_scalar, width,
+                     block_scales=None, global_scale=None, *, out):
+        """Validate once and return a callable that enqueues the tick into ``out``.
+
+        ``out`` is a triple of writable [B,N] float32 tensors (s', d', a').  The
+        callable launches on the stream that is current when it is called, so
+        it can be captured into a CUDA graph.
+        """
+        _check_state(state)
+        tick = _tick(state, dendrite, adaptation, params, input, input_scalar,
+                     dendritic_input, dendritic_scalar)
+        csr = csr_arguments(rowptr, source, weight, block_scales, global_scale, state)
+        _check(width in (4, 8, 16, 32), "width must be 4, 8, 16 or 32")
+        _check(len(out) == 3, "three output tensors are required")
+        for view in out:
+            _float_on(view, state)
+            _check(view.shape == state.shape, "output shape mismatch")
+        result = _TickOut(_out(out[0]), _out(out[1]), _out(out[2]))
+        lib, device, lanes = self.lib, state.device, int(width)
+        keep = (state, dendrite, adaptation, params, rowptr, source, weight, input,
+                dendritic_input, block_scales, global_scale, out)
+
+        def launch() -> None:
+            assert keep is not None
+            with torch.cuda.device(device):
+                status = lib.nsb_dendritic_step(ctypes.byref(tick), ctypes.byref(csr), lanes,
+                                                ctypes.byref(result), _stream(device))
+            _raise_on_status(lib, status)
+
+        return launch
+
+    def dendritic_step(self, state, dendrite, adaptation, params, rowptr, source, weight,
+                       input, input_scalar, dendritic_input, dendritic_scalar, width,
+                       block_scales=None, global_scale=None):
+        _check_state(state)
+        _, views = _outputs(3, state)
+        self.prepare_step(state, dendrite, adaptation, params, rowptr, source, weight, input,
+                          input_scalar, dendritic_input, dendritic_scalar, width, block_scales,
+                          global_scale, out=views)()
+        return views
+
+    # -- bare product --------------------------------------------------------
+    def csr_propagate(self, rowptr, source, weight, x, block_scales=None, global_scale=None):
+        """j = W @ x for x [B,N] in any weight format; a fresh contiguous [B,N] tensor."""
+        _check_state(x)
+        csr = csr_arguments(rowptr, source, weight, block_scales, global_scale, x)
+        result = torch.empty(x.shape, device=x.device, dtype=torch.float32)
+        src = _View(x.data_ptr(), x.stride(0), x.stride(1), 0.0)
+        out = _Out(result.data_ptr(), result.stride(0), result.stride(1))
+        with torch.cuda.device(x.device):
+            status = self.lib.nsb_csr_propagate(x.size(0), x.size(1), ctypes.byref(csr),
+                                                ctypes.byref(src), ctypes.byref(out),
+                                                _stream(x.device))
+        _raise_on_status(self.lib, status)
+        return result
+
+    # -- PELS tick -----------------------------------------------------------
+    def event_workspace(self, state: torch.Tensor) -> torch.Tensor:
+        size = int(self.lib.nsb_dendritic_event_workspace_size(state.size(0), state.size(1)))
+        return torch.empty(size, dtype=torch.uint8, device=state.device)
+
+    def dendritic_event(self, state, dendrite, adaptation, params, current, emitted, theta,
+                        out_rowptr, dst, out_weight_index, weight, input, input_scalar,
+                        dendritic_input, dendritic_scalar, *, workspace=None):
+        _check_state(state)
+        tick = _tick(state, dendrite, adaptation, params, input, input_scalar,
+                     dendritic_input, dendritic_scalar)
+        emitted_view = _view(emitted, state)
+        _view(current, state)
+        _check(current.is_contiguous(), "persistent current must be contiguous")
+        _index(out_rowptr, state)
+        _index(dst, state)
+        if out_weight_index is not None:
+            _index(out_weight_index, state)
+        _float_on(weight, state)
+        _float_on(theta, state)
+        _check(out_rowptr.numel() == state.size(1) + 1 and dst.numel() == weight.numel()
+               and (out_weight_index is None or dst.numel() == out_weight_index.numel())
+               and weight.is_contiguous() and weight.dim() == 1,
+               "invalid event topology geometry")
+        _check(theta.dim() == 1 and theta.numel() == state.size(1), "theta must have N values")
+        edges = dst.numel()
+        out_csr = _OutCsr(edges, out_rowptr.data_ptr(), dst.data_ptr() if edges else None,
+                          out_weight_index.data_ptr() if (out_weight_index is not None and edges)
+                          else None, weight.data_ptr() if edges else None)
+        # The PELS tick gathers nothing, so its outputs stay batch-major like the current.
+        block, views = _outputs(4, state, neuron_major=False)
+        out = _TickOut(_out(views[0]), _out(views[1]), _out(views[2]))
+        out_emitted = _out(views[3])
+        if workspace is None:
+            workspace = self.event_workspace(state)
+        with torch.cuda.device(state.device):
+            status = self.lib.nsb_dendritic_event(
+                ctypes.byref(tick), current.data_ptr(), ctypes.byref(emitted_view),
+                theta.data_ptr(), theta.stride(0), ctypes.byref(out_csr), ctypes.byref(out),
+                ctypes.byref(out_emitted), workspace.data_ptr(), workspace.numel(),
+                _stream(state.device))
+        _raise_on_status(self.lib, status)
+        return views
+
+
+@functools.lru_cache(maxsize=1)
+def load_native_extension(verbose: bool = False) -> DendriticExtension:
+    """The drop-in for the reference's loader (native.py:59-69); no JIT build."""
+    return DendriticExtension()

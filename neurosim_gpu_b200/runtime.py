@@ -1,0 +1,432 @@
+"""Drop-in native runtimes: ``NativeDendriticMatrixRuntime`` / ``NativeDendriticPELSRuntime``.
+
+Same constructor arguments, ``step`` signature, attributes and error types as
+the reference classes (src/neurosim_gpu/native_compartmental.py:46-177):
+
+* states ``state``, ``dendritic_state``, ``adaptation_state`` (+ ``emitted_state``,
+  ``persistent_current``, ``theta``, ``_tick`` for PELS) are plain tensors, so
+  the checkpoint layout is unchanged;
+* ``step`` returns the new state; returned tensors stay valid after later
+  ticks (every tick writes a fresh allocation);
+* ``last_backend`` is ``"unstepped"``, ``"native"``, ``"native-{fp16,fp8,nvfp4}-weight"``,
+  ``"native-stats"`` (PELS statistics, counted in the kernel) or
+  ``"reference-autograd"`` (a request that needs gradients);
+* ``checkpoint_precision``, ``precision_execution``, ``weight_storage_bytes``
+  and ``threads_per_row`` keep their meaning.
+
+Every inference tick runs in ``libneurosim_b200.so``.  The only non-CUDA-kernel
+path is the differentiable PyTorch tick used when autograd is requested, which
+the kernels do not implement (as in the reference, native_compartmental.py:104-108).
+
+``NativeDendriticMatrixRuntime.run(ticks, ...)`` advances many ticks by
+replaying a captured CUDA graph of the native tick.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import native as _native
+from .dynamics import DendriticDynamics
+from .precision import encode_sparse_weights, validate_precision, weight_storage_bytes
+from .topology import SparseTopology
+
+
+@dataclass(frozen=True)
+class RuntimeStats:
+    """Per-tick emission statistics (runtime.py:40-43 of the reference)."""
+
+    path: str
+    active_neurons: int
+    active_edges: int
+
+
+def validate_emission_threshold(theta: torch.Tensor, topology: SparseTopology) -> torch.Tensor:
+    """runtime.py:15-34: scalar or [N], non-negative; +inf only without out-edges."""
+    if theta.ndim == 0:
+        theta = theta.expand(topology.n_neurons)
+    if theta.shape != (topology.n_neurons,):
+        raise ValueError("theta must be scalar or have one value per neuron")
+    if bool(torch.any(theta < 0)) or bool(torch.any(torch.isnan(theta))):
+        raise ValueError("theta must be non-negative and finite, except +inf for "
+                         "zero-outdegree neurons")
+    invalid_infinity = torch.isposinf(theta) & (topology.out_degree > 0)
+    if bool(torch.any(torch.isneginf(theta))) or bool(torch.any(invalid_infinity)):
+        raise ValueError("infinite theta is allowed only for zero-outdegree neurons")
+    return theta
+
+
+class _NativeCompartments:
+    """State ownership and argument handling shared by both runtimes."""
+
+    topology: SparseTopology
+    compartment_dynamics: DendriticDynamics
+    state: torch.Tensor
+    dendritic_state: torch.Tensor
+    adaptation_state: torch.Tensor
+
+    def _init_compartments(self, topology: SparseTopology, dynamics: DendriticDynamics,
+                           initial_state: torch.Tensor, extension) -> None:
+        if initial_state.device.type != "cuda" or initial_state.dtype != torch.float32:
+            raise ValueError("native compartment runtime requires CUDA float32")
+        if initial_state.ndim != 2 or initial_state.shape[1] != topology.n_neurons:
+            raise ValueError("initial_state must have shape [batch, n_neurons]")
+        if dynamics.soma.n_neurons != topology.n_neurons:
+            raise ValueError("dynamics and topology neuron counts must match")
+        for value in (dynamics.soma.alpha, topology.weight):
+            if value.device != initial_state.device or value.dtype != initial_state.dtype:
+                raise ValueError("state, topology and dynamics must match device and dtype")
+        if not bool((torch.isfinite(initial_state) & (initial_state >= 0)
+                     & (initial_state <= 1)).all()):
+            raise ValueError("initial_state must be finite and in [0, 1]")
+        self.topology = topology
+        self.compartment_dynamics = dynamics
+        self.dynamics = dynamics.soma
+        self.state = initial_state
+        self.dendritic_state = torch.zeros_like(initial_state)
+        self.adaptation_state = torch.zeros_like(initial_state)
+        self.extension = extension if extension is not None else _native.load_native_extension()
+        self.last_backend = "unstepped"
+
+    @property
+    def device(self) -> torch.device:
+        return self.state.device
+
+    def _parameters(self) -> list[torch.Tensor]:
+        return self.compartment_dynamics.parameters()
+
+    def _needs_autograd(self, drive, dendritic_drive) -> bool:
+        if not torch.is_grad_enabled():
+            return False
+        values = [self.state, self.dendritic_state, self.adaptation_state, self.topology.weight,
+                  self.topology.in_weight, *self._parameters(), drive, dendritic_drive]
+        if hasattr(self, "persistent_current"):
+            values += [self.persistent_current, self.emitted_state]
+        return any(isinstance(v, torch.Tensor) and v.requires_grad for v in values)
+
+    def _drive(self, value, name: str = "drive") -> tuple[torch.Tensor | None, float]:
+        if not isinstance(value, torch.Tensor):
+            return None, float(value)
+        if value.device != self.state.device or value.dtype != self.state.dtype:
+            raise ValueError(f"{name} must match state device and dtype")
+        try:
+            return value.expand_as(self.state), 0.0
+        except RuntimeError as error:
+            raise ValueError(f"{name} must broadcast to [batch, n_neurons]") from error
+
+    # Differentiable PyTorch tick, used only when autograd is requested.
+    def _autograd_propagate(self, source: torch.Tensor) -> torch.Tensor:
+        return torch.sparse.mm(self.topology.sparse_matrix(), source.T).T
+
+    def _autograd_advance(self, current, drive, dendritic_drive) -> torch.Tensor:
+        for name, value in (("drive", drive), ("dendritic_drive", dendritic_drive)):
+            if isinstance(value, torch.Tensor):
+                try:
+                    shape = torch.broadcast_shapes(value.shape, self.state.shape)
+                except RuntimeError as error:
+                    raise ValueError(f"{name} must broadcast to [batch, n_neurons]") from error
+                if shape != self.state.shape:
+                    raise ValueError(f"{name} must broadcast to [batch, n_neurons]")
+        state, dendrite, adaptation = self.compartment_dynamics.advance(
+            self.state, self.dendritic_state, self.adaptation_state, current, drive,
+            dendritic_drive=dendritic_drive)
+        self.dendritic_state = dendrite
+        self.adaptation_state = adaptation
+        return state
+
+
+class NativeDendriticMatrixRuntime(_NativeCompartments):
+    """One CUDA launch per tick: CSR propagation fused with all three neuron states.
+
+    States, parameters, drives and accumulation are CUDA float32.  Optional
+    fp16 / fp8 / nvfp4 CSR weight storage is decoded in-register before the
+    fp32 multiply; reduced storage is inference-only.  ``threads_per_row``
+    picks 8/16/32 lanes per row (None: chosen from the mean degree).
+    """
+
+    def __init__(self, topology: SparseTopology, dynamics: DendriticDynamics,
+                 initial_state: torch.Tensor, *, threads_per_row: int | None = None,
+                 extension=None, weight_dtype: torch.dtype = torch.float32,
+                 weight_format: str | None = None, precision: str | None = None) -> None:
+        if precision is not None:
+            validate_precision(precision)
+            if weight_format is not None or weight_dtype != torch.float32:
+                raise ValueError("precision and weight_dtype/weight_format conflict")
+            weight_dtype = torch.float16 if precision == "fp16" else torch.float32
+            weight_format = precision if precision in ("fp8", "nvfp4") else None
+        if threads_per_row not in (None, 8, 16, 32):
+            raise ValueError("threads_per_row must be 8, 16, 32 or None")
+        if initial_state.device.type != "cuda" or initial_state.dtype != torch.float32:
+            raise ValueError("native compartment runtime requires CUDA float32")
+        if weight_dtype not in (torch.float32, torch.float16):
+            raise ValueError("weight_dtype must be torch.float32 or torch.float16")
+        if weight_format not in (None, "fp8", "nvfp4"):
+            raise ValueError("weight_format must be None, 'fp8' or 'nvfp4'")
+        if weight_format is not None and weight_dtype != torch.float32:
+            raise ValueError("weight_format and non-default weight_dtype conflict")
+        self._init_compartments(topology, dynamics, initial_state, extension)
+        degree = topology.n_edges / max(topology.n_neurons, 1)
+        # Lanes per row; each lane reads 4-edge chunks, so 32 lanes cover 128 edges.
+        self.threads_per_row = threads_per_row or (8 if degree <= 16 else 16 if degree <= 48
+                                                   else 32)
+        self.weight_dtype = weight_dtype
+        self.weight_format = weight_format
+        self.precision = "fp32"
+        self._graphs: dict = {}
+        self._invalidate_precision_cache()
+
+    def _invalidate_precision_cache(self) -> None:
+        self._packed_weight = None
+        self._packed_weight_version = -1
+        self._graphs = {}
+
+    @property
+    def checkpoint_precision(self) -> str:
+        if self.weight_format is not None:
+            return self.weight_format
+        return "fp16" if self.weight_dtype == torch.float16 else "fp32"
+
+    @property
+    def precision_execution(self) -> str:
+        return f"cuda-fused-{self.checkpoint_precision}-weights-fp32-fma"
+
+    @property
+    def weight_storage_bytes(self) -> int:
+        """Logical inference payload in bytes, excluding the original topology."""
+        return weight_storage_bytes(self.topology.n_edges, self.checkpoint_precision)
+
+    def _weights(self):
+        """(weight, block_scales, global_scale, backend) for the current weight_version."""
+        weight = self.topology.in_weight
+        if self.weight_format is None and self.weight_dtype == torch.float32:
+            return weight, None, None, "native"
+        if self._packed_weight_version != self.topology.weight_version:
+            if self.weight_format is None:
+                self._packed_weight = (weight.detach().to(torch.float16),)
+            else:
+                self._packed_weight = encode_sparse_weights(weight.detach(), self.weight_format)
+            self._packed_weight_version = self.topology.weight_version
+        packed = self._packed_weight
+        scales = packed[1] if len(packed) > 1 else None
+        scale = packed[2] if len(packed) > 2 else None
+        return packed[0], scales, scale, f"native-{self.weight_format or 'fp16'}-weight"
+
+    def _propagate(self, source: torch.Tensor) -> torch.Tensor:
+        """W @ source (fp32 weights) in one native launch."""
+        topology = self.topology
+        return self.extension.csr_propagate(topology.in_rowptr, topology.in_col,
+                                            topology.in_weight.detach(), source)
+
+    def step(self, drive: torch.Tensor | float = 0.0, *,
+             dendritic_drive: torch.Tensor | float = 0.0) -> torch.Tensor:
+        if self._needs_autograd(drive, dendritic_drive):
+            if self.weight_format is not None or self.weight_dtype == torch.float16:
+                raise RuntimeError("native reduced-precision weight storage is inference-only")
+            self.last_backend = "reference-autograd"
+            self.state = self._autograd_advance(self._autograd_propagate(self.state), drive,
+                                                dendritic_drive)
+            return self.state
+        u, us = self._drive(drive)
+        v, vs = self._drive(dendritic_drive, "dendritic_drive")
+        weight, scales, scale, backend = self._weights()
+        topology = self.topology
+        self.state, self.dendritic_state, self.adaptation_state = self.extension.dendritic_step(
+            self.state, self.dendritic_state, self.adaptation_state, self._parameters(),
+            topology.in_rowptr, topology.in_col, weight, u, us, v, vs, self.threads_per_row,
+            scales, scale)
+        self.last_backend = backend
+        return self.state
+
+    # -- multi-tick rollout through a CUDA graph -----------------------------
+    def run(self, ticks: int, drive: torch.Tensor | float = 0.0, *,
+            dendritic_drive: torch.Tensor | float = 0.0, graph_ticks: int = 64) -> torch.Tensor:
+        """Advance ``ticks`` ticks with fixed drives; returns the final state.
+
+        The native tick is captured once into a CUDA graph of ``graph_ticks``
+        ticks over two resident state buffers and replayed, so the host issues
+        one launch per ``graph_ticks`` ticks.  Tensor drives are read at replay
+        time (their values may change between calls, their storage may not).
+        Results equal ``ticks`` calls of :meth:`step`.
+        """
+        if ticks < 0:
+            raise ValueError("ticks must be non-negative")
+        if self._needs_autograd(drive, dendritic_drive):
+            raise RuntimeError("run() is inference-only; use step() for autograd")
+        if ticks == 0:
+            return self.state
+        u, us = self._drive(drive)
+        v, vs = self._drive(dendritic_drive, "dendritic_drive")
+        weight, scales, scale, backend = self._weights()
+        graph_ticks = max(1, min(graph_ticks, ticks))
+        key = (graph_ticks, tuple(self.state.shape),
+               None if u is None else (u.data_ptr(), u.stride()), us,
+               None if v is None else (v.data_ptr(), v.stride()), vs,
+               weight.data_ptr(), self.topology.weight_version,
+               tuple(p.data_ptr() for p in self._parameters()))
+        entry = self._graphs.get(key)
+        if entry is None:
+            self._graphs = {}
+            entry = self._graphs[key] = _TickGraph(self, graph_ticks, u, us, v, vs, weight,
+                                                   scales, scale)
+        entry.load(self.state, self.dendritic_state, self.adaptation_state)
+        for _ in range(ticks // graph_ticks):
+            entry.replay()
+        states = entry.result()
+        rest = ticks % graph_ticks
+        self.state, self.dendritic_state, self.adaptation_state = states
+        for _ in range(rest):
+            self.step(drive, dendritic_drive=dendritic_drive)
+        self.last_backend = backend
+        return self.state
+
+
+class _TickGraph:
+    """A CUDA graph of ``ticks`` native ticks ping-ponging between two buffers."""
+
+    def __init__(self, runtime: NativeDendriticMatrixRuntime, ticks: int, u, us, v, vs,
+                 weight, scales, scale) -> None:
+        ext = runtime.extension
+        state = runtime.state
+        self.ticks = ticks
+        self.buffers = [_native._outputs(3, state)[1] for _ in range(2)]
+        topology = runtime.topology
+        params = runtime._parameters()
+        self.graph = torch.cuda.CUDAGraph()
+        stream = torch.cuda.Stream(device=state.device)
+        stream.wait_stream(torch.cuda.current_stream(state.device))
+        calls = []
+        for k in range(ticks):
+            src, dst = self.buffers[k % 2], self.buffers[(k + 1) % 2]
+            calls.append(ext.prepare_step(src[0], src[1], src[2], params, topology.in_rowptr,
+                                          topology.in_col, weight, u, us, v, vs,
+                                          runtime.threads_per_row, scales, scale, out=dst))
+        with torch.cuda.stream(stream):
+            calls[0]()  # warm-up outside capture (kernel attributes, occupancy queries)
+        torch.cuda.current_stream(state.device).wait_stream(stream)
+        with torch.cuda.graph(self.graph, stream=stream):
+            for call in calls:
+                call()
+        self.final = self.buffers[ticks % 2]
+
+    def load(self, s, d, a) -> None:
+        for buffer, value in zip(self.buffers[0], (s, d, a)):
+            buffer.copy_(value)
+
+    def replay(self) -> None:
+        self.graph.replay()
+        for target, source in zip(self.buffers[0], self.final):
+            if target.data_ptr() != source.data_ptr():
+                target.copy_(source)
+
+    def result(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        return tuple(b.clone() for b in self.buffers[0])
+
+
+class NativeDendriticPELSRuntime(_NativeCompartments):
+    """Two CUDA launches per tick: advance + emission, then the active-edge scatter.
+
+    The advance kernel queues every emitting (b, n) with its delta on the
+    device; the scatter visits only those sources' out-edges and adds
+    delta * w into the persistent current with float atomics (non-deterministic
+    summation order).  ``collect_stats=True`` returns counts the kernel
+    accumulated; autograd requests use the differentiable PyTorch tick.
+    """
+
+    def __init__(self, topology: SparseTopology, dynamics: DendriticDynamics,
+                 initial_state: torch.Tensor, *, theta: float | torch.Tensor,
+                 extension=None, precision: str | None = None) -> None:
+        if precision not in (None, "fp32"):
+            raise ValueError("native PELS supports FP32 only")
+        if initial_state.device.type != "cuda" or initial_state.dtype != torch.float32:
+            raise ValueError("native compartment runtime requires CUDA float32")
+        self._init_compartments(topology, dynamics, initial_state, extension)
+        theta = torch.as_tensor(theta, dtype=initial_state.dtype, device=initial_state.device)
+        self.theta = validate_emission_threshold(theta, topology)
+        self.precision = "fp32"
+        self.propagation = "event"
+        self.emitted_state = initial_state.clone()
+        self.persistent_current = self._propagate(self.emitted_state)
+        self._tick = 0
+        self._weight_version = topology.weight_version
+        self._workspace = None
+
+    def _invalidate_precision_cache(self) -> None:
+        pass
+
+    @property
+    def checkpoint_precision(self) -> str:
+        return "fp32"
+
+    @property
+    def precision_execution(self) -> str:
+        return "cuda-fused-pels-fp32"
+
+    def _propagate(self, source: torch.Tensor) -> torch.Tensor:
+        topology = self.topology
+        if torch.is_grad_enabled() and (source.requires_grad or topology.in_weight.requires_grad):
+            return self._autograd_propagate(source)
+        return self.extension.csr_propagate(topology.in_rowptr, topology.in_col,
+                                            topology.in_weight.detach(), source)
+
+    def _refresh_current(self) -> None:
+        """Recompute W @ emitted after a versioned weight change (runtime.py:217-223)."""
+        if self._weight_version != self.topology.weight_version:
+            self.persistent_current = self._propagate(self.emitted_state).contiguous()
+            self._weight_version = self.topology.weight_version
+
+    def _workspace_for(self, state: torch.Tensor) -> torch.Tensor:
+        need = int(self.extension.lib.nsb_dendritic_event_workspace_size(*state.shape))
+        if self._workspace is None or self._workspace.numel() < need \
+                or self._workspace.device != state.device:
+            self._workspace = torch.empty(need, dtype=torch.uint8, device=state.device)
+        return self._workspace
+
+    def step(self, drive: torch.Tensor | float = 0.0, *,
+             dendritic_drive: torch.Tensor | float = 0.0, collect_stats: bool = False):
+        if self._needs_autograd(drive, dendritic_drive):
+            self.last_backend = "reference-autograd"
+            return self._autograd_step(drive, dendritic_drive, collect_stats)
+        u, us = self._drive(drive)
+        v, vs = self._drive(dendritic_drive, "dendritic_drive")
+        self._refresh_current()
+        if not self.persistent_current.is_contiguous():
+            self.persistent_current = self.persistent_current.contiguous()
+        workspace = self._workspace_for(self.state)
+        topology = self.topology
+        # The advance reads the current before the scatter updates it (stream order).
+        self.state, self.dendritic_state, self.adaptation_state, self.emitted_state = (
+            self.extension.dendritic_event(
+                self.state, self.dendritic_state, self.adaptation_state, self._parameters(),
+                self.persistent_current, self.emitted_state, self.theta, topology.out_rowptr,
+                topology.dst, None, topology.weight.detach(), u, us, v, vs,
+                workspace=workspace))
+        self._tick += 1
+        if not collect_stats:
+            self.last_backend = "native"
+            return self.state
+        self.last_backend = "native-stats"
+        counters = _native.EventCounters.from_buffer_copy(
+            workspace[: ctypes.sizeof(_native.EventCounters)].cpu().numpy().tobytes())
+        active, edges = int(counters.active_neurons), int(counters.active_edges)
+        return self.state, RuntimeStats("event" if active else "idle", active, edges)
+
+    def _autograd_step(self, drive, dendritic_drive, collect_stats: bool):
+        """Differentiable PELS tick (runtime.py:264-314 with the emit rule above)."""
+        self._refresh_current()
+        state = self._autograd_advance(self.persistent_current, drive, dendritic_drive)
+        residual = state - self.emitted_state
+        active = residual.detach().abs() >= self.theta
+        delta = torch.where(active, residual, torch.zeros_like(residual))
+        self.persistent_current = self.persistent_current + self._autograd_propagate(delta)
+        self.emitted_state = self.emitted_state + delta
+        self.state = state
+        self._tick += 1
+        if not collect_stats:
+            return self.state
+        pairs = torch.nonzero(active, as_tuple=False)
+        edges = int(self.topology.out_degree[pairs[:, 1]].sum()) if pairs.numel() else 0
+        count = int(active.sum())
+        return self.state, RuntimeStats("event" if count else "idle", count, edges)

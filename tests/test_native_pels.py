@@ -1,0 +1,199 @@
+"""Native PELS tick vs the CPU oracle (reference tests/test_native_compartmental.py:99-178)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from _util import GOLDEN, OracleMatrix, assert_same_as, bench_model, csr_of, drive_np, make, npy, params_of
+from neurosim_gpu_b200 import (NativeDendriticPELSRuntime, load_native_extension,
+                               random_topology)
+
+pytestmark = pytest.mark.gpu
+
+EPSILON = 1e-6  # emit decisions may differ only this close to the threshold
+
+
+@pytest.fixture(scope="module")
+def ext():
+    return load_native_extension()
+
+
+# test_native_compartmental.py:99-110
+def test_theta_zero_long_rollout_matches_matrix(ext):
+    graph, model, state = make(1024, 2, 16000)
+    native = NativeDendriticPELSRuntime(graph, model, state.clone(), theta=0, extension=ext)
+    reference = OracleMatrix(graph, model, state)
+    with torch.inference_mode():
+        for t in range(500):
+            value = 0.2 if t % 70 < 35 else 0.05
+            native.step(value, dendritic_drive=0.1)
+            reference.step(value, 0.1)
+    assert_same_as(native, reference, atol=8e-6)
+    torch.testing.assert_close(native.persistent_current,
+                               native._propagate(native.emitted_state), rtol=2e-4, atol=1e-5)
+
+
+def _snapshot(rt):
+    return {name: npy(getattr(rt, name)).copy() for name in
+            ("state", "dendritic_state", "adaptation_state", "emitted_state",
+             "persistent_current")}
+
+
+def _teacher_forced_tick(ext, native, theta, drive, dendritic_drive, csr, params):
+    """Step native once and check it against one oracle tick from the same pre-state."""
+    pre = _snapshot(native)
+    shape = pre["state"].shape
+    with torch.inference_mode():
+        native.step(drive, dendritic_drive=dendritic_drive)
+    s, d, a, e, cur, active = oracle.event_tick(
+        csr, pre["state"], pre["dendritic_state"], pre["adaptation_state"], params,
+        pre["persistent_current"], pre["emitted_state"], np.full(shape[1], theta, np.float32),
+        drive_np(drive, shape), drive_np(dendritic_drive, shape))
+    ns, ne = npy(native.state), npy(native.emitted_state)
+    np.testing.assert_allclose(ns, s, atol=1e-6, rtol=0)
+    np.testing.assert_allclose(npy(native.dendritic_state), d, atol=1e-6, rtol=0)
+    np.testing.assert_allclose(npy(native.adaptation_state), a, atol=1e-6, rtol=0)
+    native_active = (ne == ns) & (ns != pre["emitted_state"])
+    residual = np.abs(s - pre["emitted_state"])
+    differ = native_active != active
+    assert np.all(np.abs(residual[differ] - theta) <= EPSILON), "emit mask disagrees"
+    if not differ.any():
+        np.testing.assert_allclose(ne, e, atol=1e-6, rtol=0)
+        np.testing.assert_allclose(npy(native.persistent_current), cur, atol=2e-6, rtol=0)
+    return int(active.sum()), int(differ.sum())
+
+
+# test_native_compartmental.py:142-164, teacher-forced tick by tick
+def test_nonzero_threshold_emit_mask_agrees_tick_by_tick(ext):
+    graph, model, state = make()
+    native = NativeDendriticPELSRuntime(graph, model, state.clone(), theta=0.02, extension=ext)
+    params = params_of(model)
+    flips = 0
+    for t in range(50):
+        if t == 25:
+            graph.apply_source_weights_(graph.weight * 0.7)
+            native._refresh_current()
+        _, differ = _teacher_forced_tick(ext, native, 0.02, 0.3, 0.1, csr_of(graph), params)
+        flips += differ
+        assert float((native.state - native.emitted_state).abs().max()) < 0.020001
+        torch.testing.assert_close(native.persistent_current,
+                                   native._propagate(native.emitted_state), rtol=2e-4, atol=2e-6)
+    assert flips <= 2
+
+
+def test_nonzero_threshold_free_run_against_reference_golden(ext):
+    """The reference's own DendriticPELSRuntime(theta=0.02) trajectory (small_pels.npz)."""
+    golden = np.load(GOLDEN / "small_pels.npz")
+    graph, model, state = make()
+    native = NativeDendriticPELSRuntime(graph, model, state.clone(), theta=0.02, extension=ext)
+    with torch.inference_mode():
+        for t in range(50):
+            if t == 25:
+                graph.apply_source_weights_(graph.weight * 0.7)
+            native.step(0.3, dendritic_drive=0.1)
+    for name in ("state", "dendritic_state", "adaptation_state", "emitted_state"):
+        np.testing.assert_allclose(npy(getattr(native, name)), golden[name][50], atol=2e-6,
+                                   rtol=2e-4, err_msg=name)
+
+
+def test_statistics_are_counted_natively(ext):
+    graph, model, state = make()
+    native = NativeDendriticPELSRuntime(graph, model, state.clone(), theta=0.02, extension=ext)
+    degree = npy(graph.out_degree)
+    for _ in range(6):
+        before = npy(native.emitted_state).copy()
+        with torch.inference_mode():
+            _, stats = native.step(0.3, collect_stats=True)
+        after = npy(native.emitted_state)
+        active = after != before
+        assert native.last_backend == "native-stats"
+        assert stats.active_neurons == int(active.sum())
+        assert stats.active_edges == int((active * degree[None, :]).sum())
+        assert stats.path == ("event" if stats.active_neurons else "idle")
+
+
+# test_native_compartmental.py:166-178
+def test_idle_updates_traces_and_retains_returned_state(ext):
+    graph, model, state = make()
+    native = NativeDendriticPELSRuntime(graph, model, state.clone(), theta=2, extension=ext)
+    with torch.inference_mode():
+        previous = native.step(0.5)
+        saved = previous.clone()
+        current = native.persistent_current.clone()
+        first_adaptation = native.adaptation_state.clone()
+        for _ in range(10):
+            native.step(0.5)
+    assert torch.equal(previous, saved)
+    assert torch.equal(native.persistent_current, current)
+    assert not torch.equal(first_adaptation, native.adaptation_state)
+    _, stats = native.step(0.5, collect_stats=True)
+    assert stats.path == "idle" and stats.active_edges == 0
+
+
+def test_reference_call_form_with_weight_index(ext):
+    """dendritic_event with (out_weight_index, in_weight), as the reference runtime calls it."""
+    graph, model, state = make(300, 4, 6000)
+    a = NativeDendriticPELSRuntime(graph, model, state.clone(), theta=0.0, extension=ext)
+    b = NativeDendriticPELSRuntime(graph, model, state.clone(), theta=0.0, extension=ext)
+    with torch.inference_mode():
+        for _ in range(10):
+            a.step(0.25, dendritic_drive=0.05)
+            s, d, ad, e = ext.dendritic_event(
+                b.state, b.dendritic_state, b.adaptation_state, b._parameters(),
+                b.persistent_current, b.emitted_state, b.theta, graph.out_rowptr, graph.dst,
+                graph.out_weight_index, graph.in_weight, None, 0.25, None, 0.05)
+            b.state, b.dendritic_state, b.adaptation_state, b.emitted_state = s, d, ad, e
+    assert_same_as(a, b, atol=1e-6)
+    torch.testing.assert_close(a.persistent_current, b.persistent_current, atol=1e-6, rtol=0)
+
+
+def test_theta_validation():
+    graph, model, state = make()
+    with pytest.raises(ValueError):
+        NativeDendriticPELSRuntime(graph, model, state.clone(), theta=-1.0)
+    with pytest.raises(ValueError, match="infinite"):
+        NativeDendriticPELSRuntime(graph, model, state.clone(), theta=float("inf"))
+    with pytest.raises(ValueError, match="FP32"):
+        NativeDendriticPELSRuntime(graph, model, state.clone(), theta=0.0, precision="fp8")
+
+
+@pytest.mark.parametrize("batch", [1, 8])
+def test_config2_theta_zero_1000_ticks_matches_reference_matrix(ext, batch):
+    """N=50k, M=1M: PELS at theta=0 against the reference matrix trajectory."""
+    golden = np.load(GOLDEN / "trajectories.npz")
+    n = 50000
+    graph = random_topology(n, 1000000, device="cpu", seed=0).to("cuda")
+    drive = torch.from_numpy(golden[f"n50000_b{batch}_drive"]).cuda()
+    native = NativeDendriticPELSRuntime(graph, bench_model(n),
+                                        torch.zeros(batch, n, device="cuda"), theta=0.0,
+                                        extension=ext)
+    with torch.inference_mode():
+        for _ in range(1000):
+            native.step(drive, dendritic_drive=0.1)
+    sample = golden["n50000_sample_index"]
+    for name in ("state", "dendritic_state", "adaptation_state"):
+        got = npy(getattr(native, name))[:, sample]
+        np.testing.assert_allclose(got, golden[f"n50000_b{batch}_t1000_{name}_sample"],
+                                   atol=1e-5, rtol=0, err_msg=name)
+
+
+def test_config2_theta_002_teacher_forced(ext):
+    n, batch = 50000, 8
+    graph = random_topology(n, 1000000, device="cpu", seed=0).to("cuda")
+    model = bench_model(n)
+    drive = torch.rand((batch, 1), generator=torch.Generator().manual_seed(0)).cuda() * 0.4
+    native = NativeDendriticPELSRuntime(graph, model, torch.zeros(batch, n, device="cuda"),
+                                        theta=0.02, extension=ext)
+    csr, params = csr_of(graph), params_of(model)
+    with torch.inference_mode():
+        for _ in range(30):
+            native.step(drive, dendritic_drive=0.1)
+    total_flips = 0
+    for _ in range(5):
+        active, flips = _teacher_forced_tick(ext, native, 0.02, drive, 0.1, csr, params)
+        assert active > 0
+        total_flips += flips
+    assert total_flips <= 10
