@@ -289,6 +289,28 @@ def run_native(args, workload: str) -> dict:
     return result
 
 
+def run_profile(args, workload: str) -> None:
+    """Eager ticks only (no graph, no copies, no CPU leg): the command ncu captures.
+
+    ``--warmup`` ticks run first, then ``--steps`` ticks; each tick is exactly one
+    launch of the tick kernel, so ``ncu -s <warmup> -c <n>`` selects ticks.
+    """
+    neurons, edges, batch, precision = WORKLOADS[workload]
+    device = torch.device("cuda", 0)
+    graph = build_graph(neurons, edges, device)
+    runtime = NativeDendriticMatrixRuntime(graph, bench_model(neurons, device),
+                                           torch.zeros(batch, neurons, device=device),
+                                           precision=precision)
+    with torch.inference_mode():
+        runtime._weights()  # pack reduced-precision weights before the counted launches
+        torch.cuda.synchronize()
+        for _ in range(args.warmup + args.steps):
+            runtime.step(0.2, dendritic_drive=0.1)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": workload, "ticks": args.warmup + args.steps,
+                      "state_mean": float(runtime.state.mean())}))
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -298,7 +320,12 @@ def main() -> None:
     parser.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--skip-cpu-baseline", action="store_true")
+    parser.add_argument("--profile", action="store_true",
+                        help="eager ticks only, for ncu captures (prints no bench line)")
     args = parser.parse_args()
+    if args.profile:
+        run_profile(args, args.workload)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":

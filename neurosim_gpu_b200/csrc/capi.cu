@@ -115,8 +115,8 @@ int nsb_dendritic_step(const nsb_tick* tick, const nsb_csr* csr, int32_t width,
   nsb::Csr c;
   if (!check_tick(tick, &t) || !check_csr(csr, &c) || !check_width(width)) return NSB_ERR_ARGUMENT;
   if (!out) return fail(NSB_ERR_ARGUMENT, "outputs are required");
-  if (!check_out(out->state, "state") || !check_out(out->dendrite, "dendrite") ||
-      !check_out(out->adaptation, "adaptation"))
+  if (t.batch > 0 && (!check_out(out->state, "state") || !check_out(out->dendrite, "dendrite") ||
+                      !check_out(out->adaptation, "adaptation")))
     return NSB_ERR_ARGUMENT;
   g_error.clear();
   if (t.batch == 0) return NSB_OK;
@@ -164,8 +164,9 @@ int nsb_dendritic_event(const nsb_tick* tick, float* current, const nsb_view* em
       (out_csr->n_edges > 0 && (!out_csr->dst || !out_csr->weight)))
     return fail(NSB_ERR_ARGUMENT, "invalid event topology geometry");
   if (!out || !out_emitted) return fail(NSB_ERR_ARGUMENT, "outputs are required");
-  if (!check_out(out->state, "state") || !check_out(out->dendrite, "dendrite") ||
-      !check_out(out->adaptation, "adaptation") || !check_out(*out_emitted, "emitted"))
+  if (t.batch > 0 && (!check_out(out->state, "state") || !check_out(out->dendrite, "dendrite") ||
+                      !check_out(out->adaptation, "adaptation") ||
+                      !check_out(*out_emitted, "emitted")))
     return NSB_ERR_ARGUMENT;
   const size_t need = nsb::event_workspace_bytes(t.batch, t.neurons);
   if (!workspace || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)

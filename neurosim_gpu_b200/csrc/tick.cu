@@ -44,9 +44,10 @@ csr_tick_kernel(TickArgs t, View x, const int32_t* __restrict__ rowptr,
 
   for (int64_t base = warp * kRowsPerWarp; base < neurons; base += n_warps * kRowsPerWarp) {
     const int64_t n = base + lane / G;
+    // -0.0 is the exact additive identity: a one-term row keeps a signed zero.
     float acc[BT];
 #pragma unroll
-    for (int b = 0; b < BT; ++b) acc[b] = 0.0f;
+    for (int b = 0; b < BT; ++b) acc[b] = -0.0f;
 
     if (n < neurons) {
       const int64_t e0 = rowptr[n];

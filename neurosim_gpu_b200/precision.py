@@ -46,9 +46,19 @@ def _tiny() -> float:
     return torch.finfo(torch.float32).tiny
 
 
+def _true_div(value: torch.Tensor, constant: float) -> torch.Tensor:
+    """value / constant with IEEE division on every device.
+
+    PyTorch divides a CUDA tensor by a Python scalar as value * (1 / scalar),
+    which can differ from the CPU result by one ulp; a tensor divisor keeps
+    the encoding identical on CPU and GPU.
+    """
+    return value / torch.full_like(value, constant)
+
+
 def _fp8(value: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     amax = value.abs().amax() if value.numel() else value.new_zeros(())
-    scale = (amax / 448.0).clamp_min(_tiny())
+    scale = _true_div(amax, 448.0).clamp_min(_tiny())
     codes = (value / scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
     return codes, scale
 
@@ -63,7 +73,7 @@ def _nvfp4(value: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tenso
     magnitude = blocks.abs()
     block_amax = magnitude.amax(dim=-1, keepdim=True)
     amax = block_amax.amax() if value.numel() else value.new_zeros(())
-    global_scale = (amax / (6.0 * 448.0)).clamp_min(_tiny())
+    global_scale = _true_div(amax, 6.0 * 448.0).clamp_min(_tiny())
     block_scale = (block_amax / (6.0 * global_scale)).clamp_max(448.0).to(torch.float8_e4m3fn)
     denominator = global_scale * block_scale.float()
     normalized = magnitude / torch.where(denominator > 0, denominator, 1.0)

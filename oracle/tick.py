@@ -95,6 +95,9 @@ class CSR:
 
     @classmethod
     def make(cls, n: int, rowptr, col, weight) -> "CSR":
+        for name, value in (("rowptr", rowptr), ("col", col)):
+            if not np.issubdtype(np.asarray(value).dtype, np.integer):
+                raise TypeError(f"{name} must be an integer array (float32 cannot hold >2^24 offsets)")
         rowptr = np.ascontiguousarray(np.asarray(rowptr, dtype=np.int32))
         col = np.ascontiguousarray(np.asarray(col, dtype=np.int32))
         weight = _f32(weight)

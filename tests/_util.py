@@ -34,8 +34,12 @@ def bench_model(n, device="cuda", alpha=0.72, gain=0.8, tau_d=4.0, tau_a=25.0, c
 
 
 def npy(value) -> np.ndarray:
+    """A CPU numpy copy; floating tensors become float32, integer tensors keep their dtype."""
     if isinstance(value, torch.Tensor):
-        return value.detach().float().cpu().numpy()
+        value = value.detach()
+        if value.is_floating_point():
+            value = value.float()
+        return value.cpu().numpy()
     return np.asarray(value, dtype=np.float32)
 
 

@@ -123,3 +123,9 @@ def test_event_rejects_small_workspace(lib):
                                      ctypes.byref(out_csr), ctypes.byref(out),
                                      ctypes.byref(out_emitted), 0xB000, 1 << 20, None)
     assert status == -1 and "theta" in lib.nsb_last_error().decode()
+
+
+def test_empty_batch_needs_no_output_arrays(lib):
+    out = native._TickOut()
+    status, message = _step(lib, _tick(batch=0), _csr(), out=out)
+    assert status == 0 and message == ""
