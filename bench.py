@@ -257,6 +257,7 @@ def run_native(args, workload: str) -> dict:
         e2e_ms = max(e0.elapsed_time(e1), wall * 1e3) / e2e_steps
 
     m = graph.n_edges
+    layout = runtime._tiled_layout()
     rate = m * batch / (tick_ms * 1e-3)
     peak, peak_kind = hbm_peak()
     algo = algorithmic_bytes(neurons, m, batch, precision)
@@ -269,10 +270,17 @@ def run_native(args, workload: str) -> dict:
         "config": {"workload": workload, "neurons": neurons, "edges": m, "batch": batch,
                    "weights": precision, "parallelism": "single GPU",
                    "l2": "inputs larger than L2 (edge stream %.0f MB vs 126 MB)" % (algo / 1e6),
-                   "ticks_per_graph": chunk},
+                   "ticks_per_graph": chunk,
+                   "kernel_path": runtime.kernel_path,
+                   "column_blocks": layout.blocks if layout is not None else None,
+                   "padding_fraction": round(layout.padding_fraction, 4) if layout is not None
+                   else None},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": ncu_traffic(workload),
                      "algorithmic_bytes_per_launch": algo, "peak_source": peak_kind,
+                     "kernel": "tiled_tick_kernel" if layout is not None else "csr_tick_kernel",
+                     "streamed_bytes_per_launch": (layout.stream_bytes() + 28 * batch * neurons
+                                                   if layout is not None else None),
                      "launch_ms_graph": tick_ms, "launch_ms_eager_median": launch_ms},
         "e2e": {"value": m * batch / (e2e_ms * 1e-3), "unit": "synapse-updates/s",
                 "h2d_bytes_per_step": 4 * batch * neurons, "d2h_bytes_per_step": 4 * batch * neurons,

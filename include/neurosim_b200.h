@@ -169,6 +169,50 @@ NSB_API int nsb_dendritic_event(const nsb_tick* tick, float* current, const nsb_
                         const nsb_out* out_emitted, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* Column-blocked layout of one graph for the B = 1 tick (built by the host,
+ * see neurosim_gpu_b200/tiled.py; it re-arranges the destination CSR, the
+ * arithmetic is that of nsb_dendritic_step).
+ *  - CTA c (one per SM) owns destination rows [row_begin[c], row_begin[c+1]).
+ *  - Columns are split into `blocks` blocks of `block_cols` columns; one block
+ *    of the source state is staged in shared memory at a time (`buffers` = 1
+ *    or 2 copies in flight).
+ *  - Task q (tasks of CTA c and block k are task_ptr[c*blocks+k] ..
+ *    task_ptr[c*blocks+k+1]-1) covers 32 rows: lane i owns row
+ *    row_begin[c] + task_rows[32q+i] (-1: no row) and its edges with column in
+ *    block k sit at slots task_offset[q] + 32j + i, j < task_len[q].
+ *  - col[slot] is the column minus the block start; padding slots hold
+ *    block_cols and weight 0.  NVFP4 codes are packed two per byte by slot;
+ *    task_orig[32q+i] is the CSR position of the lane's first edge, which
+ *    selects the original 16-edge block scale of each edge. */
+typedef struct nsb_tiled_layout {
+  int32_t ctas, blocks, block_cols, buffers, max_rows, format;
+  int64_t n_tasks, n_slots, n_block_scales;
+  const int32_t* row_begin;    /* [ctas+1]            */
+  const int32_t* task_ptr;     /* [ctas*blocks+1]     */
+  const int32_t* task_offset;  /* [n_tasks]           */
+  const int32_t* task_len;     /* [n_tasks]           */
+  const int16_t* task_rows;    /* [n_tasks*32]        */
+  const int32_t* task_orig;    /* [n_tasks*32] (NVFP4) */
+  const int32_t* col;          /* [n_slots]           */
+  const void* weight;          /* [n_slots] (NVFP4: [n_slots/2]) */
+  const uint8_t* block_scales; /* NVFP4: block scales of the original CSR */
+  const float* global_scale;   /* E4M3 / NVFP4        */
+} nsb_tiled_layout;
+
+/* Dynamic shared memory one CTA of the tiled tick needs. */
+NSB_API size_t nsb_tiled_smem_bytes(int32_t block_cols, int32_t max_rows, int32_t buffers);
+
+/* Matrix tick for B = 1 over a tiled layout (same update as nsb_dendritic_step).
+ * The state must be contiguous (neuron_stride 1) and 16-byte aligned.  `status`
+ * (device int, may be NULL) receives a nonzero code if an internal pipeline
+ * wait timed out; it is never cleared by the library. */
+NSB_API int nsb_dendritic_step_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
+                                     const nsb_tick_out* out, int* status, void* stream);
+
+/* result[n] = sum of w[e] * source[col[e]] over the tiled layout (B = 1). */
+NSB_API int nsb_tiled_propagate(int64_t neurons, const nsb_tiled_layout* layout,
+                                const float* source, float* result, int* status, void* stream);
+
 /* Thread-local message of the last failing call ("" if none). */
 NSB_API const char* nsb_last_error(void);
 

@@ -146,6 +146,88 @@ int nsb_csr_propagate(int64_t batch, int64_t neurons, const nsb_csr* csr,
   return NSB_OK;
 }
 
+size_t nsb_tiled_smem_bytes(int32_t block_cols, int32_t max_rows, int32_t buffers) {
+  if (block_cols <= 0 || max_rows < 0 || buffers < 1 || buffers > 2) return 0;
+  return nsb::tiled_smem_bytes(block_cols, max_rows, buffers);
+}
+
+namespace {
+
+bool check_tiled(const nsb_tiled_layout* L, int64_t neurons) {
+  if (!L) return fail(NSB_ERR_ARGUMENT, "tiled layout is required"), false;
+  if (L->ctas <= 0 || L->blocks <= 0 || L->block_cols <= 0 || L->block_cols % 4 != 0 ||
+      (L->buffers != 1 && L->buffers != 2) || L->max_rows < 0 || L->n_tasks < 0 ||
+      L->n_slots < 0 || static_cast<int64_t>(L->blocks) * L->block_cols < neurons)
+    return fail(NSB_ERR_ARGUMENT, "invalid tiled layout geometry"), false;
+  if (!L->row_begin || !L->task_ptr || (L->n_tasks > 0 && (!L->task_offset || !L->task_len ||
+                                                          !L->task_rows)) ||
+      (L->n_slots > 0 && (!L->col || !L->weight)))
+    return fail(NSB_ERR_ARGUMENT, "tiled layout arrays are required"), false;
+  switch (L->format) {
+    case NSB_WEIGHT_F32:
+    case NSB_WEIGHT_F16:
+      break;
+    case NSB_WEIGHT_E4M3:
+      if (!L->global_scale) return fail(NSB_ERR_ARGUMENT, "quantized weights require a global scale"), false;
+      break;
+    case NSB_WEIGHT_NVFP4:
+      if (!L->global_scale || (L->n_tasks > 0 && (!L->task_orig || !L->block_scales)) ||
+          L->n_block_scales <= 0 || L->n_slots % 2 != 0)
+        return fail(NSB_ERR_ARGUMENT, "invalid NVFP4 tiled layout"), false;
+      break;
+    default:
+      return fail(NSB_ERR_ARGUMENT, "unknown CSR weight format"), false;
+  }
+  int device = 0, optin = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err == cudaSuccess)
+    err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  if (err != cudaSuccess) return cuda_fail(err, "shared memory query"), false;
+  if (nsb::tiled_smem_bytes(L->block_cols, L->max_rows, L->buffers) > static_cast<size_t>(optin))
+    return fail(NSB_ERR_ARGUMENT, "tiled layout needs more shared memory than a CTA can use"), false;
+  return true;
+}
+
+}  // namespace
+
+int nsb_dendritic_step_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
+                             const nsb_tick_out* out, int* status, void* stream) {
+  nsb::TickArgs t;
+  if (!check_tick(tick, &t)) return NSB_ERR_ARGUMENT;
+  if (t.batch != 1) return fail(NSB_ERR_ARGUMENT, "the tiled tick takes B = 1");
+  if (t.s.sn != 1 || reinterpret_cast<uintptr_t>(t.s.data) % 16 != 0)
+    return fail(NSB_ERR_ARGUMENT, "the tiled tick needs a contiguous, 16-byte aligned state");
+  if (!out || !check_out(out->state, "state") || !check_out(out->dendrite, "dendrite") ||
+      !check_out(out->adaptation, "adaptation"))
+    return NSB_ERR_ARGUMENT;
+  if (!check_tiled(layout, t.neurons)) return g_error.rfind("shared memory query", 0) == 0
+                                                  ? NSB_ERR_CUDA : NSB_ERR_ARGUMENT;
+  g_error.clear();
+  const nsb::TickOut o{to_out(out->state), to_out(out->dendrite), to_out(out->adaptation)};
+  const cudaError_t err = nsb::launch_tiled(*layout, t, t.s.data, true, o, nsb::Out{nullptr, 0, 0},
+                                            status, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_step_tiled launch");
+  return NSB_OK;
+}
+
+int nsb_tiled_propagate(int64_t neurons, const nsb_tiled_layout* layout, const float* source,
+                        float* result, int* status, void* stream) {
+  if (neurons <= 0) return fail(NSB_ERR_ARGUMENT, "source must be [1,N], N > 0");
+  if (!source || !result) return fail(NSB_ERR_ARGUMENT, "source and result arrays are required");
+  if (reinterpret_cast<uintptr_t>(source) % 16 != 0)
+    return fail(NSB_ERR_ARGUMENT, "the tiled product needs a 16-byte aligned source");
+  if (!check_tiled(layout, neurons)) return NSB_ERR_ARGUMENT;
+  g_error.clear();
+  nsb::TickArgs t{};
+  t.batch = 1;
+  t.neurons = neurons;
+  const cudaError_t err = nsb::launch_tiled(*layout, t, source, false, nsb::TickOut{},
+                                            nsb::Out{result, 0, 1}, status,
+                                            static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_tiled_propagate launch");
+  return NSB_OK;
+}
+
 size_t nsb_dendritic_event_workspace_size(int64_t batch, int64_t neurons) {
   if (batch < 0 || neurons < 0) return 0;
   return nsb::event_workspace_bytes(batch, neurons);

@@ -73,6 +73,19 @@ class _OutCsr(ctypes.Structure):
                 ("weight", ctypes.c_void_p)]
 
 
+class _TiledLayout(ctypes.Structure):
+    _fields_ = [("ctas", ctypes.c_int32), ("blocks", ctypes.c_int32),
+                ("block_cols", ctypes.c_int32), ("buffers", ctypes.c_int32),
+                ("max_rows", ctypes.c_int32), ("format", ctypes.c_int32),
+                ("n_tasks", ctypes.c_int64), ("n_slots", ctypes.c_int64),
+                ("n_block_scales", ctypes.c_int64),
+                ("row_begin", ctypes.c_void_p), ("task_ptr", ctypes.c_void_p),
+                ("task_offset", ctypes.c_void_p), ("task_len", ctypes.c_void_p),
+                ("task_rows", ctypes.c_void_p), ("task_orig", ctypes.c_void_p),
+                ("col", ctypes.c_void_p), ("weight", ctypes.c_void_p),
+                ("block_scales", ctypes.c_void_p), ("global_scale", ctypes.c_void_p)]
+
+
 class EventCounters(ctypes.Structure):
     """Head of the nsb_dendritic_event workspace (nsb_event_counters)."""
 
@@ -83,6 +96,7 @@ class EventCounters(ctypes.Structure):
 
 EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_dendritic_event_workspace_size", "nsb_dendritic_event",
+                    "nsb_tiled_smem_bytes", "nsb_dendritic_step_tiled", "nsb_tiled_propagate",
                     "nsb_last_error", "nsb_abi_version")
 
 
@@ -104,6 +118,12 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_dendritic_event.argtypes = [p(_Tick), ctypes.c_void_p, p(_View), ctypes.c_void_p,
                                         ctypes.c_int64, p(_OutCsr), p(_TickOut), p(_Out),
                                         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.nsb_tiled_smem_bytes.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
+    lib.nsb_tiled_smem_bytes.restype = ctypes.c_size_t
+    lib.nsb_dendritic_step_tiled.argtypes = [p(_Tick), p(_TiledLayout), p(_TickOut),
+                                             ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_tiled_propagate.argtypes = [ctypes.c_int64, p(_TiledLayout), ctypes.c_void_p,
+                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_last_error.restype = ctypes.c_char_p
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
@@ -270,6 +290,58 @@ class DendriticExtension:
             _raise_on_status(lib, status)
 
         return launch
+
+    def prepare_step_tiled(self, state, dendrite, adaptation, params, layout, input,
+                           input_scalar, dendritic_input, dendritic_scalar, *, out, status=None):
+        """Like :meth:`prepare_step` for B = 1 over a :class:`~neurosim_gpu_b200.tiled.TiledLayout`."""
+        _check_state(state)
+        _check(state.size(0) == 1, "the tiled tick takes B = 1")
+        _check(state.stride(1) == 1 and state.data_ptr() % 16 == 0,
+               "the tiled tick needs a contiguous, 16-byte aligned state")
+        _check(layout.neurons == state.size(1), "layout and state neuron counts differ")
+        tick = _tick(state, dendrite, adaptation, params, input, input_scalar,
+                     dendritic_input, dendritic_scalar)
+        for view in out:
+            _float_on(view, state)
+            _check(view.shape == state.shape, "output shape mismatch")
+        result = _TickOut(_out(out[0]), _out(out[1]), _out(out[2]))
+        c_layout = layout.c_struct()
+        status_ptr = status.data_ptr() if status is not None else None
+        lib, device = self.lib, state.device
+        keep = (state, dendrite, adaptation, params, layout, input, dendritic_input, out, status)
+
+        def launch() -> None:
+            assert keep is not None
+            with torch.cuda.device(device):
+                code = lib.nsb_dendritic_step_tiled(ctypes.byref(tick), ctypes.byref(c_layout),
+                                                    ctypes.byref(result), status_ptr,
+                                                    _stream(device))
+            _raise_on_status(lib, code)
+
+        return launch
+
+    def dendritic_step_tiled(self, state, dendrite, adaptation, params, layout, input,
+                             input_scalar, dendritic_input, dendritic_scalar, status=None):
+        _check_state(state)
+        _, views = _outputs(3, state)
+        self.prepare_step_tiled(state, dendrite, adaptation, params, layout, input, input_scalar,
+                                dendritic_input, dendritic_scalar, out=views, status=status)()
+        return views
+
+    def tiled_propagate(self, layout, x, status=None):
+        """j = W @ x for x [1,N] over a tiled layout; a fresh [1,N] tensor."""
+        _check_state(x)
+        _check(x.size(0) == 1 and x.stride(1) == 1 and x.data_ptr() % 16 == 0,
+               "the tiled product needs a contiguous, 16-byte aligned [1,N] source")
+        result = torch.empty_like(x, memory_format=torch.contiguous_format)
+        c_layout = layout.c_struct()
+        with torch.cuda.device(x.device):
+            code = self.lib.nsb_tiled_propagate(x.size(1), ctypes.byref(c_layout), x.data_ptr(),
+                                                result.data_ptr(),
+                                                status.data_ptr() if status is not None else None,
+                                                _stream(x.device))
+        _raise_on_status(self.lib, code)
+        return result
 
     def dendritic_step(self, state, dendrite, adaptation, params, rowptr, source, weight,
                        input, input_scalar, dendritic_input, dendritic_scalar, width,

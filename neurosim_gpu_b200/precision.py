@@ -131,6 +131,18 @@ def quantize_dequantize(value: torch.Tensor, precision: str) -> torch.Tensor:
     return _straight_through(value, decoded)
 
 
+def e4m3_to_float(codes: torch.Tensor) -> torch.Tensor:
+    """Exact float32 values of E4M3FN byte codes."""
+    return codes.contiguous().view(torch.float8_e4m3fn).float()
+
+
+def e2m1_to_float(codes: torch.Tensor) -> torch.Tensor:
+    """Exact float32 values of 4-bit E2M1 codes (sign in bit 3)."""
+    levels = _levels(codes.device, torch.float32)
+    magnitude = levels[(codes & 7).long()]
+    return torch.where(codes >= 8, -magnitude, magnitude)
+
+
 def weight_storage_bytes(n_edges: int, precision: str) -> int:
     """Logical packed payload (native_compartmental.py:92-100)."""
     if precision == "nvfp4":

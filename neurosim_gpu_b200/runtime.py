@@ -30,6 +30,7 @@ from dataclasses import dataclass
 import torch
 
 from . import native as _native
+from . import tiled as _tiled
 from .dynamics import DendriticDynamics
 from .precision import encode_sparse_weights, validate_precision, weight_storage_bytes
 from .topology import SparseTopology
@@ -150,7 +151,8 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
     def __init__(self, topology: SparseTopology, dynamics: DendriticDynamics,
                  initial_state: torch.Tensor, *, threads_per_row: int | None = None,
                  extension=None, weight_dtype: torch.dtype = torch.float32,
-                 weight_format: str | None = None, precision: str | None = None) -> None:
+                 weight_format: str | None = None, precision: str | None = None,
+                 kernel: str = "auto") -> None:
         if precision is not None:
             validate_precision(precision)
             if weight_format is not None or weight_dtype != torch.float32:
@@ -167,7 +169,13 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
             raise ValueError("weight_format must be None, 'fp8' or 'nvfp4'")
         if weight_format is not None and weight_dtype != torch.float32:
             raise ValueError("weight_format and non-default weight_dtype conflict")
+        if kernel not in ("auto", "csr", "tiled"):
+            raise ValueError("kernel must be 'auto', 'csr' or 'tiled'")
+        self.kernel = kernel
         self._init_compartments(topology, dynamics, initial_state, extension)
+        self._status = _tiled.status_word(initial_state.device)
+        self._layout = None
+        self._layout_key = None
         degree = topology.n_edges / max(topology.n_neurons, 1)
         # Lanes per row; each lane reads 4-edge chunks, so 32 lanes cover 128 edges.
         self.threads_per_row = threads_per_row or (8 if degree <= 16 else 16 if degree <= 48
@@ -182,6 +190,54 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         self._packed_weight = None
         self._packed_weight_version = -1
         self._graphs = {}
+        self._layout = None
+        self._layout_key = None
+
+    @property
+    def kernel_path(self) -> str:
+        """'tiled' (B = 1, state gathered from shared memory) or 'csr' (any B)."""
+        return "tiled" if self._tiled_layout() is not None else "csr"
+
+    def check_status(self) -> None:
+        """Raise if a tiled launch reported an internal pipeline timeout (reads the device)."""
+        code = int(self._status.item())
+        if code:
+            raise RuntimeError(f"tiled tick pipeline timeout (code {code})")
+
+    def _tiled_layout(self):
+        """The column-blocked layout of the current weights, or None if not used."""
+        if self.kernel == "csr" or self.state.shape[0] != 1 or self.topology.n_edges == 0:
+            return None
+        key = (self.topology.weight_version, self.checkpoint_precision, self.state.device)
+        if self._layout_key != key:
+            weight, scales, scale, _ = self._weights()
+            device = self.state.device
+            try:
+                self._layout = _tiled.build_tiled_layout(
+                    self.topology.in_rowptr, self.topology.in_col, weight.detach(),
+                    neurons=self.topology.n_neurons, ctas=_tiled.sm_count(device),
+                    smem_limit=_tiled.smem_limit(device), block_scales=scales,
+                    global_scale=scale)
+            except ValueError:
+                if self.kernel == "tiled":
+                    raise
+                self._layout = None
+            self._layout_key = key
+        return self._layout
+
+    def _prepare(self, s, d, a, u, us, v, vs, out):
+        """A launch callable for one tick from (s, d, a) into the three `out` tensors."""
+        layout = self._tiled_layout()
+        if layout is not None:
+            if s.stride(1) != 1 or s.data_ptr() % 16:
+                s = s.contiguous().clone()
+            return self.extension.prepare_step_tiled(s, d, a, self._parameters(), layout, u, us,
+                                                     v, vs, out=out, status=self._status)
+        weight, scales, scale, _ = self._weights()
+        topology = self.topology
+        return self.extension.prepare_step(s, d, a, self._parameters(), topology.in_rowptr,
+                                           topology.in_col, weight, u, us, v, vs,
+                                           self.threads_per_row, scales, scale, out=out)
 
     @property
     def checkpoint_precision(self) -> str:
@@ -231,12 +287,11 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
             return self.state
         u, us = self._drive(drive)
         v, vs = self._drive(dendritic_drive, "dendritic_drive")
-        weight, scales, scale, backend = self._weights()
-        topology = self.topology
-        self.state, self.dendritic_state, self.adaptation_state = self.extension.dendritic_step(
-            self.state, self.dendritic_state, self.adaptation_state, self._parameters(),
-            topology.in_rowptr, topology.in_col, weight, u, us, v, vs, self.threads_per_row,
-            scales, scale)
+        backend = self._weights()[3]
+        _, views = _native._outputs(3, self.state)
+        self._prepare(self.state, self.dendritic_state, self.adaptation_state, u, us, v, vs,
+                      views)()
+        self.state, self.dendritic_state, self.adaptation_state = views
         self.last_backend = backend
         return self.state
 
@@ -259,7 +314,8 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
             return self.state
         u, us = self._drive(drive)
         v, vs = self._drive(dendritic_drive, "dendritic_drive")
-        weight, scales, scale, backend = self._weights()
+        weight, _, _, backend = self._weights()
+        self._tiled_layout()  # build outside any capture
         graph_ticks = max(1, min(graph_ticks, ticks))
         key = (graph_ticks, tuple(self.state.shape),
                None if u is None else (u.data_ptr(), u.stride()), us,
@@ -269,8 +325,7 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         entry = self._graphs.get(key)
         if entry is None:
             self._graphs = {}
-            entry = self._graphs[key] = _TickGraph(self, graph_ticks, u, us, v, vs, weight,
-                                                   scales, scale)
+            entry = self._graphs[key] = _TickGraph(self, graph_ticks, u, us, v, vs)
         entry.load(self.state, self.dendritic_state, self.adaptation_state)
         for _ in range(ticks // graph_ticks):
             entry.replay()
@@ -286,23 +341,17 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
 class _TickGraph:
     """A CUDA graph of ``ticks`` native ticks ping-ponging between two buffers."""
 
-    def __init__(self, runtime: NativeDendriticMatrixRuntime, ticks: int, u, us, v, vs,
-                 weight, scales, scale) -> None:
-        ext = runtime.extension
+    def __init__(self, runtime: NativeDendriticMatrixRuntime, ticks: int, u, us, v, vs) -> None:
         state = runtime.state
         self.ticks = ticks
         self.buffers = [_native._outputs(3, state)[1] for _ in range(2)]
-        topology = runtime.topology
-        params = runtime._parameters()
         self.graph = torch.cuda.CUDAGraph()
         stream = torch.cuda.Stream(device=state.device)
         stream.wait_stream(torch.cuda.current_stream(state.device))
         calls = []
         for k in range(ticks):
             src, dst = self.buffers[k % 2], self.buffers[(k + 1) % 2]
-            calls.append(ext.prepare_step(src[0], src[1], src[2], params, topology.in_rowptr,
-                                          topology.in_col, weight, u, us, v, vs,
-                                          runtime.threads_per_row, scales, scale, out=dst))
+            calls.append(runtime._prepare(src[0], src[1], src[2], u, us, v, vs, dst))
         with torch.cuda.stream(stream):
             calls[0]()  # warm-up outside capture (kernel attributes, occupancy queries)
         torch.cuda.current_stream(state.device).wait_stream(stream)

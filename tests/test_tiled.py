@@ -1,0 +1,112 @@
+"""The column-blocked B = 1 tick (nsb_dendritic_step_tiled) against the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from _util import OracleMatrix, assert_same_as, bench_model, csr_of, make, npy
+from neurosim_gpu_b200 import (NativeDendriticMatrixRuntime, encode_sparse_weights,
+                               load_native_extension, quantize_dequantize, random_topology)
+from neurosim_gpu_b200 import native
+from neurosim_gpu_b200.tiled import build_tiled_layout, emulate
+
+
+def _packed(graph, fmt):
+    if fmt == "fp32":
+        return graph.in_weight, None, None, graph.in_weight
+    if fmt == "fp16":
+        return graph.in_weight.half(), None, None, graph.in_weight.half().float()
+    codes, scales, scale = encode_sparse_weights(graph.in_weight, fmt)
+    return codes, scales, scale, quantize_dequantize(graph.in_weight, fmt)
+
+
+def _smem_bytes():
+    lib = native.load_library()
+    return lambda cols, rows, bufs: int(lib.nsb_tiled_smem_bytes(cols, rows, bufs))
+
+
+@pytest.mark.parametrize("fmt", ["fp32", "fp16", "fp8", "nvfp4"])
+@pytest.mark.parametrize("n,m,ctas,smem", [(97, 600, 4, 232448), (2000, 60000, 8, 8000),
+                                           (5000, 100000, 16, 6000), (3001, 40001, 5, 232448)])
+def test_layout_emulation_matches_oracle_cpu(fmt, n, m, ctas, smem):
+    """The layout builder alone, emulated on CPU (no GPU needed)."""
+    graph = random_topology(n, m, device="cpu", seed=3)
+    weight, scales, scale, decoded = _packed(graph, fmt)
+    layout = build_tiled_layout(graph.in_rowptr, graph.in_col, weight, neurons=n, ctas=ctas,
+                                smem_limit=smem, block_scales=scales, global_scale=scale,
+                                smem_bytes=_smem_bytes())
+    x = torch.rand(1, n, generator=torch.Generator().manual_seed(1))
+    want = oracle.spmv(csr_of(graph, decoded), npy(x))[0]
+    np.testing.assert_allclose(emulate(layout, x).numpy(), want, atol=1e-6, rtol=0)
+    assert layout.n_slots >= graph.n_edges
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["fp32", "fp16", "fp8", "nvfp4"])
+@pytest.mark.parametrize("n,m,ctas,smem", [(97, 600, 4, 232448), (2000, 60000, 8, 8000),
+                                           (5000, 100000, 16, 6000), (3001, 40001, 5, 232448),
+                                           (20000, 400000, 148, 24000)])
+def test_tiled_tick_matches_oracle(fmt, n, m, ctas, smem):
+    ext = load_native_extension()
+    graph = random_topology(n, m, device="cpu", seed=3).to("cuda")
+    weight, scales, scale, decoded = _packed(graph, fmt)
+    layout = build_tiled_layout(graph.in_rowptr, graph.in_col, weight, neurons=n, ctas=ctas,
+                                smem_limit=smem, block_scales=scales, global_scale=scale)
+    model = bench_model(n)
+    state = torch.rand(1, n, generator=torch.Generator().manual_seed(2)).cuda()
+    dendrite = torch.rand(1, n, generator=torch.Generator().manual_seed(4)).cuda() - 0.5
+    adaptation = torch.rand(1, n, generator=torch.Generator().manual_seed(5)).cuda()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    # product
+    got = ext.tiled_propagate(layout, state, status=status)
+    want = oracle.spmv(csr_of(graph, decoded), npy(state))
+    np.testing.assert_allclose(npy(got), want, atol=2e-6, rtol=0)
+    # tick
+    s, d, a = ext.dendritic_step_tiled(state, dendrite, adaptation, model.parameters(), layout,
+                                       None, 0.2, None, 0.1, status=status)
+    ws, wd, wa = oracle.matrix_tick(csr_of(graph, decoded), npy(state), npy(dendrite),
+                                    npy(adaptation), [npy(p) for p in model.parameters()], 0.2, 0.1)
+    for got, want in ((s, ws), (d, wd), (a, wa)):
+        np.testing.assert_allclose(npy(got), want, atol=2e-6, rtol=0)
+    assert int(status.item()) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["fp32", "nvfp4"])
+def test_runtime_uses_tiled_path_for_single_batch(fmt):
+    graph, model, state = make(3000, 1, 90000)
+    tiled = NativeDendriticMatrixRuntime(graph, model, state.clone(), precision=fmt)
+    csr = NativeDendriticMatrixRuntime(graph, model, state.clone(), precision=fmt, kernel="csr")
+    decoded = quantize_dequantize(graph.in_weight, fmt)
+    reference = OracleMatrix(graph, model, state, weight=decoded)
+    with torch.inference_mode():
+        for _ in range(20):
+            tiled.step(0.2, dendritic_drive=0.1)
+            csr.step(0.2, dendritic_drive=0.1)
+            reference.step(0.2, 0.1)
+        tiled.run(45, 0.2, dendritic_drive=0.1, graph_ticks=16)
+        csr.run(45, 0.2, dendritic_drive=0.1, graph_ticks=16)
+    for _ in range(45):
+        reference.step(0.2, 0.1)
+    assert tiled.kernel_path == "tiled" and csr.kernel_path == "csr"
+    assert_same_as(tiled, reference, atol=2e-6)
+    assert_same_as(tiled, csr, atol=2e-6)
+    tiled.check_status()
+
+
+@pytest.mark.gpu
+def test_tiled_rejects_bad_inputs():
+    ext = load_native_extension()
+    graph, model, state = make(500, 2, 5000)
+    layout = build_tiled_layout(graph.in_rowptr, graph.in_col, graph.in_weight, neurons=500,
+                                ctas=4, smem_limit=232448)
+    with pytest.raises(RuntimeError, match="B = 1"):
+        ext.dendritic_step_tiled(state, state, state, model.parameters(), layout, None, 0.,
+                                 None, 0.)
+    one = state[:1].contiguous()
+    with pytest.raises(RuntimeError, match="aligned"):
+        odd = torch.zeros(1, 501, device="cuda")[:, 1:]
+        ext.dendritic_step_tiled(odd, one, one, model.parameters(), layout, None, 0., None, 0.)
