@@ -169,6 +169,35 @@ NSB_API int nsb_dendritic_event(const nsb_tick* tick, float* current, const nsb_
                         const nsb_out* out_emitted, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* Largest B * N that nsb_dendritic_event_noalloc accepts. */
+#define NSB_EVENT_NOALLOC_MAX_PAIRS (1 << 20)
+
+/* PELS tick without any device allocation (no counterpart in the reference).
+ *
+ * Same arguments, checks and results as nsb_dendritic_event, minus the
+ * workspace: the counters and the emitter queue live in a fixed array inside
+ * the library (256 B + 8 B x NSB_EVENT_NOALLOC_MAX_PAIRS = 8 MiB), which every
+ * GPU that loads the library holds until the process exits.  For hosts that
+ * cannot hand the library scratch memory: an application whose device memory
+ * is all reserved up front by its own pool and that may not allocate during
+ * the simulation loop, or a foreign-language host (cgo, JNI, ...) that only
+ * holds plain device pointers and has no CUDA allocator of its own.
+ *
+ * - B * N above NSB_EVENT_NOALLOC_MAX_PAIRS is rejected with NSB_ERR_ARGUMENT.
+ * - The first call on a device looks up the array's device address with that
+ *   device current (cudaGetSymbolAddress) and keeps it; make that first call
+ *   before any stream capture.
+ * - All calls on a device share the one array, and each call only clears the
+ *   counter head it needs zeroed; calls whose work overlaps on the GPU (other
+ *   streams, other threads) race on the array and must be serialised by the
+ *   caller.
+ * - Calls no cudaMalloc / cudaFree or other allocating routine. */
+NSB_API int nsb_dendritic_event_noalloc(const nsb_tick* tick, float* current,
+                                        const nsb_view* emitted, const float* theta,
+                                        int64_t theta_stride, const nsb_out_csr* out_csr,
+                                        const nsb_tick_out* out, const nsb_out* out_emitted,
+                                        void* stream);
+
 /* Column-blocked layout of one graph for the B = 1 tick (built by the host,
  * see neurosim_gpu_b200/tiled.py; it re-arranges the destination CSR, the
  * arithmetic is that of nsb_dendritic_step).

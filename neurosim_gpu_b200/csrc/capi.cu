@@ -274,4 +274,24 @@ int nsb_dendritic_event(const nsb_tick* tick, float* current, const nsb_view* em
   return NSB_OK;
 }
 
+int nsb_dendritic_event_noalloc(const nsb_tick* tick, float* current, const nsb_view* emitted,
+                                const float* theta, int64_t theta_stride,
+                                const nsb_out_csr* out_csr, const nsb_tick_out* out,
+                                const nsb_out* out_emitted, void* stream) {
+  if (tick && tick->batch > 0 && tick->neurons > 0 &&
+      tick->batch * tick->neurons > static_cast<int64_t>(NSB_EVENT_NOALLOC_MAX_PAIRS))
+    return fail(NSB_ERR_ARGUMENT,
+                "nsb_dendritic_event_noalloc: B*N = " + std::to_string(tick->batch * tick->neurons) +
+                    " exceeds its fixed scratch of " + std::to_string(NSB_EVENT_NOALLOC_MAX_PAIRS) +
+                    " pairs; use nsb_dendritic_event with a caller workspace");
+  void* scratch = nullptr;
+  const cudaError_t err = nsb::event_noalloc_scratch(&scratch);
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_event_noalloc scratch address");
+  return nsb_dendritic_event(tick, current, emitted, theta, theta_stride, out_csr, out,
+                             out_emitted, scratch,
+                             nsb::event_workspace_bytes(tick ? tick->batch : 0,
+                                                        tick ? tick->neurons : 0),
+                             stream);
+}
+
 }  // extern "C"

@@ -56,4 +56,8 @@ cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, cons
 cudaError_t launch_event(const TickArgs& t, const EventArgs& e, const TickOut& out,
                          const Out& out_emitted, void* workspace, cudaStream_t stream);
 
+// Address of the fixed scratch array used by nsb_dendritic_event_noalloc on the
+// current device (pels.cu; first call per device looks it up).
+cudaError_t event_noalloc_scratch(void** address);
+
 }  // namespace nsb

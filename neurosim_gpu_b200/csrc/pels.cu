@@ -14,6 +14,7 @@
 //   (csrc/compartmental.cu:160-173).
 // Stream order makes launch 1 read the current before launch 2 updates it.
 #include <algorithm>
+#include <mutex>
 
 #include "nsb_launch.h"
 
@@ -165,6 +166,39 @@ cudaError_t launch_scatter(const EventArgs& e, int64_t neurons, const uint2* que
 
 size_t event_workspace_bytes(int64_t batch, int64_t neurons) {
   return 256 + static_cast<size_t>(batch * neurons) * sizeof(uint2);
+}
+
+// ---------------------------------------------------------------------------
+// Scratch for nsb_dendritic_event_noalloc: a fixed array in the library's own
+// device image, so that entry point needs no allocation from its caller or
+// from the library.  It holds the counter head and the emitter queue of
+// NSB_EVENT_NOALLOC_MAX_PAIRS (b, n) pairs, lives on every GPU that loads the
+// library until the process exits, and is shared by all calls on that GPU.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_event_scratch[256 + NSB_EVENT_NOALLOC_MAX_PAIRS * 8];
+
+namespace {
+std::mutex g_scratch_mutex;
+void* g_scratch_address[64] = {nullptr};
+}  // namespace
+
+// Device address of g_event_scratch on the current device.  The host-side name
+// of the array is only a stand-in; the first call on each device asks the
+// runtime for the real address (with that device current) and keeps it.
+cudaError_t event_noalloc_scratch(void** address) {
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return err;
+  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_address[device]) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_event_scratch);
+    if (err != cudaSuccess) return err;
+    g_scratch_address[device] = ptr;
+  }
+  *address = g_scratch_address[device];
+  return cudaSuccess;
 }
 
 cudaError_t launch_event(const TickArgs& t, const EventArgs& e, const TickOut& out,

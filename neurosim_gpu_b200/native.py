@@ -97,7 +97,7 @@ class EventCounters(ctypes.Structure):
 EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_dendritic_event_workspace_size", "nsb_dendritic_event",
                     "nsb_tiled_smem_bytes", "nsb_dendritic_step_tiled", "nsb_tiled_propagate",
-                    "nsb_last_error", "nsb_abi_version")
+                    "nsb_dendritic_event_noalloc", "nsb_last_error", "nsb_abi_version")
 
 
 @functools.lru_cache(maxsize=1)
@@ -124,6 +124,9 @@ def load_library() -> ctypes.CDLL:
                                              ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_tiled_propagate.argtypes = [ctypes.c_int64, p(_TiledLayout), ctypes.c_void_p,
                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_dendritic_event_noalloc.argtypes = [p(_Tick), ctypes.c_void_p, p(_View),
+                                                ctypes.c_void_p, ctypes.c_int64, p(_OutCsr),
+                                                p(_TickOut), p(_Out), ctypes.c_void_p]
     lib.nsb_last_error.restype = ctypes.c_char_p
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
@@ -411,6 +414,49 @@ class DendriticExtension:
                 _stream(state.device))
         _raise_on_status(self.lib, status)
         return views
+
+
+def _event_noalloc(ext: DendriticExtension, state, dendrite, adaptation, params, current,
+                   emitted, theta, out_rowptr, dst, out_weight_index, weight, input,
+                   input_scalar, dendritic_input, dendritic_scalar):
+    """PELS tick through ``nsb_dendritic_event_noalloc``: no workspace from the caller.
+
+    For hosts that cannot give the library scratch memory (device memory
+    reserved up front by the application's own pool, or a foreign-language host
+    without a CUDA allocator).  The library's fixed scratch array is shared by
+    all such calls on a GPU, so calls must not overlap on the GPU.  Outputs are
+    allocated here, as in :meth:`DendriticExtension.dendritic_event`.
+    """
+    _check_state(state)
+    tick = _tick(state, dendrite, adaptation, params, input, input_scalar, dendritic_input,
+                 dendritic_scalar)
+    emitted_view = _view(emitted, state)
+    _view(current, state)
+    _check(current.is_contiguous(), "persistent current must be contiguous")
+    _index(out_rowptr, state)
+    _index(dst, state)
+    if out_weight_index is not None:
+        _index(out_weight_index, state)
+    _float_on(weight, state)
+    _float_on(theta, state)
+    _check(theta.dim() == 1 and theta.numel() == state.size(1), "theta must have N values")
+    edges = dst.numel()
+    out_csr = _OutCsr(edges, out_rowptr.data_ptr(), dst.data_ptr() if edges else None,
+                      out_weight_index.data_ptr() if (out_weight_index is not None and edges)
+                      else None, weight.data_ptr() if edges else None)
+    _, views = _outputs(4, state, neuron_major=False)
+    out = _TickOut(_out(views[0]), _out(views[1]), _out(views[2]))
+    out_emitted = _out(views[3])
+    with torch.cuda.device(state.device):
+        status = ext.lib.nsb_dendritic_event_noalloc(
+            ctypes.byref(tick), current.data_ptr(), ctypes.byref(emitted_view), theta.data_ptr(),
+            theta.stride(0), ctypes.byref(out_csr), ctypes.byref(out), ctypes.byref(out_emitted),
+            _stream(state.device))
+    _raise_on_status(ext.lib, status)
+    return views
+
+
+DendriticExtension.dendritic_event_noalloc = _event_noalloc
 
 
 @functools.lru_cache(maxsize=1)
