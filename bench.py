@@ -18,7 +18,14 @@ stream), B=1, fp32 weights, constant drives 0.2 / 0.1.  A step is one tick.
 
 ``--impl reference`` times that CPU implementation alone (the reference path
 is Python/PyTorch-CPU and cannot run on the GPU box; its arithmetic is the
-oracle's).  ``--gpus N`` under torchrun shards destination rows across ranks.
+oracle's).
+
+``--gpus N`` (under torchrun, one rank per GPU) row-shards the graph over the
+ranks and all-gathers the soma vector every tick (NCCL).  With the default
+workload the graph grows with N -- N*166,000 neurons and N*25M candidate
+edges, i.e. a fixed 166k-row, ~25M-edge share per GPU ("scaling": "weak"; at
+N = 8 this is the 1.33M / 200M graph).  An explicit ``--workload`` is split
+over the N GPUs as it is ("scaling": "strong").
 """
 
 from __future__ import annotations
@@ -170,19 +177,22 @@ def build_graph(neurons: int, edges: int, device):
     return random_topology(neurons, edges, device="cpu", seed=0, build_device=device)
 
 
-def run_reference(args, workload: str) -> dict:
+def run_reference(args, workload: str, explicit_workload: bool, world: int) -> dict:
     neurons, edges, batch, precision = WORKLOADS[workload]
+    name = workload
+    if world > 1 and not explicit_workload:
+        neurons, edges = neurons * world, edges * world
+        name = f"matrix_weak_n{neurons}_m{edges}_b{batch}_{precision}"
     graph = random_topology(neurons, edges, device="cpu", seed=0)
-    for _ in range(args.warmup):
-        pass
-    rate, per_tick, ticks, cores = cpu_oracle_rate(graph, batch, seconds=1e9,
+    # Each step is one full tick; the run is capped at about a minute of CPU time.
+    rate, per_tick, ticks, cores = cpu_oracle_rate(graph, batch, seconds=60.0,
                                                    max_ticks=max(args.steps, 1))
     return {
         "metric": "synapse-updates/s (M*B/tick)", "value": rate, "unit": "synapse-updates/s",
         "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": per_tick * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference random_topology stream, seed 0)",
-        "config": {"workload": workload, "neurons": neurons, "edges": graph.n_edges,
+        "config": {"workload": name, "neurons": neurons, "edges": graph.n_edges,
                    "batch": batch, "weights": "fp32"},
         "cpu_baseline": {"value": rate, "unit": "synapse-updates/s", "cores": cores,
                          "kind": "port", "sample": f"{ticks} ticks of the full graph"},
@@ -297,6 +307,107 @@ def run_native(args, workload: str) -> dict:
     return result
 
 
+def run_sharded(args, explicit_workload: bool) -> dict:
+    """Row-sharded ticks on every rank of the torchrun job; rank 0 reports."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from neurosim_gpu_b200.sharded import ShardedDendriticMatrixRuntime, broadcast_graph
+
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", device_id=device,
+                            timeout=datetime.timedelta(seconds=300))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    neurons, edges, batch, precision = WORKLOADS[args.workload]
+    if explicit_workload:
+        scaling, name = "strong", args.workload
+    else:
+        neurons, edges = neurons * world, edges * world
+        scaling = "weak"
+        name = f"matrix_weak_n{neurons}_m{edges}_b{batch}_{precision}"
+    graph = broadcast_graph(neurons, edges, seed=0, device=device)
+    m = int(graph[1].numel())
+    model = bench_model(neurons, device)
+    runtime = ShardedDendriticMatrixRuntime(graph, model, torch.zeros(batch, neurons, device=device),
+                                            precision=precision)
+    chunk = 32
+    steps = max(args.steps - args.steps % chunk, chunk)
+
+    def timed(fn) -> float:
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1)], device=device)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    with torch.inference_mode():
+        runtime.run(max(args.warmup, chunk), 0.2, dendritic_drive=0.1, graph_ticks=chunk)
+        torch.cuda.synchronize()
+        sampler = ClockSampler(local_rank) if rank == 0 else None
+        if sampler:
+            sampler.__enter__()
+        total_ms = timed(lambda: runtime.run(steps, 0.2, dendritic_drive=0.1, graph_ticks=chunk))
+        if sampler:
+            sampler.__exit__(None, None, None)
+        tick_ms = total_ms / steps
+        # End to end through the public step(): per step every rank copies its rows'
+        # drive in from pinned host memory and its rows' new state back out.
+        rows = runtime.shard.rows
+        host_drive = torch.full((batch, rows), 0.2).pin_memory()
+        host_state = torch.empty((batch, rows)).pin_memory()
+        dev_drive = torch.zeros((batch, neurons), device=device)
+        lo, hi = runtime.shard.lo, runtime.shard.hi
+        e2e_steps = min(steps, 512)
+
+        def e2e():
+            for _ in range(e2e_steps):
+                dev_drive[:, lo:hi].copy_(host_drive, non_blocking=True)
+                runtime.step(dev_drive, dendritic_drive=0.1)
+                host_state.copy_(runtime.shard.own(runtime.shard.current), non_blocking=True)
+
+        e2e()
+        e2e_ms = timed(e2e) / e2e_steps
+    runtime.check_status()
+    layout = runtime.layout
+    local_algo = algorithmic_bytes(rows, runtime.local_edges, batch, precision)
+    peak, peak_kind = hbm_peak()
+    achieved = local_algo / (tick_ms * 1e-3) / 1e9
+    result = {
+        "metric": "synapse-updates/s (M*B/tick)", "value": m * batch / (tick_ms * 1e-3),
+        "unit": "synapse-updates/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": tick_ms, "higher_is_better": True, "scaling": scaling,
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (reference random_topology stream, seed 0; drives 0.2/0.1)",
+        "config": {"workload": name, "neurons": neurons, "edges": m, "batch": batch,
+                   "weights": precision, "parallelism": f"row-sharded x{world}, NCCL all-gather",
+                   "l2": "inputs larger than L2", "kernel_path": runtime.kernel_path,
+                   "column_blocks": layout.blocks if layout is not None else None,
+                   "ticks_per_graph": chunk},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None, "per_gpu": True,
+                     "algorithmic_bytes_per_launch": local_algo, "peak_source": peak_kind,
+                     "kernel": "tiled_tick_kernel" if layout is not None else "csr_tick_kernel"},
+        "e2e": {"value": m * batch / (e2e_ms * 1e-3), "unit": "synapse-updates/s",
+                "h2d_bytes_per_step": 4 * batch * neurons, "d2h_bytes_per_step": 4 * batch * neurons,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": steps * world,
+        "clocks": sampler.summary() if sampler else None,
+    }
+    runtime.release_graphs()
+    torch.cuda.synchronize()
+    dist.barrier()
+    dist.destroy_process_group()
+    return result
+
+
 def run_profile(args, workload: str) -> None:
     """Eager ticks only (no graph, no copies, no CPU leg): the command ncu captures.
 
@@ -325,12 +436,15 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=4096)
     parser.add_argument("--warmup", type=int, default=64)
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
-    parser.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    parser.add_argument("--workload", choices=sorted(WORKLOADS), default=None)
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--skip-cpu-baseline", action="store_true")
     parser.add_argument("--profile", action="store_true",
                         help="eager ticks only, for ncu captures (prints no bench line)")
     args = parser.parse_args()
+    explicit_workload = args.workload is not None
+    if args.workload is None:
+        args.workload = DEFAULT_WORKLOAD
     if args.profile:
         run_profile(args, args.workload)
         return
@@ -338,12 +452,12 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference(args, args.workload)))
+            print(json.dumps(run_reference(args, args.workload, explicit_workload,
+                                           max(world, args.gpus))))
         return
     if world > 1 or args.gpus > 1:
-        from neurosim_gpu_b200.sharded import bench_sharded
-        result = bench_sharded(args, WORKLOADS[args.workload], args.workload)
-        if result is not None and rank == 0:
+        result = run_sharded(args, explicit_workload)
+        if rank == 0:
             print(json.dumps(result))
         return
     print(json.dumps(run_native(args, args.workload)))

@@ -216,6 +216,7 @@ NSB_API int nsb_dendritic_event_noalloc(const nsb_tick* tick, float* current,
 typedef struct nsb_tiled_layout {
   int32_t ctas, blocks, block_cols, buffers, max_rows, format;
   int64_t n_tasks, n_slots, n_block_scales;
+  int64_t cols;                /* length of the gathered source vector      */
   const int32_t* row_begin;    /* [ctas+1]            */
   const int32_t* task_ptr;     /* [ctas*blocks+1]     */
   const int32_t* task_offset;  /* [n_tasks]           */
@@ -232,11 +233,23 @@ typedef struct nsb_tiled_layout {
 NSB_API size_t nsb_tiled_smem_bytes(int32_t block_cols, int32_t max_rows, int32_t buffers);
 
 /* Matrix tick for B = 1 over a tiled layout (same update as nsb_dendritic_step).
- * The state must be contiguous (neuron_stride 1) and 16-byte aligned.  `status`
- * (device int, may be NULL) receives a nonzero code if an internal pipeline
- * wait timed out; it is never cleared by the library. */
+ * `source` is the gathered state vector of layout->cols floats, contiguous and
+ * 16-byte aligned; NULL means the tick's own state (then tick->neurons ==
+ * layout->cols and the state must be contiguous and aligned).  With a separate
+ * source, tick->neurons rows are updated (a rank's rows of a sharded graph).
+ * `status` (device int, may be NULL) receives a nonzero code if an internal
+ * pipeline wait timed out; it is never cleared by the library. */
 NSB_API int nsb_dendritic_step_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
-                                     const nsb_tick_out* out, int* status, void* stream);
+                                     const float* source, const nsb_tick_out* out, int* status,
+                                     void* stream);
+
+/* Matrix tick of a block of destination rows (any B): the CSR holds those rows
+ * (rowptr rebased to 0, col indexing the full source), `source` is the full
+ * gathered state [B, n_cols] and the tick's operands are the rows' own.  Used
+ * by row-sharded multi-GPU runs; nsb_dendritic_step is the case source = state. */
+NSB_API int nsb_dendritic_step_rows(const nsb_tick* tick, const nsb_csr* csr,
+                                    const nsb_view* source, int64_t n_cols, int32_t width,
+                                    const nsb_tick_out* out, void* stream);
 
 /* result[n] = sum of w[e] * source[col[e]] over the tiled layout (B = 1). */
 NSB_API int nsb_tiled_propagate(int64_t neurons, const nsb_tiled_layout* layout,

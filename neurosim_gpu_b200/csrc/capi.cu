@@ -127,6 +127,26 @@ int nsb_dendritic_step(const nsb_tick* tick, const nsb_csr* csr, int32_t width,
   return NSB_OK;
 }
 
+int nsb_dendritic_step_rows(const nsb_tick* tick, const nsb_csr* csr, const nsb_view* source,
+                            int64_t n_cols, int32_t width, const nsb_tick_out* out, void* stream) {
+  nsb::TickArgs t;
+  nsb::Csr c;
+  if (!check_tick(tick, &t) || !check_csr(csr, &c) || !check_width(width)) return NSB_ERR_ARGUMENT;
+  if (!source || (t.batch > 0 && !source->data) || n_cols <= 0)
+    return fail(NSB_ERR_ARGUMENT, "the gathered source [B, n_cols] is required");
+  if (!out) return fail(NSB_ERR_ARGUMENT, "outputs are required");
+  if (t.batch > 0 && (!check_out(out->state, "state") || !check_out(out->dendrite, "dendrite") ||
+                      !check_out(out->adaptation, "adaptation")))
+    return NSB_ERR_ARGUMENT;
+  g_error.clear();
+  if (t.batch == 0) return NSB_OK;
+  const nsb::TickOut o{to_out(out->state), to_out(out->dendrite), to_out(out->adaptation)};
+  const cudaError_t err = nsb::launch_csr(t, to_view(*source), c, width, true, o,
+                                          nsb::Out{nullptr, 0, 0}, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_step_rows launch");
+  return NSB_OK;
+}
+
 int nsb_csr_propagate(int64_t batch, int64_t neurons, const nsb_csr* csr,
                       const nsb_view* source, const nsb_out* result, void* stream) {
   nsb::Csr c;
@@ -153,11 +173,11 @@ size_t nsb_tiled_smem_bytes(int32_t block_cols, int32_t max_rows, int32_t buffer
 
 namespace {
 
-bool check_tiled(const nsb_tiled_layout* L, int64_t neurons) {
+bool check_tiled(const nsb_tiled_layout* L) {
   if (!L) return fail(NSB_ERR_ARGUMENT, "tiled layout is required"), false;
   if (L->ctas <= 0 || L->blocks <= 0 || L->block_cols <= 0 || L->block_cols % 4 != 0 ||
       (L->buffers != 1 && L->buffers != 2) || L->max_rows < 0 || L->n_tasks < 0 ||
-      L->n_slots < 0 || static_cast<int64_t>(L->blocks) * L->block_cols < neurons)
+      L->n_slots < 0 || L->cols <= 0 || static_cast<int64_t>(L->blocks) * L->block_cols < L->cols)
     return fail(NSB_ERR_ARGUMENT, "invalid tiled layout geometry"), false;
   if (!L->row_begin || !L->task_ptr || (L->n_tasks > 0 && (!L->task_offset || !L->task_len ||
                                                           !L->task_rows)) ||
@@ -191,20 +211,26 @@ bool check_tiled(const nsb_tiled_layout* L, int64_t neurons) {
 }  // namespace
 
 int nsb_dendritic_step_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
-                             const nsb_tick_out* out, int* status, void* stream) {
+                             const float* source, const nsb_tick_out* out, int* status,
+                             void* stream) {
   nsb::TickArgs t;
   if (!check_tick(tick, &t)) return NSB_ERR_ARGUMENT;
   if (t.batch != 1) return fail(NSB_ERR_ARGUMENT, "the tiled tick takes B = 1");
-  if (t.s.sn != 1 || reinterpret_cast<uintptr_t>(t.s.data) % 16 != 0)
+  if (!source) {
+    if (t.s.sn != 1)
+      return fail(NSB_ERR_ARGUMENT, "the tiled tick needs a contiguous, 16-byte aligned state");
+    source = t.s.data;
+  }
+  if (reinterpret_cast<uintptr_t>(source) % 16 != 0)
     return fail(NSB_ERR_ARGUMENT, "the tiled tick needs a contiguous, 16-byte aligned state");
   if (!out || !check_out(out->state, "state") || !check_out(out->dendrite, "dendrite") ||
       !check_out(out->adaptation, "adaptation"))
     return NSB_ERR_ARGUMENT;
-  if (!check_tiled(layout, t.neurons)) return g_error.rfind("shared memory query", 0) == 0
-                                                  ? NSB_ERR_CUDA : NSB_ERR_ARGUMENT;
+  if (!check_tiled(layout)) return g_error.rfind("shared memory query", 0) == 0
+                                       ? NSB_ERR_CUDA : NSB_ERR_ARGUMENT;
   g_error.clear();
   const nsb::TickOut o{to_out(out->state), to_out(out->dendrite), to_out(out->adaptation)};
-  const cudaError_t err = nsb::launch_tiled(*layout, t, t.s.data, true, o, nsb::Out{nullptr, 0, 0},
+  const cudaError_t err = nsb::launch_tiled(*layout, t, source, true, o, nsb::Out{nullptr, 0, 0},
                                             status, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_step_tiled launch");
   return NSB_OK;
@@ -216,7 +242,8 @@ int nsb_tiled_propagate(int64_t neurons, const nsb_tiled_layout* layout, const f
   if (!source || !result) return fail(NSB_ERR_ARGUMENT, "source and result arrays are required");
   if (reinterpret_cast<uintptr_t>(source) % 16 != 0)
     return fail(NSB_ERR_ARGUMENT, "the tiled product needs a 16-byte aligned source");
-  if (!check_tiled(layout, neurons)) return NSB_ERR_ARGUMENT;
+  if (!check_tiled(layout)) return NSB_ERR_ARGUMENT;
+  if (layout->cols != neurons) return fail(NSB_ERR_ARGUMENT, "layout and source sizes differ");
   g_error.clear();
   nsb::TickArgs t{};
   t.batch = 1;

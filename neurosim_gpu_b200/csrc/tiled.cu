@@ -167,6 +167,7 @@ struct TiledArgs {
   int32_t block_cols;          // CB
   int32_t buffers;             // NBUF (1 or 2)
   int32_t max_rows;            // rows of the largest CTA range
+  int64_t cols;                // length of the gathered source vector
 };
 
 template <typename W>
@@ -254,7 +255,7 @@ tiled_tick_kernel(TiledArgs L, W w, TickArgs t, const float* __restrict__ x, Tic
         if (k >= nbuf && !mbar_wait(empty + b, (use - 1) & 1)) atomicExch(st, 1);
         fence_proxy_async_smem();
         const int first = k * L.block_cols;
-        const int count = min(L.block_cols, static_cast<int>(t.neurons) - first);
+        const int count = min(static_cast<int64_t>(L.block_cols), L.cols - first);
         const int bulk = count & ~3;  // 16-byte multiple, rest by plain stores
         float* dst = sbuf + b * cb_pad;
         for (int i = bulk; i < count; ++i) dst[i] = __ldg(x + first + i);
@@ -374,6 +375,7 @@ cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, cons
   L.block_cols = layout.block_cols;
   L.buffers = layout.buffers;
   L.max_rows = layout.max_rows;
+  L.cols = layout.cols;
   const int ctas = layout.ctas;
   switch (layout.format) {
     case NSB_WEIGHT_F16:

@@ -78,7 +78,7 @@ class _TiledLayout(ctypes.Structure):
                 ("block_cols", ctypes.c_int32), ("buffers", ctypes.c_int32),
                 ("max_rows", ctypes.c_int32), ("format", ctypes.c_int32),
                 ("n_tasks", ctypes.c_int64), ("n_slots", ctypes.c_int64),
-                ("n_block_scales", ctypes.c_int64),
+                ("n_block_scales", ctypes.c_int64), ("cols", ctypes.c_int64),
                 ("row_begin", ctypes.c_void_p), ("task_ptr", ctypes.c_void_p),
                 ("task_offset", ctypes.c_void_p), ("task_len", ctypes.c_void_p),
                 ("task_rows", ctypes.c_void_p), ("task_orig", ctypes.c_void_p),
@@ -97,7 +97,8 @@ class EventCounters(ctypes.Structure):
 EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_dendritic_event_workspace_size", "nsb_dendritic_event",
                     "nsb_tiled_smem_bytes", "nsb_dendritic_step_tiled", "nsb_tiled_propagate",
-                    "nsb_dendritic_event_noalloc", "nsb_last_error", "nsb_abi_version")
+                    "nsb_dendritic_event_noalloc", "nsb_dendritic_step_rows",
+                    "nsb_last_error", "nsb_abi_version")
 
 
 @functools.lru_cache(maxsize=1)
@@ -120,8 +121,10 @@ def load_library() -> ctypes.CDLL:
                                         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.nsb_tiled_smem_bytes.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
     lib.nsb_tiled_smem_bytes.restype = ctypes.c_size_t
-    lib.nsb_dendritic_step_tiled.argtypes = [p(_Tick), p(_TiledLayout), p(_TickOut),
-                                             ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_dendritic_step_tiled.argtypes = [p(_Tick), p(_TiledLayout), ctypes.c_void_p,
+                                             p(_TickOut), ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_dendritic_step_rows.argtypes = [p(_Tick), p(_Csr), p(_View), ctypes.c_int64,
+                                            ctypes.c_int32, p(_TickOut), ctypes.c_void_p]
     lib.nsb_tiled_propagate.argtypes = [ctypes.c_int64, p(_TiledLayout), ctypes.c_void_p,
                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_dendritic_event_noalloc.argtypes = [p(_Tick), ctypes.c_void_p, p(_View),
@@ -295,11 +298,18 @@ class DendriticExtension:
         return launch
 
     def prepare_step_tiled(self, state, dendrite, adaptation, params, layout, input,
-                           input_scalar, dendritic_input, dendritic_scalar, *, out, status=None):
-        """Like :meth:`prepare_step` for B = 1 over a :class:`~neurosim_gpu_b200.tiled.TiledLayout`."""
+                           input_scalar, dendritic_input, dendritic_scalar, *, out, status=None,
+                           source=None):
+        """Like :meth:`prepare_step` for B = 1 over a :class:`~neurosim_gpu_b200.tiled.TiledLayout`.
+
+        ``source`` (optional) is the full gathered state of ``layout.cols``
+        floats when ``state`` holds only this layout's rows (row sharding).
+        """
         _check_state(state)
         _check(state.size(0) == 1, "the tiled tick takes B = 1")
-        _check(state.stride(1) == 1 and state.data_ptr() % 16 == 0,
+        gather = state if source is None else source
+        _check(gather.is_cuda and gather.dtype == torch.float32 and gather.is_contiguous()
+               and gather.data_ptr() % 16 == 0 and gather.numel() == layout.cols,
                "the tiled tick needs a contiguous, 16-byte aligned state")
         _check(layout.neurons == state.size(1), "layout and state neuron counts differ")
         tick = _tick(state, dendrite, adaptation, params, input, input_scalar,
@@ -310,15 +320,53 @@ class DendriticExtension:
         result = _TickOut(_out(out[0]), _out(out[1]), _out(out[2]))
         c_layout = layout.c_struct()
         status_ptr = status.data_ptr() if status is not None else None
+        source_ptr = source.data_ptr() if source is not None else None
         lib, device = self.lib, state.device
-        keep = (state, dendrite, adaptation, params, layout, input, dendritic_input, out, status)
+        keep = (state, dendrite, adaptation, params, layout, input, dendritic_input, out, status,
+                source)
 
         def launch() -> None:
             assert keep is not None
             with torch.cuda.device(device):
                 code = lib.nsb_dendritic_step_tiled(ctypes.byref(tick), ctypes.byref(c_layout),
-                                                    ctypes.byref(result), status_ptr,
+                                                    source_ptr, ctypes.byref(result), status_ptr,
                                                     _stream(device))
+            _raise_on_status(lib, code)
+
+        return launch
+
+    def prepare_step_rows(self, state, dendrite, adaptation, params, rowptr, source_col, weight,
+                          input, input_scalar, dendritic_input, dendritic_scalar, width,
+                          block_scales=None, global_scale=None, *, source, out):
+        """A launch callable for a block of rows against the full gathered ``source``.
+
+        ``state`` / ``dendrite`` / ``adaptation`` / drives / params are the rows'
+        own ([B, rows]); the CSR holds those rows with columns indexing
+        ``source`` ([B, n_cols]); ``out`` receives the rows' new states.
+        """
+        _check_state(state)
+        tick = _tick(state, dendrite, adaptation, params, input, input_scalar,
+                     dendritic_input, dendritic_scalar)
+        _check(source.is_cuda and source.device == state.device and source.dtype == torch.float32
+               and source.dim() == 2 and source.size(0) == state.size(0),
+               "the gathered source must be a [B, n_cols] float32 tensor on the state device")
+        csr = csr_arguments(rowptr, source_col, weight, block_scales, global_scale, state)
+        _check(width in (4, 8, 16, 32), "width must be 4, 8, 16 or 32")
+        for view in out:
+            _float_on(view, state)
+            _check(view.shape == state.shape, "output shape mismatch")
+        result = _TickOut(_out(out[0]), _out(out[1]), _out(out[2]))
+        src = _View(source.data_ptr(), source.stride(0), source.stride(1), 0.0)
+        lib, device, lanes, cols = self.lib, state.device, int(width), source.size(1)
+        keep = (state, dendrite, adaptation, params, rowptr, source_col, weight, input,
+                dendritic_input, block_scales, global_scale, out, source)
+
+        def launch() -> None:
+            assert keep is not None
+            with torch.cuda.device(device):
+                code = lib.nsb_dendritic_step_rows(ctypes.byref(tick), ctypes.byref(csr),
+                                                   ctypes.byref(src), cols, lanes,
+                                                   ctypes.byref(result), _stream(device))
             _raise_on_status(lib, code)
 
         return launch
@@ -334,7 +382,8 @@ class DendriticExtension:
     def tiled_propagate(self, layout, x, status=None):
         """j = W @ x for x [1,N] over a tiled layout; a fresh [1,N] tensor."""
         _check_state(x)
-        _check(x.size(0) == 1 and x.stride(1) == 1 and x.data_ptr() % 16 == 0,
+        _check(x.size(0) == 1 and x.stride(1) == 1 and x.data_ptr() % 16 == 0
+               and layout.cols == layout.neurons == x.size(1),
                "the tiled product needs a contiguous, 16-byte aligned [1,N] source")
         result = torch.empty_like(x, memory_format=torch.contiguous_format)
         c_layout = layout.c_struct()

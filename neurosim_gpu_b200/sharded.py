@@ -1,0 +1,319 @@
+"""Row-sharded matrix tick across the GPUs of one node (one process per GPU).
+
+Destination rows are cut into ``world`` equal ranges: rank r owns rows
+``[r*R, min(N, (r+1)*R))`` with ``R = ceil(N / world)``.  Every tick each rank
+
+1. runs the native tick on its own rows, gathering from the full soma vector
+   ``x`` (all N neurons, laid out ``[world*R, B]`` so neuron n sits at row n on
+   every rank) and writing its new soma values straight into its own slice of
+   the next buffer;
+2. all-gathers the slices in place over NCCL (``all_gather_into_tensor``,
+   ``N*B*4`` bytes per tick), so every rank holds the next full soma vector.
+
+Per-row sums are the same as on one GPU with the same kernel, so sharded
+states are bit-identical to the single-GPU runtime's.  Each rank keeps its own
+dendrite / adaptation slices and parameter views.  ``run`` captures ticks and
+collectives together in one CUDA graph.
+
+The partition and exchange logic lives in :class:`RowShard`, which runs on any
+device and backend (the CPU tests drive it over gloo with the oracle tick).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from . import native as _native
+from . import tiled as _tiled
+from .dynamics import DendriticDynamics
+from .precision import encode_sparse_weights
+
+
+@dataclass
+class RowShard:
+    """Rows of one rank and the double-buffered full soma vector."""
+
+    neurons: int
+    batch: int
+    rank: int
+    world: int
+    device: torch.device
+
+    def __post_init__(self) -> None:
+        self.rows_per_rank = math.ceil(self.neurons / self.world)
+        self.lo = min(self.neurons, self.rank * self.rows_per_rank)
+        self.hi = min(self.neurons, self.lo + self.rows_per_rank)
+        self.cols = self.world * self.rows_per_rank
+        shape = (self.cols, self.batch)
+        self.buffers = [torch.zeros(shape, device=self.device) for _ in range(2)]
+        self.current = 0
+
+    @property
+    def rows(self) -> int:
+        return self.hi - self.lo
+
+    def load(self, full_state: torch.Tensor) -> None:
+        """Set the soma vector from a full [B, N] state."""
+        self.buffers[self.current][: self.neurons].copy_(full_state.T)
+
+    def source(self, index: int | None = None) -> torch.Tensor:
+        """The full gathered soma vector [B, cols] (strides (1, B))."""
+        return self.buffers[self.current if index is None else index].t()
+
+    def own(self, index: int) -> torch.Tensor:
+        """This rank's rows of buffer ``index`` as a [B, rows] view."""
+        return self.buffers[index][self.lo: self.hi].t()
+
+    def exchange(self, index: int, group=None) -> None:
+        """All-gather every rank's slice of buffer ``index`` in place."""
+        flat = self.buffers[index].view(-1)
+        chunk = self.rows_per_rank * self.batch
+        dist.all_gather_into_tensor(flat, flat[self.rank * chunk: (self.rank + 1) * chunk],
+                                    group=group)
+
+    def state(self) -> torch.Tensor:
+        """The full soma state [B, N] (a view of the current buffer)."""
+        return self.source()[:, : self.neurons]
+
+    def local(self, value):
+        """A drive (scalar or broadcastable to [B, N]) restricted to this rank's rows."""
+        if not isinstance(value, torch.Tensor):
+            return value
+        return value.expand(self.batch, self.neurons)[:, self.lo: self.hi]
+
+
+def _unpack_nibbles(packed: torch.Tensor, count: int) -> torch.Tensor:
+    return torch.stack((packed & 15, packed >> 4), dim=1).flatten()[:count]
+
+
+def _pack_nibbles(codes: torch.Tensor) -> torch.Tensor:
+    if codes.numel() % 2:
+        codes = torch.cat([codes, codes.new_zeros(1)])
+    return (codes[0::2] | (codes[1::2] << 4)).contiguous()
+
+
+class ShardedDendriticMatrixRuntime:
+    """The matrix tick of one graph, rows split over the ranks of ``group``.
+
+    ``graph`` is a :class:`~neurosim_gpu_b200.topology.SparseTopology` or a tuple
+    ``(in_rowptr, in_col, in_weight)`` of the full destination CSR on this
+    rank's device; ``dynamics`` and ``initial_state`` ([B, N]) are the full ones.
+    ``state`` is the full soma state on every rank; ``dendritic_state`` and
+    ``adaptation_state`` are this rank's rows.
+    """
+
+    def __init__(self, graph, dynamics: DendriticDynamics, initial_state: torch.Tensor, *,
+                 group=None, precision: str = "fp32", kernel: str = "auto",
+                 threads_per_row: int | None = None, extension=None,
+                 rank: int | None = None, world: int | None = None) -> None:
+        if isinstance(graph, tuple):
+            in_rowptr, in_col, in_weight = graph
+        else:
+            in_rowptr, in_col, in_weight = graph.in_rowptr, graph.in_col, graph.in_weight
+        if initial_state.device.type != "cuda" or initial_state.dtype != torch.float32:
+            raise ValueError("native compartment runtime requires CUDA float32")
+        if kernel not in ("auto", "csr", "tiled"):
+            raise ValueError("kernel must be 'auto', 'csr' or 'tiled'")
+        self.group = group
+        # rank / world may be given explicitly to build one rank's share without a
+        # process group (the exchange is then up to the caller).
+        self.rank = dist.get_rank(group) if rank is None else rank
+        self.world = dist.get_world_size(group) if world is None else world
+        device = initial_state.device
+        batch, neurons = initial_state.shape
+        self.neurons, self.batch = neurons, batch
+        self.extension = extension if extension is not None else _native.load_native_extension()
+        self.shard = RowShard(neurons, batch, self.rank, self.world, device)
+        lo, hi = self.shard.lo, self.shard.hi
+        self.compartment_dynamics = dynamics
+        self.params = [p[lo:hi] for p in dynamics.parameters()]
+        self.shard.load(initial_state)
+        self.dendritic_state = torch.zeros(batch, hi - lo, device=device)
+        self.adaptation_state = torch.zeros(batch, hi - lo, device=device)
+        self.precision = precision
+        self.status = _tiled.status_word(device)
+        self._graphs: dict = {}
+        self._tick = 0
+
+        rowptr = in_rowptr.to(torch.int64)
+        e0, e1 = int(rowptr[lo]), int(rowptr[hi])
+        self.n_edges = int(rowptr[-1])
+        self.local_edges = e1 - e0
+        # Weights in the storage format, encoded over the WHOLE graph (global scales).
+        if precision == "fp32":
+            full, scales, scale = in_weight.detach(), None, None
+        elif precision == "fp16":
+            full, scales, scale = in_weight.detach().half(), None, None
+        else:
+            full, scales, scale = encode_sparse_weights(in_weight.detach(), precision)
+        self.layout = None
+        if batch == 1 and kernel != "csr" and self.local_edges > 0:
+            if precision == "nvfp4":
+                local = _pack_nibbles(_unpack_nibbles(full, self.n_edges)[e0:e1])
+            else:
+                local = full[e0:e1]
+            self.layout = _tiled.build_tiled_layout(
+                (rowptr[lo: hi + 1] - e0).to(torch.int32), in_col[e0:e1].contiguous(),
+                local.contiguous(), neurons=hi - lo, cols=self.shard.cols,
+                ctas=_tiled.sm_count(device), smem_limit=_tiled.smem_limit(device),
+                block_scales=scales, global_scale=scale, scale_offset=e0)
+        # Row-block CSR for the general kernel: the rows' offsets into the full arrays.
+        self.csr = (in_rowptr[lo: hi + 1].contiguous(), in_col, full, scales, scale)
+        degree = self.n_edges / max(neurons, 1)
+        self.threads_per_row = threads_per_row or (8 if degree <= 16 else 16 if degree <= 48
+                                                   else 32)
+
+    @property
+    def kernel_path(self) -> str:
+        return "tiled" if self.layout is not None else "csr"
+
+    @property
+    def state(self) -> torch.Tensor:
+        return self.shard.state()
+
+    def check_status(self) -> None:
+        code = int(self.status.item())
+        if code:
+            raise RuntimeError(f"tiled tick pipeline timeout (code {code})")
+
+    def _prepare(self, src: int, dst: int, d, a, u, us, v, vs, out_d, out_a):
+        shard = self.shard
+        s_rows = shard.own(src)
+        out = (shard.own(dst), out_d, out_a)
+        if self.layout is not None:
+            return self.extension.prepare_step_tiled(
+                s_rows, d, a, self.params, self.layout, u, us, v, vs, out=out,
+                status=self.status, source=shard.buffers[src].view(-1))
+        rowptr, col, weight, scales, scale = self.csr
+        return self.extension.prepare_step_rows(
+            s_rows, d, a, self.params, rowptr, col, weight, u, us, v, vs, self.threads_per_row,
+            scales, scale, source=shard.source(src), out=out)
+
+    def _drives(self, drive, dendritic_drive):
+        def split(value):
+            value = self.shard.local(value)
+            return (None, float(value)) if not isinstance(value, torch.Tensor) else (value, 0.0)
+        return split(drive) + split(dendritic_drive)
+
+    def local_step(self, drive=0.0, *, dendritic_drive=0.0) -> int:
+        """The kernel half of a tick: this rank's rows into the next buffer.
+
+        Returns the index of the buffer written; :meth:`finish` adopts it after
+        the exchange.
+        """
+        u, us, v, vs = self._drives(drive, dendritic_drive)
+        src = self.shard.current
+        dst = 1 - src
+        out_d = torch.empty_like(self.dendritic_state)
+        out_a = torch.empty_like(self.adaptation_state)
+        self._prepare(src, dst, self.dendritic_state, self.adaptation_state, u, us, v, vs,
+                      out_d, out_a)()
+        self.dendritic_state, self.adaptation_state = out_d, out_a
+        return dst
+
+    def finish(self, dst: int) -> None:
+        self.shard.current = dst
+        self._tick += 1
+
+    def step(self, drive=0.0, *, dendritic_drive=0.0) -> torch.Tensor:
+        """One tick on every rank (all ranks must call it); returns the full state."""
+        dst = self.local_step(drive, dendritic_drive=dendritic_drive)
+        self.shard.exchange(dst, self.group)
+        self.finish(dst)
+        return self.state
+
+    def run(self, ticks: int, drive=0.0, *, dendritic_drive=0.0, graph_ticks: int = 32
+            ) -> torch.Tensor:
+        """``ticks`` ticks with fixed drives, replaying a CUDA graph of ticks + all-gathers."""
+        graph_ticks = max(2, min(graph_ticks, ticks) // 2 * 2)
+        if ticks < graph_ticks:
+            for _ in range(ticks):
+                self.step(drive, dendritic_drive=dendritic_drive)
+            return self.state
+        key = (graph_ticks, repr(drive), repr(dendritic_drive))
+        entry = self._graphs.get(key)
+        if entry is None:
+            self._graphs = {}
+            entry = self._graphs[key] = self._capture(graph_ticks, drive, dendritic_drive)
+        graph, (d0, a0), final = entry
+        d0.copy_(self.dendritic_state)
+        a0.copy_(self.adaptation_state)
+        if self.shard.current != 0:
+            self.shard.buffers[0].copy_(self.shard.buffers[1])
+            self.shard.current = 0
+        for _ in range(ticks // graph_ticks):
+            graph.replay()
+        self.dendritic_state, self.adaptation_state = final[0].clone(), final[1].clone()
+        self._tick += ticks // graph_ticks * graph_ticks
+        for _ in range(ticks % graph_ticks):
+            self.step(drive, dendritic_drive=dendritic_drive)
+        return self.state
+
+    def _capture(self, ticks: int, drive, dendritic_drive):
+        u, us, v, vs = self._drives(drive, dendritic_drive)
+        d_buf = [torch.empty_like(self.dendritic_state) for _ in range(2)]
+        a_buf = [torch.empty_like(self.adaptation_state) for _ in range(2)]
+        calls = []
+        for k in range(ticks):
+            src, dst = k % 2, (k + 1) % 2
+            calls.append((self._prepare(src, dst, d_buf[src], a_buf[src], u, us, v, vs,
+                                        d_buf[dst], a_buf[dst]), dst))
+        saved = [b.clone() for b in self.shard.buffers]
+        stream = torch.cuda.Stream(device=self.shard.device)
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):  # warm-up of the exact calls, outside capture
+            for call, dst in calls[:2]:
+                call()
+                self.shard.exchange(dst, self.group)
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        for buffer, value in zip(self.shard.buffers, saved):  # the warm-up must not advance
+            buffer.copy_(value)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for call, dst in calls:
+                call()
+                self.shard.exchange(dst, self.group)
+        return graph, (d_buf[0], a_buf[0]), (d_buf[0], a_buf[0])
+
+    def release_graphs(self) -> None:
+        """Drop captured graphs (do this before destroying the process group)."""
+        self._graphs = {}
+
+    def gather(self, name: str) -> torch.Tensor:
+        """The full [B, N] dendrite or adaptation state (an all-gather)."""
+        local = getattr(self, name)
+        padded = torch.zeros(self.batch, self.shard.rows_per_rank, device=local.device)
+        padded[:, : local.shape[1]] = local
+        parts = [torch.empty_like(padded) for _ in range(self.world)]
+        dist.all_gather(parts, padded.contiguous(), group=self.group)
+        return torch.cat(parts, dim=1)[:, : self.neurons]
+
+
+def broadcast_graph(neurons: int, edges: int, *, seed: int, device: torch.device, group=None):
+    """Rank 0 builds ``random_topology`` (the reference stream) and broadcasts its CSR.
+
+    Returns ``(in_rowptr, in_col, in_weight)`` on ``device`` on every rank.
+    """
+    from .topology import random_topology
+
+    rank = dist.get_rank(group)
+    if rank == 0:
+        graph = random_topology(neurons, edges, device="cpu", seed=seed, build_device=device)
+        arrays = [graph.in_rowptr, graph.in_col, graph.in_weight]
+        count = torch.tensor([graph.n_edges], device=device, dtype=torch.int64)
+    else:
+        count = torch.zeros(1, device=device, dtype=torch.int64)
+    dist.broadcast(count, 0, group=group)
+    m = int(count.item())
+    if rank != 0:
+        arrays = [torch.empty(neurons + 1, dtype=torch.int32, device=device),
+                  torch.empty(m, dtype=torch.int32, device=device),
+                  torch.empty(m, dtype=torch.float32, device=device)]
+    for array in arrays:
+        dist.broadcast(array, 0, group=group)
+    return tuple(arrays)

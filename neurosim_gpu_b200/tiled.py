@@ -37,7 +37,7 @@ MAX_CTA_ROWS = 32767  # row ids are int16 inside a CTA
 
 @dataclass
 class TiledLayout:
-    neurons: int
+    neurons: int          # destination rows of this layout
     n_edges: int
     ctas: int
     blocks: int
@@ -55,6 +55,11 @@ class TiledLayout:
     weight: torch.Tensor
     block_scales: torch.Tensor | None
     global_scale: torch.Tensor | None
+    cols: int = 0         # length of the gathered source vector (0: same as neurons)
+
+    def __post_init__(self) -> None:
+        if self.cols == 0:
+            self.cols = self.neurons
 
     @property
     def n_tasks(self) -> int:
@@ -82,7 +87,7 @@ class TiledLayout:
         return native._TiledLayout(
             self.ctas, self.blocks, self.block_cols, self.buffers, self.max_rows, self.format,
             self.n_tasks, self.n_slots,
-            self.block_scales.numel() if self.block_scales is not None else 0,
+            self.block_scales.numel() if self.block_scales is not None else 0, self.cols,
             ptr(self.row_begin), ptr(self.task_ptr), ptr(self.task_offset), ptr(self.task_len),
             ptr(self.task_rows), ptr(self.task_orig), ptr(self.col), ptr(self.weight),
             ptr(self.block_scales), ptr(self.global_scale))
@@ -116,14 +121,23 @@ def cta_row_ranges(rowptr: torch.Tensor, ctas: int) -> torch.Tensor:
 
 def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: torch.Tensor,
                        *, neurons: int, ctas: int, smem_limit: int, block_scales=None,
-                       global_scale=None, smem_bytes=None) -> TiledLayout:
-    """Build the tiled layout of one graph.  ``weight`` is the CSR value array in
-    its storage format (float32 / float16 / uint8 E4M3 codes / uint8 packed NVFP4)."""
+                       global_scale=None, smem_bytes=None, cols: int | None = None,
+                       scale_offset: int = 0) -> TiledLayout:
+    """Build the tiled layout of one graph.
+
+    ``weight`` is the CSR value array in its storage format (float32 / float16 /
+    uint8 E4M3 codes / uint8 packed NVFP4).  ``neurons`` is the number of
+    destination rows (``in_rowptr`` has neurons + 1 entries, starting at 0);
+    ``cols`` is the length of the gathered source (default: ``neurons``).  For a
+    block of rows cut out of a larger NVFP4 CSR, ``scale_offset`` is the CSR
+    position of the block's first edge (it selects the original block scales).
+    """
     device = in_col.device
     if smem_bytes is None:
         lib = native.load_library()
         smem_bytes = lambda cols, rows, bufs: int(lib.nsb_tiled_smem_bytes(cols, rows, bufs))  # noqa: E731
     n, m = neurons, in_col.numel()
+    cols = n if cols is None else cols
     if block_scales is not None:
         fmt = native.NVFP4
     elif weight.dtype == torch.uint8:
@@ -138,7 +152,7 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
     max_rows = int(rows_per_cta.max())
     if max_rows > MAX_CTA_ROWS:
         raise ValueError("too many rows per CTA for the tiled layout")
-    blocks, block_cols, buffers = plan_blocks(n, max_rows, smem_limit, smem_bytes)
+    blocks, block_cols, buffers = plan_blocks(cols, max_rows, smem_limit, smem_bytes)
 
     degree = rowptr[1:] - rowptr[:-1]
     row_of_edge = torch.repeat_interleave(torch.arange(n, device=device), degree)
@@ -190,7 +204,7 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
         codes[slot] = nibbles
         tiled_weight = (codes[0::2] | (codes[1::2] << 4)).contiguous()
         task_orig = torch.zeros((n_tasks, LANES), dtype=torch.int32, device=device)
-        task_orig[pair_task, pair_lane] = piece_start.flatten()[order].to(torch.int32)
+        task_orig[pair_task, pair_lane] = (piece_start.flatten()[order] + scale_offset).to(torch.int32)
     else:
         tiled_weight = torch.zeros(slots, dtype=weight.dtype, device=device)
         tiled_weight[slot] = weight
@@ -199,7 +213,8 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
         max_rows=max_rows, format=fmt, row_begin=row_begin.to(torch.int32),
         task_ptr=task_ptr.to(torch.int32), task_offset=task_offset.to(torch.int32),
         task_len=task_len.to(torch.int32), task_rows=task_rows.contiguous(), task_orig=task_orig,
-        col=col, weight=tiled_weight, block_scales=block_scales, global_scale=global_scale)
+        col=col, weight=tiled_weight, block_scales=block_scales, global_scale=global_scale,
+        cols=cols)
 
 
 def emulate(layout: TiledLayout, source: torch.Tensor) -> torch.Tensor:
@@ -215,6 +230,7 @@ def emulate(layout: TiledLayout, source: torch.Tensor) -> torch.Tensor:
         (layout.task_ptr[1:] - layout.task_ptr[:-1]).long())
     cta = blocks_of_task // layout.blocks
     block = blocks_of_task % layout.blocks
+    out = torch.zeros(layout.neurons, dtype=torch.float64, device=x.device)
     padded = torch.cat([x, torch.zeros(layout.blocks * layout.block_cols + 1 - x.numel(),
                                        dtype=x.dtype, device=x.device)])
     for q in range(layout.n_tasks):
