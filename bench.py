@@ -409,10 +409,11 @@ def run_sharded(args, explicit_workload: bool) -> dict:
 
 
 def run_profile(args, workload: str) -> None:
-    """Eager ticks only (no graph, no copies, no CPU leg): the command ncu captures.
+    """Eager launches only (no graph, no copies, no CPU leg): the command ncu captures.
 
-    ``--warmup`` ticks run first, then ``--steps`` ticks; each tick is exactly one
-    launch of the tick kernel, so ``ncu -s <warmup> -c <n>`` selects ticks.
+    ``--warmup`` launches run first, then ``--steps`` launches; each launch is one
+    tick, or ``--launch-ticks`` ticks of the persistent tiled kernel, so
+    ``ncu -s <warmup> -c <n>`` selects launches.
     """
     neurons, edges, batch, precision = WORKLOADS[workload]
     device = torch.device("cuda", 0)
@@ -422,9 +423,13 @@ def run_profile(args, workload: str) -> None:
                                            precision=precision)
     with torch.inference_mode():
         runtime._weights()  # pack reduced-precision weights before the counted launches
+        runtime._tiled_layout()
         torch.cuda.synchronize()
         for _ in range(args.warmup + args.steps):
-            runtime.step(0.2, dendritic_drive=0.1)
+            if args.launch_ticks > 1:
+                runtime.run(args.launch_ticks, 0.2, dendritic_drive=0.1)
+            else:
+                runtime.step(0.2, dendritic_drive=0.1)
     torch.cuda.synchronize()
     print(json.dumps({"profile": workload, "ticks": args.warmup + args.steps,
                       "state_mean": float(runtime.state.mean())}))
@@ -440,7 +445,9 @@ def main() -> None:
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--skip-cpu-baseline", action="store_true")
     parser.add_argument("--profile", action="store_true",
-                        help="eager ticks only, for ncu captures (prints no bench line)")
+                        help="eager launches only, for ncu captures (prints no bench line)")
+    parser.add_argument("--launch-ticks", type=int, default=1,
+                        help="with --profile: ticks per launch of the persistent tiled kernel")
     args = parser.parse_args()
     explicit_workload = args.workload is not None
     if args.workload is None:

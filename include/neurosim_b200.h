@@ -45,7 +45,7 @@ extern "C" {
 #define NSB_API
 #endif
 
-#define NSB_ABI_VERSION 1
+#define NSB_ABI_VERSION 3
 
 enum nsb_status {
   NSB_OK = 0,
@@ -200,37 +200,56 @@ NSB_API int nsb_dendritic_event_noalloc(const nsb_tick* tick, float* current,
 
 /* Column-blocked layout of one graph for the B = 1 tick (built by the host,
  * see neurosim_gpu_b200/tiled.py; it re-arranges the destination CSR, the
- * arithmetic is that of nsb_dendritic_step).
- *  - CTA c (one per SM) owns destination rows [row_begin[c], row_begin[c+1]).
- *  - Columns are split into `blocks` blocks of `block_cols` columns; one block
- *    of the source state is staged in shared memory at a time (`buffers` = 1
- *    or 2 copies in flight).
- *  - Task q (tasks of CTA c and block k are task_ptr[c*blocks+k] ..
- *    task_ptr[c*blocks+k+1]-1) covers 32 rows: lane i owns row
- *    row_begin[c] + task_rows[32q+i] (-1: no row) and its edges with column in
- *    block k sit at slots task_offset[q] + 32j + i, j < task_len[q].
- *  - col[slot] is the column minus the block start; padding slots hold
- *    block_cols and weight 0.  NVFP4 codes are packed two per byte by slot;
- *    task_orig[32q+i] is the CSR position of the lane's first edge, which
- *    selects the original 16-edge block scale of each edge. */
+ * arithmetic is that of nsb_dendritic_step).  It has no counterpart in the
+ * reference: it is how this library stores the CSR it is given.
+ *  - The gathered columns (`cols` of them) are split into `blocks` blocks of
+ *    `block_cols` columns (a multiple of 32, <= 65504).  A stage is one block
+ *    and a range of destination rows; CTA c runs stages stage_ptr[c] ..
+ *    stage_ptr[c+1]-1 (block stage_block[s]) with `buffers` (1 or 2) state
+ *    blocks in shared memory.
+ *  - Tasks of CTA c are task_ptr[c] .. task_ptr[c+1]-1.  tasks[4q..4q+3] =
+ *    first slot, chunks C, stage (index among the CTA's stages), first scale
+ *    pair.  Lane i owns row task_rows[32q+i] & 0x0FFFFFFF (0x0FFFFFFF: no
+ *    row); its j-th edge in the stage's block sits at slot
+ *    first + 128*(j/4) + 4*i + j%4, j < 4C.
+ *  - col[slot] is the column minus the block start (uint16); padding slots
+ *    hold block_cols and weight 0.  n_slots is a multiple of 128.
+ *  - NVFP4: codes are packed two per byte by slot (even slot in the low
+ *    nibble).  If lane i's first edge is at CSR position o, its edge j takes
+ *    the E4M3 scale of CSR block (o + j) / 16; bits 28..31 of task_rows[32q+i]
+ *    hold o % 16, and scale_pairs[first scale pair + 32*b + i] holds the
+ *    scales of CSR blocks o/16 + b (low byte) and o/16 + b + 1 (high byte).
+ *  - Pointer alignment: tasks 16 B; col 8 B; weight 16 B (f32), 8 B (f16),
+ *    4 B (E4M3), 2 B (NVFP4).
+ *  - The kernels trust the layout's contents (offsets, lengths, rows): pass
+ *    layouts made by the builder.  `ctas` must not exceed the SM count: the
+ *    tick is a cooperative launch with one CTA per SM. */
 typedef struct nsb_tiled_layout {
-  int32_t ctas, blocks, block_cols, buffers, max_rows, format;
-  int64_t n_tasks, n_slots, n_block_scales;
+  int32_t ctas, blocks, block_cols, buffers, format, reserved;
+  int64_t n_stages, n_tasks, n_slots, n_scale_pairs;
+  int64_t rows;                /* destination rows                          */
   int64_t cols;                /* length of the gathered source vector      */
-  const int32_t* row_begin;    /* [ctas+1]            */
-  const int32_t* task_ptr;     /* [ctas*blocks+1]     */
-  const int32_t* task_offset;  /* [n_tasks]           */
-  const int32_t* task_len;     /* [n_tasks]           */
-  const int16_t* task_rows;    /* [n_tasks*32]        */
-  const int32_t* task_orig;    /* [n_tasks*32] (NVFP4) */
-  const int32_t* col;          /* [n_slots]           */
+  const int32_t* stage_ptr;    /* [ctas+1]            */
+  const int32_t* stage_block;  /* [n_stages]          */
+  const int32_t* task_ptr;     /* [ctas+1]            */
+  const int32_t* tasks;        /* [n_tasks*4]         */
+  const int32_t* task_rows;    /* [n_tasks*32]        */
+  const uint16_t* col;         /* [n_slots]           */
   const void* weight;          /* [n_slots] (NVFP4: [n_slots/2]) */
-  const uint8_t* block_scales; /* NVFP4: block scales of the original CSR */
+  const uint16_t* scale_pairs; /* NVFP4: [n_scale_pairs] */
   const float* global_scale;   /* E4M3 / NVFP4        */
 } nsb_tiled_layout;
 
 /* Dynamic shared memory one CTA of the tiled tick needs. */
-NSB_API size_t nsb_tiled_smem_bytes(int32_t block_cols, int32_t max_rows, int32_t buffers);
+NSB_API size_t nsb_tiled_smem_bytes(int32_t block_cols, int32_t buffers);
+
+/* Device workspace of the tiled calls, in bytes (256-byte aligned, caller-owned):
+ * a grid-barrier head and the per-block row sums.  It must be zero-filled
+ * before its first use; every call leaves it zero-filled again, so one
+ * workspace serves any number of calls on one stream.  After a call reported
+ * a timeout in `status`, zero-fill it again.  Calls that overlap on the GPU
+ * need separate workspaces. */
+NSB_API size_t nsb_tiled_workspace_size(const nsb_tiled_layout* layout);
 
 /* Matrix tick for B = 1 over a tiled layout (same update as nsb_dendritic_step).
  * `source` is the gathered state vector of layout->cols floats, contiguous and
@@ -238,10 +257,20 @@ NSB_API size_t nsb_tiled_smem_bytes(int32_t block_cols, int32_t max_rows, int32_
  * layout->cols and the state must be contiguous and aligned).  With a separate
  * source, tick->neurons rows are updated (a rank's rows of a sharded graph).
  * `status` (device int, may be NULL) receives a nonzero code if an internal
- * pipeline wait timed out; it is never cleared by the library. */
+ * wait timed out; it is never cleared by the library.  One cooperative launch. */
 NSB_API int nsb_dendritic_step_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
-                                     const float* source, const nsb_tick_out* out, int* status,
+                                     const float* source, const nsb_tick_out* out,
+                                     void* workspace, size_t workspace_bytes, int* status,
                                      void* stream);
+
+/* `ticks` (>= 1) matrix ticks with the same drives in ONE cooperative launch:
+ * the first tick reads tick->state / dendrite / adaptation and writes `out`,
+ * the later ones update `out` in place.  out->state must be contiguous and
+ * 16-byte aligned (it is the gathered source of the later ticks).  Equal to
+ * `ticks` calls of nsb_dendritic_step_tiled, bit for bit. */
+NSB_API int nsb_dendritic_run_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
+                                    int64_t ticks, const nsb_tick_out* out, void* workspace,
+                                    size_t workspace_bytes, int* status, void* stream);
 
 /* Matrix tick of a block of destination rows (any B): the CSR holds those rows
  * (rowptr rebased to 0, col indexing the full source), `source` is the full
@@ -253,7 +282,8 @@ NSB_API int nsb_dendritic_step_rows(const nsb_tick* tick, const nsb_csr* csr,
 
 /* result[n] = sum of w[e] * source[col[e]] over the tiled layout (B = 1). */
 NSB_API int nsb_tiled_propagate(int64_t neurons, const nsb_tiled_layout* layout,
-                                const float* source, float* result, int* status, void* stream);
+                                const float* source, float* result, void* workspace,
+                                size_t workspace_bytes, int* status, void* stream);
 
 /* Thread-local message of the last failing call ("" if none). */
 NSB_API const char* nsb_last_error(void);

@@ -166,90 +166,159 @@ int nsb_csr_propagate(int64_t batch, int64_t neurons, const nsb_csr* csr,
   return NSB_OK;
 }
 
-size_t nsb_tiled_smem_bytes(int32_t block_cols, int32_t max_rows, int32_t buffers) {
-  if (block_cols <= 0 || max_rows < 0 || buffers < 1 || buffers > 2) return 0;
-  return nsb::tiled_smem_bytes(block_cols, max_rows, buffers);
+size_t nsb_tiled_smem_bytes(int32_t block_cols, int32_t buffers) {
+  if (block_cols <= 0 || buffers < 1 || buffers > 2) return 0;
+  return nsb::tiled_smem_bytes(block_cols, buffers);
 }
 
 namespace {
 
+bool aligned(const void* p, uintptr_t bytes) {
+  return reinterpret_cast<uintptr_t>(p) % bytes == 0;
+}
+
 bool check_tiled(const nsb_tiled_layout* L) {
   if (!L) return fail(NSB_ERR_ARGUMENT, "tiled layout is required"), false;
-  if (L->ctas <= 0 || L->blocks <= 0 || L->block_cols <= 0 || L->block_cols % 4 != 0 ||
-      (L->buffers != 1 && L->buffers != 2) || L->max_rows < 0 || L->n_tasks < 0 ||
-      L->n_slots < 0 || L->cols <= 0 || static_cast<int64_t>(L->blocks) * L->block_cols < L->cols)
+  if (L->ctas <= 0 || L->blocks <= 0 || L->block_cols <= 0 || L->block_cols % 32 != 0 ||
+      L->block_cols > 65504 || (L->buffers != 1 && L->buffers != 2) || L->n_stages < 0 ||
+      L->n_stages >= (int64_t{1} << 24) || L->n_tasks < 0 || L->n_slots < 0 ||
+      L->n_slots % 128 != 0 || L->n_slots >= (int64_t{1} << 31) || L->rows <= 0 ||
+      L->rows >= (int64_t{1} << 28) - 1 || L->cols <= 0 ||
+      static_cast<int64_t>(L->blocks) * L->block_cols < L->cols ||
+      static_cast<int64_t>(L->blocks - 1) * L->block_cols >= L->cols)
     return fail(NSB_ERR_ARGUMENT, "invalid tiled layout geometry"), false;
-  if (!L->row_begin || !L->task_ptr || (L->n_tasks > 0 && (!L->task_offset || !L->task_len ||
-                                                          !L->task_rows)) ||
+  if (!L->stage_ptr || !L->task_ptr || (L->n_stages > 0 && !L->stage_block) ||
+      (L->n_tasks > 0 && (!L->tasks || !L->task_rows)) ||
       (L->n_slots > 0 && (!L->col || !L->weight)))
     return fail(NSB_ERR_ARGUMENT, "tiled layout arrays are required"), false;
+  static const uintptr_t weight_alignment[4] = {16, 8, 4, 2};
+  if (L->format < 0 || L->format > 3)
+    return fail(NSB_ERR_ARGUMENT, "unknown CSR weight format"), false;
+  if (!aligned(L->tasks, 16) || !aligned(L->col, 8) ||
+      !aligned(L->weight, weight_alignment[L->format]))
+    return fail(NSB_ERR_ARGUMENT, "tiled layout arrays are misaligned"), false;
   switch (L->format) {
-    case NSB_WEIGHT_F32:
-    case NSB_WEIGHT_F16:
-      break;
     case NSB_WEIGHT_E4M3:
       if (!L->global_scale) return fail(NSB_ERR_ARGUMENT, "quantized weights require a global scale"), false;
       break;
     case NSB_WEIGHT_NVFP4:
-      if (!L->global_scale || (L->n_tasks > 0 && (!L->task_orig || !L->block_scales)) ||
-          L->n_block_scales <= 0 || L->n_slots % 2 != 0)
+      if (!L->global_scale || (L->n_tasks > 0 && (!L->scale_pairs || L->n_scale_pairs <= 0)) ||
+          !aligned(L->scale_pairs, 2))
         return fail(NSB_ERR_ARGUMENT, "invalid NVFP4 tiled layout"), false;
       break;
     default:
-      return fail(NSB_ERR_ARGUMENT, "unknown CSR weight format"), false;
+      break;
   }
-  int device = 0, optin = 0;
+  int device = 0, optin = 0, sms = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err == cudaSuccess)
     err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
-  if (err != cudaSuccess) return cuda_fail(err, "shared memory query"), false;
-  if (nsb::tiled_smem_bytes(L->block_cols, L->max_rows, L->buffers) > static_cast<size_t>(optin))
+  if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (err != cudaSuccess) return cuda_fail(err, "device attribute query"), false;
+  if (nsb::tiled_smem_bytes(L->block_cols, L->buffers) > static_cast<size_t>(optin))
     return fail(NSB_ERR_ARGUMENT, "tiled layout needs more shared memory than a CTA can use"), false;
+  if (L->ctas > sms)
+    return fail(NSB_ERR_ARGUMENT, "tiled layout has more CTAs than the device has SMs"), false;
   return true;
 }
 
-}  // namespace
+int tiled_status(int code) {
+  return g_error.rfind("device attribute query", 0) == 0 ? NSB_ERR_CUDA : code;
+}
 
-int nsb_dendritic_step_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
-                             const float* source, const nsb_tick_out* out, int* status,
-                             void* stream) {
-  nsb::TickArgs t;
-  if (!check_tick(tick, &t)) return NSB_ERR_ARGUMENT;
-  if (t.batch != 1) return fail(NSB_ERR_ARGUMENT, "the tiled tick takes B = 1");
-  if (!source) {
-    if (t.s.sn != 1)
+bool check_workspace(const nsb_tiled_layout* layout, void* workspace, size_t bytes) {
+  if (!workspace || !aligned(workspace, 256) || bytes < nsb::tiled_workspace_bytes(*layout))
+    return fail(NSB_ERR_WORKSPACE, "tiled workspace missing, misaligned or too small"), false;
+  return true;
+}
+
+// Checks shared by the tiled tick entry points; fills t and o.
+int check_tiled_tick(const nsb_tick* tick, const nsb_tiled_layout* layout, const float** source,
+                     const nsb_tick_out* out, void* workspace, size_t workspace_bytes,
+                     nsb::TickArgs* t, nsb::TickOut* o) {
+  if (!check_tick(tick, t)) return NSB_ERR_ARGUMENT;
+  if (t->batch != 1) return fail(NSB_ERR_ARGUMENT, "the tiled tick takes B = 1");
+  if (!*source) {
+    if (t->s.sn != 1)
       return fail(NSB_ERR_ARGUMENT, "the tiled tick needs a contiguous, 16-byte aligned state");
-    source = t.s.data;
+    *source = t->s.data;
   }
-  if (reinterpret_cast<uintptr_t>(source) % 16 != 0)
+  if (!aligned(*source, 16))
     return fail(NSB_ERR_ARGUMENT, "the tiled tick needs a contiguous, 16-byte aligned state");
   if (!out || !check_out(out->state, "state") || !check_out(out->dendrite, "dendrite") ||
       !check_out(out->adaptation, "adaptation"))
     return NSB_ERR_ARGUMENT;
-  if (!check_tiled(layout)) return g_error.rfind("shared memory query", 0) == 0
-                                       ? NSB_ERR_CUDA : NSB_ERR_ARGUMENT;
+  if (!check_tiled(layout)) return tiled_status(NSB_ERR_ARGUMENT);
+  if (layout->rows != t->neurons)
+    return fail(NSB_ERR_ARGUMENT, "layout and state neuron counts differ");
+  if (!check_workspace(layout, workspace, workspace_bytes)) return NSB_ERR_WORKSPACE;
+  *o = nsb::TickOut{to_out(out->state), to_out(out->dendrite), to_out(out->adaptation)};
+  return NSB_OK;
+}
+
+}  // namespace
+
+size_t nsb_tiled_workspace_size(const nsb_tiled_layout* layout) {
+  if (!layout || layout->blocks <= 0 || layout->rows <= 0) return 0;
+  return nsb::tiled_workspace_bytes(*layout);
+}
+
+int nsb_dendritic_step_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
+                             const float* source, const nsb_tick_out* out, void* workspace,
+                             size_t workspace_bytes, int* status, void* stream) {
+  nsb::TickArgs t;
+  nsb::TickOut o;
+  const bool self_source = source == nullptr;
+  const int code = check_tiled_tick(tick, layout, &source, out, workspace, workspace_bytes, &t, &o);
+  if (code != NSB_OK) return code;
+  if (self_source && layout->cols != t.neurons)
+    return fail(NSB_ERR_ARGUMENT, "layout and state sizes differ");
   g_error.clear();
-  const nsb::TickOut o{to_out(out->state), to_out(out->dendrite), to_out(out->adaptation)};
-  const cudaError_t err = nsb::launch_tiled(*layout, t, source, true, o, nsb::Out{nullptr, 0, 0},
-                                            status, static_cast<cudaStream_t>(stream));
+  const cudaError_t err = nsb::launch_tiled(*layout, t, source, true, 1, o, nsb::Out{nullptr, 0, 0},
+                                            workspace, status, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_step_tiled launch");
   return NSB_OK;
 }
 
+int nsb_dendritic_run_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout, int64_t ticks,
+                            const nsb_tick_out* out, void* workspace, size_t workspace_bytes,
+                            int* status, void* stream) {
+  if (ticks < 1 || ticks > (int64_t{1} << 24))
+    return fail(NSB_ERR_ARGUMENT, "ticks must be in [1, 2^24]");
+  nsb::TickArgs t;
+  nsb::TickOut o;
+  const float* source = nullptr;
+  const int code = check_tiled_tick(tick, layout, &source, out, workspace, workspace_bytes, &t, &o);
+  if (code != NSB_OK) return code;
+  if (layout->cols != t.neurons)
+    return fail(NSB_ERR_ARGUMENT, "layout and state sizes differ");
+  if (ticks > 1 && (out->state.neuron_stride != 1 || !aligned(out->state.data, 16)))
+    return fail(NSB_ERR_ARGUMENT, "multi-tick runs need a contiguous, 16-byte aligned state output");
+  g_error.clear();
+  const cudaError_t err = nsb::launch_tiled(*layout, t, source, true, static_cast<int>(ticks), o,
+                                            nsb::Out{nullptr, 0, 0}, workspace, status,
+                                            static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_run_tiled launch");
+  return NSB_OK;
+}
+
 int nsb_tiled_propagate(int64_t neurons, const nsb_tiled_layout* layout, const float* source,
-                        float* result, int* status, void* stream) {
+                        float* result, void* workspace, size_t workspace_bytes, int* status,
+                        void* stream) {
   if (neurons <= 0) return fail(NSB_ERR_ARGUMENT, "source must be [1,N], N > 0");
   if (!source || !result) return fail(NSB_ERR_ARGUMENT, "source and result arrays are required");
-  if (reinterpret_cast<uintptr_t>(source) % 16 != 0)
+  if (!aligned(source, 16))
     return fail(NSB_ERR_ARGUMENT, "the tiled product needs a 16-byte aligned source");
-  if (!check_tiled(layout)) return NSB_ERR_ARGUMENT;
-  if (layout->cols != neurons) return fail(NSB_ERR_ARGUMENT, "layout and source sizes differ");
+  if (!check_tiled(layout)) return tiled_status(NSB_ERR_ARGUMENT);
+  if (layout->cols != neurons || layout->rows != neurons)
+    return fail(NSB_ERR_ARGUMENT, "layout and source sizes differ");
+  if (!check_workspace(layout, workspace, workspace_bytes)) return NSB_ERR_WORKSPACE;
   g_error.clear();
   nsb::TickArgs t{};
   t.batch = 1;
   t.neurons = neurons;
-  const cudaError_t err = nsb::launch_tiled(*layout, t, source, false, nsb::TickOut{},
-                                            nsb::Out{result, 0, 1}, status,
+  const cudaError_t err = nsb::launch_tiled(*layout, t, source, false, 1, nsb::TickOut{},
+                                            nsb::Out{result, 0, 1}, workspace, status,
                                             static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "nsb_tiled_propagate launch");
   return NSB_OK;

@@ -47,11 +47,14 @@ struct EventArgs {
   int64_t n_edges;
 };
 
-// Tiled B = 1 tick with the gathered state staged in shared memory (tiled.cu).
-size_t tiled_smem_bytes(int block_cols, int max_rows, int buffers);
+// Tiled B = 1 tick with the gathered state staged in shared memory (tiled.cu):
+// `ticks` ticks in one cooperative launch (the first reads `t`, later ones run
+// in place on `out`).
+size_t tiled_smem_bytes(int block_cols, int buffers);
+size_t tiled_workspace_bytes(const nsb_tiled_layout& layout);
 cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, const float* x,
-                         bool update, const TickOut& out, const Out& product, int* status,
-                         cudaStream_t stream);
+                         bool update, int ticks, const TickOut& out, const Out& product,
+                         void* workspace, int* status, cudaStream_t stream);
 
 cudaError_t launch_event(const TickArgs& t, const EventArgs& e, const TickOut& out,
                          const Out& out_emitted, void* workspace, cudaStream_t stream);

@@ -2,32 +2,46 @@
 //
 // Why: at B = 1 every edge gathers one float s[col] at a random column.  Served
 // from L2, those 4-byte gathers cost one L2 tag lookup each and cap the tick
-// far below HBM bandwidth.  Here the columns are split into K blocks that fit
-// in shared memory and every CTA streams its edges block by block, gathering
-// from shared memory instead.
+// far below HBM bandwidth.  Here the gathered columns are split into blocks
+// that fit in one CTA's shared memory, and each CTA streams the edges of one
+// column block (a "stage": that block x a range of destination rows), so the
+// gathers hit shared memory and each block of the state is staged once per
+// tick per CTA that needs it.
 //
 // Data layout (built once per weight version by neurosim_gpu_b200/tiled.py):
-//   * CTA c owns destination rows [row_begin[c], row_begin[c+1]) (balanced by
-//     edge count, one CTA per SM).
-//   * A task is 32 of those rows x one column block k.  Lane i of the warp that
-//     runs the task owns row task_rows[q][i]; its edges with col in block k
-//     are stored at slots off + j*32 + i (j = 0..len-1), so each load of the
-//     warp reads 32 consecutive slots.  Rows are sorted by piece length inside
-//     (c, k) before grouping, so the padding to the task length is small.
-//     Padding slots hold column index `block_cols` (a shared-memory zero) and
-//     weight 0.
-//   * col holds the column relative to its block.
-// Pipeline per CTA (1024 threads):
-//   * warp 31 (producer) copies column block k of s into buffer k % NBUF with a
-//     TMA bulk copy (cp.async.bulk, completion on mbarrier full[b]); it reuses a
-//     buffer after mbarrier empty[b] says all consumer warps left its block.
-//   * warps 0..30 (consumers) take tasks in (block, sorted row group) order
-//     from a shared counter, wait full[b] of the task's block, accumulate their
-//     row's dot product sequentially and add it to jacc[k % NBUF][row].
-//   * after all tasks, every thread applies the pointwise update to rows of the
-//     CTA (j = jacc[0][row] + jacc[1][row]) and writes s', d', a'.
-// Every mbarrier wait is bounded; on timeout the kernel records an error code
-// in `status` and continues, so a fault in the pipeline never hangs the GPU.
+//   * CTA c runs stages stage_ptr[c] .. stage_ptr[c+1]-1 (normally one).
+//   * A task is 32 rows x the stage's block.  Lane i owns row
+//     task_rows[32q+i] & 0x0FFFFFFF; its edges in the block form a contiguous
+//     run of its CSR row (the "piece").  The task has C chunks; chunk c of
+//     lane i holds the lane's edges 4c..4c+3 at slots first + 128c + 4i +
+//     (0..3), so one 8-byte load of the 16-bit columns and one vector load of
+//     the weights serve four edges, and a warp's loads cover 128 consecutive
+//     slots.  Padding slots hold column `block_cols` (a shared-memory zero)
+//     and weight 0.
+//   * NVFP4: the nibble of slot s is in byte s/2 (even slot low).  Edge j of a
+//     lane sits at CSR position o + j and takes the E4M3 scale of CSR block
+//     (o + j) / 16.  Per task, scale_pairs[first pair + 32b + i] = (scale of
+//     block o/16 + b) | (scale of block o/16 + b + 1) << 8, so a chunk needs one
+//     2-byte load for both scales it can touch; the lane's phase o % 16 sits in
+//     bits 28..31 of its task_rows word.
+// One launch runs `ticks` ticks (a cooperative launch, one CTA per SM):
+//   1. warp 31 (producer) copies the block of each stage into a shared-memory
+//      buffer with a TMA bulk copy (cp.async.bulk, completion on mbarrier
+//      full[b]); with two buffers it reuses one after mbarrier empty[b] says all
+//      consumer warps left its stage.
+//   2. warps 0..30 (consumers) take tasks from a shared counter.  Each warp
+//      keeps a ring of D chunks in registers: the loads of a chunk are issued D
+//      chunks before it is used, across task and stage boundaries, so a warp
+//      always has D chunks of edges in flight (also while the state block is
+//      still being staged).  A lane's sum over its piece (sequential, CSR
+//      order) is stored to part[block][row].
+//   3. grid barrier; every CTA takes rows [c*R/C, (c+1)*R/C), adds their sums
+//      in block order (clearing part for the next tick), applies the pointwise
+//      update and writes s', d', a'.
+//   4. for the next tick (in place on the outputs): grid barrier, back to 1.
+// Every wait (mbarrier or grid barrier) is bounded; on timeout the kernel
+// records an error code in `status` and continues, so a fault in the pipeline
+// never hangs the GPU.
 #include <algorithm>
 
 #include "nsb_launch.h"
@@ -39,7 +53,22 @@ constexpr int kTiledThreads = 1024;
 constexpr int kConsumerWarps = kTiledThreads / 32 - 1;
 constexpr int kProducerWarp = kTiledThreads / 32 - 1;
 constexpr long long kWaitLimit = 1ll << 24;  // try_wait polls before giving up
+constexpr long long kGridWaitLimit = 1ll << 24;  // polls of the grid barrier
 constexpr int kTiledHeader = 64;             // mbarriers + task counter
+constexpr int kChunk = 4;                    // slots of one lane per vector load
+constexpr int kChunkSlots = 32 * kChunk;     // slots of one warp-wide chunk
+// L2 prefetch of task data by the producer warp: bytes of tasks a CTA keeps
+// prefetched beyond the hand-out counter.  Only the narrower weight formats
+// use it: an fp32 tick streams more bytes than L2 holds, and prefetched lines
+// were evicted before use (measured: 43.9 us without, 46-51 us with).
+constexpr int kPrefetchBudget = 128 << 10;
+constexpr uint32_t kRowMask = 0x0FFFFFFFu;   // task_rows: row bits; kRowMask = padding lane
+
+// Tag of a chunk in a consumer's ring (one 32-bit word per lane).
+constexpr uint32_t kTagValid = 1u;
+constexpr uint32_t kTagLast = 2u;   // last chunk of its task
+constexpr int kTagPhase = 2;        // NVFP4: (phase + 4c) % 16, 4 bits
+constexpr int kTagStage = 8;        // CTA-local stage, 24 bits
 
 // Error word used when the caller passes no status pointer.
 __device__ int g_tiled_status;
@@ -95,23 +124,8 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__device__ __forceinline__ int ld_stream_s32(const int* p, uint64_t pol) {
-  int r;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.s32 %0, [%1], %2;"
-               : "=r"(r)
-               : "l"(p), "l"(pol));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t ld_stream_u32(const uint32_t* p, uint64_t pol) {
-  uint32_t r;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.u32 %0, [%1], %2;"
-               : "=r"(r)
-               : "l"(p), "l"(pol));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t ld_stream_u16(const uint16_t* p, uint64_t pol) {
+// Streaming loads: read once per tick, no L1 allocation, evict-first in L2.
+__device__ __forceinline__ uint32_t ld_stream_u16(const void* p, uint64_t pol) {
   unsigned short r;
   asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.u16 %0, [%1], %2;"
                : "=h"(r)
@@ -119,103 +133,204 @@ __device__ __forceinline__ uint32_t ld_stream_u16(const uint16_t* p, uint64_t po
   return r;
 }
 
-__device__ __forceinline__ uint32_t ld_stream_u8(const uint8_t* p, uint64_t pol) {
-  unsigned short r;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.u8 %0, [%1], %2;"
-               : "=h"(r)
+__device__ __forceinline__ uint32_t ld_stream_u32(const void* p, uint64_t pol) {
+  uint32_t r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.u32 %0, [%1], %2;"
+               : "=r"(r)
                : "l"(p), "l"(pol));
   return r;
 }
 
-// Per-slot weight readers of the tiled layout.  `slot` indexes the tiled
-// arrays; `orig` is the edge's position in the original CSR (NVFP4 scales).
-struct TiledF32 {
+__device__ __forceinline__ uint2 ld_stream_v2(const void* p, uint64_t pol) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0,%1}, [%2], %3;"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p), "l"(pol));
+  return r;
+}
+
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p, uint64_t pol) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p), "l"(pol));
+  return r;
+}
+
+// Bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, multiple of 16).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Two E4M3 codes (low byte first) -> two floats, exact (every E4M3 value is
+// an f16 value).  Hardware conversion on sm_100a.
+__device__ __forceinline__ float2 e4m3x2_to_float2(uint32_t two) {
+  uint32_t h;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, lo;\n\t}"
+      : "=r"(h)
+      : "r"(two));
+  return __half22float2(*reinterpret_cast<__half2*>(&h));
+}
+
+// Four E2M1 codes (nibbles, lowest first) -> four floats, exact.
+__device__ __forceinline__ void e2m1x4_to_float(uint32_t four, float (&v)[4]) {
+  uint32_t h0, h1;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t}"
+      : "=r"(h0), "=r"(h1)
+      : "r"(four));
+  const float2 a = __half22float2(*reinterpret_cast<__half2*>(&h0));
+  const float2 b = __half22float2(*reinterpret_cast<__half2*>(&h1));
+  v[0] = a.x;
+  v[1] = a.y;
+  v[2] = b.x;
+  v[3] = b.y;
+}
+
+// Chunk readers: load(slot, scale_entry) fetches the weights of one lane's
+// four slots; decode() turns them into the four float32 weights, equal bit for
+// bit to the reference quantizer's dequantized values (precision.py:102-109):
+// fp8 -> e4m3(code) * g, nvfp4 -> e2m1(code) * (e4m3(block scale) * g).
+struct ChunkF32 {
+  using Raw = uint4;
   const float* w;
-  __device__ __forceinline__ float at(int64_t slot, uint64_t pol) const {
-    return __uint_as_float(ld_stream_u32(reinterpret_cast<const uint32_t*>(w) + slot, pol));
+  __device__ __forceinline__ void prefetch(int first, int chunks, int) const {
+    prefetch_l2(w + first, static_cast<uint32_t>(chunks) * kChunkSlots * 4u);
+  }
+  __device__ __forceinline__ void set_scale(float) {}
+  __device__ __forceinline__ Raw load(int64_t slot, int64_t, uint64_t pol) const {
+    return ld_stream_v4(w + slot, pol);
+  }
+  __device__ __forceinline__ void decode(const Raw& r, uint32_t, float (&v)[4]) const {
+    v[0] = __uint_as_float(r.x);
+    v[1] = __uint_as_float(r.y);
+    v[2] = __uint_as_float(r.z);
+    v[3] = __uint_as_float(r.w);
   }
 };
-struct TiledF16 {
+
+struct ChunkF16 {
+  using Raw = uint2;
   const __half* w;
-  __device__ __forceinline__ float at(int64_t slot, uint64_t pol) const {
-    return __half2float(__ushort_as_half(static_cast<unsigned short>(
-        ld_stream_u16(reinterpret_cast<const uint16_t*>(w) + slot, pol))));
+  __device__ __forceinline__ void prefetch(int first, int chunks, int) const {
+    prefetch_l2(w + first, static_cast<uint32_t>(chunks) * kChunkSlots * 2u);
+  }
+  __device__ __forceinline__ void set_scale(float) {}
+  __device__ __forceinline__ Raw load(int64_t slot, int64_t, uint64_t pol) const {
+    return ld_stream_v2(w + slot, pol);
+  }
+  __device__ __forceinline__ void decode(const Raw& r, uint32_t, float (&v)[4]) const {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+    v[0] = a.x;
+    v[1] = a.y;
+    v[2] = b.x;
+    v[3] = b.y;
   }
 };
-struct TiledE4M3 {
+
+struct ChunkE4M3 {
+  using Raw = uint32_t;
   const uint8_t* codes;
-  const float* global;
-  __device__ __forceinline__ float at(int64_t slot, uint64_t pol) const {
-    return __fmul_rn(e4m3_value(ld_stream_u8(codes + slot, pol)), __ldg(global));
+  float g;
+  __device__ __forceinline__ void prefetch(int first, int chunks, int) const {
+    prefetch_l2(codes + first, static_cast<uint32_t>(chunks) * kChunkSlots);
+  }
+  __device__ __forceinline__ void set_scale(float s) { g = s; }
+  __device__ __forceinline__ Raw load(int64_t slot, int64_t, uint64_t pol) const {
+    return ld_stream_u32(codes + slot, pol);
+  }
+  __device__ __forceinline__ void decode(Raw r, uint32_t, float (&v)[4]) const {
+    const float2 a = e4m3x2_to_float2(r & 0xFFFFu);
+    const float2 b = e4m3x2_to_float2(r >> 16);
+    v[0] = __fmul_rn(a.x, g);
+    v[1] = __fmul_rn(a.y, g);
+    v[2] = __fmul_rn(b.x, g);
+    v[3] = __fmul_rn(b.y, g);
+  }
+};
+
+struct ChunkNVFP4 {
+  using Raw = uint32_t;  // four codes (low 16 bits) | scale pair << 16
+  const uint8_t* codes;
+  const uint16_t* pairs;
+  float g;
+  // Codes and the task's scale table ((11 + 4C) / 16 + 1 rows of 32 pairs).
+  __device__ __forceinline__ void prefetch(int first, int chunks, int entry) const {
+    prefetch_l2(codes + (first >> 1), static_cast<uint32_t>(chunks) * (kChunkSlots / 2));
+    prefetch_l2(pairs + entry, static_cast<uint32_t>(((11 + kChunk * chunks) >> 4) + 1) * 64u);
+  }
+  __device__ __forceinline__ void set_scale(float s) { g = s; }
+  __device__ __forceinline__ Raw load(int64_t slot, int64_t entry, uint64_t pol) const {
+    return ld_stream_u16(codes + (slot >> 1), pol) | (static_cast<uint32_t>(__ldg(pairs + entry)) << 16);
+  }
+  __device__ __forceinline__ void decode(Raw r, uint32_t tag, float (&v)[4]) const {
+    const float2 scale = e4m3x2_to_float2(r >> 16);
+    const float f0 = __fmul_rn(scale.x, g), f1 = __fmul_rn(scale.y, g);
+    const int phase = (tag >> kTagPhase) & 15;  // edge e is in the next block iff phase + e >= 16
+    float q[4];
+    e2m1x4_to_float(r & 0xFFFFu, q);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = __fmul_rn(q[e], phase + e >= 16 ? f1 : f0);
   }
 };
 
 struct TiledArgs {
-  const int32_t* row_begin;    // [C+1]
-  const int32_t* task_ptr;     // [C*K+1]
-  const int32_t* task_offset;  // [T]  first slot of the task
-  const int32_t* task_len;     // [T]
-  const int16_t* task_rows;    // [T*32] row relative to row_begin[c], -1 = empty lane
-  const int32_t* task_orig;    // [T*32] NVFP4: CSR position of the lane's first edge
-  const int32_t* col;          // [S] column relative to the block, block_cols = padding
-  const void* weight;          // [S] (NVFP4: [S/2] packed codes)
-  const uint8_t* scales;       // NVFP4 block scales of the original CSR
-  const float* global_scale;
-  int64_t n_scales;
-  int32_t format;
-  int32_t blocks;              // K
+  const int32_t* stage_ptr;    // [C+1]
+  const int32_t* stage_block;  // [stages]
+  const int32_t* task_ptr;     // [C+1]
+  const int4* tasks;           // [T]: first slot, chunks, stage (CTA-local), first scale pair
+  const int32_t* task_rows;    // [T*32]: row | phase << 28
+  const uint16_t* col;         // [S] column relative to the block, block_cols = padding
+  const float* global_scale;   // E4M3 / NVFP4: one float
+  float* part;                 // workspace: [blocks][rows] per-block row sums (zero between launches)
+  unsigned long long* barrier; // workspace: grid-barrier arrival counter
   int32_t block_cols;          // CB
   int32_t buffers;             // NBUF (1 or 2)
-  int32_t max_rows;            // rows of the largest CTA range
+  int32_t prefetch_ahead;      // tasks prefetched beyond the hand-out counter
+  int32_t prefetch_first;      // tasks of the next tick's first round prefetched (0 or warps)
+  int64_t rows;                // destination rows
   int64_t cols;                // length of the gathered source vector
 };
 
-template <typename W>
-__device__ __forceinline__ float task_dot(const W& w, const int* __restrict__ col,
-                                          const float* __restrict__ sb, int64_t base, int len,
-                                          uint64_t pol) {
-  float acc = -0.0f;
-  int j = 0;
-  for (; j + 8 <= len; j += 8) {
-    int c[8];
-    float v[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) c[u] = ld_stream_s32(col + base + (j + u) * 32, pol);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = w.at(base + (j + u) * 32, pol);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) acc = fmaf(v[u], sb[c[u]], acc);
-  }
-  for (; j < len; ++j) acc = fmaf(w.at(base + j * 32, pol), sb[ld_stream_s32(col + base + j * 32, pol)], acc);
-  return acc;
+__device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
-__device__ __forceinline__ float task_dot_nvfp4(const TiledArgs& L, const int* __restrict__ col,
-                                                const float* __restrict__ sb, int64_t base,
-                                                int len, int orig, uint64_t pol) {
-  const uint8_t* codes = static_cast<const uint8_t*>(L.weight);
-  const float g = __ldg(L.global_scale);
-  const int shift = (threadIdx.x & 1) * 4;  // slot parity = lane parity (base % 32 == 0)
-  float acc = -0.0f;
-  int64_t block = -1;
-  float factor = 0.0f;
-  for (int j = 0; j < len; ++j) {
-    const int64_t slot = base + j * 32;
-    const uint32_t code = (ld_stream_u8(codes + (slot >> 1), pol) >> shift) & 15u;
-    const int64_t b = min(static_cast<int64_t>(orig + j) >> 4, L.n_scales - 1);
-    if (b != block) {
-      block = b;
-      factor = __fmul_rn(e4m3_value(__ldg(L.scales + b)), g);
+// Grid-wide barrier of a cooperative launch over a monotonic 64-bit arrival
+// counter: the CTA whose arrival is number a (0-based) waits until the counter
+// reaches the next multiple of the grid size above a.  Nothing is reset, so the
+// critical path is one atomic and the pollers' next read.  Every launch that
+// uses a workspace has the same grid size and passes every barrier, so the
+// counter is a multiple of the grid size between launches.  The wait is
+// bounded: on timeout it records code 4.
+__device__ void grid_barrier(unsigned long long* count, int* st) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned long long arrival = atomicAdd(count, 1ull);
+    const unsigned long long target = (arrival / gridDim.x + 1) * gridDim.x;
+    long long polls = 0;
+    while (ld_acquire_gpu(count) < target) {
+      if (++polls > (1 << 16)) {
+        if (polls > kGridWaitLimit) {
+          atomicExch(st, 4);
+          break;
+        }
+        __nanosleep(256);
+      }
     }
-    acc = fmaf(__fmul_rn(e2m1_value(code), factor), sb[ld_stream_s32(col + slot, pol)], acc);
+    __threadfence();
   }
-  return acc;
+  __syncthreads();
 }
 
-template <typename W>
+template <typename W, int D>
 __global__ void __launch_bounds__(kTiledThreads, 1)
-tiled_tick_kernel(TiledArgs L, W w, TickArgs t, const float* __restrict__ x, TickOut out,
-                  Out product, bool update, int* status) {
+tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ x0, TickOut out,
+                  Out product, bool update, int ticks, int* status) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int nbuf = L.buffers;
   const int cb_pad = L.block_cols + 4;
@@ -223,117 +338,287 @@ tiled_tick_kernel(TiledArgs L, W w, TickArgs t, const float* __restrict__ x, Tic
   uint64_t* empty = full + 2;                                         // [2]
   int* next_task = reinterpret_cast<int*>(empty + 2);
   float* sbuf = reinterpret_cast<float*>(smem_raw + kTiledHeader);    // [nbuf][cb_pad]
-  float* jacc = sbuf + nbuf * cb_pad;                                 // [nbuf][max_rows]
   int* st = status ? status : &g_tiled_status;
 
   const int c = blockIdx.x;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int row0 = L.row_begin[c];
-  const int rows = L.row_begin[c + 1] - row0;
-  const int K = L.blocks;
-  const int task_first = L.task_ptr[c * K];
-  const int task_count = L.task_ptr[(c + 1) * K] - task_first;
+  const int stage_first = L.stage_ptr[c];
+  const int stages = L.stage_ptr[c + 1] - stage_first;
+  const int task_first = L.task_ptr[c];
+  const int task_count = L.task_ptr[c + 1] - task_first;
+  const int uses = ticks * stages;  // stage uses of this launch, in order
+  const int64_t update_lo = L.rows * c / gridDim.x;
+  const int64_t update_hi = L.rows * (c + 1) / gridDim.x;
 
-  for (int i = threadIdx.x; i < nbuf * L.max_rows; i += blockDim.x) jacc[i] = 0.0f;
   if (threadIdx.x < 4 * nbuf) sbuf[(threadIdx.x >> 2) * cb_pad + L.block_cols + (threadIdx.x & 3)] = 0.0f;
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
       mbar_init(full + b, 1);
       mbar_init(empty + b, kConsumerWarps);
     }
-    *next_task = 0;
+    *next_task = kConsumerWarps;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  if (warp == kProducerWarp) {
-    if (lane == 0) {
-      for (int k = 0; k < K; ++k) {
-        const int b = k % nbuf;
-        const int use = k / nbuf;
-        if (k >= nbuf && !mbar_wait(empty + b, (use - 1) & 1)) atomicExch(st, 1);
-        fence_proxy_async_smem();
-        const int first = k * L.block_cols;
-        const int count = min(static_cast<int64_t>(L.block_cols), L.cols - first);
-        const int bulk = count & ~3;  // 16-byte multiple, rest by plain stores
-        float* dst = sbuf + b * cb_pad;
-        for (int i = bulk; i < count; ++i) dst[i] = __ldg(x + first + i);
-        mbar_arrive_expect_tx(full + b, static_cast<uint32_t>(bulk) * 4u);
-        if (bulk > 0) bulk_copy_to_smem(dst, x + first, static_cast<uint32_t>(bulk) * 4u, full + b);
-      }
-      // Do not retire while a copy into this CTA's shared memory may be in flight.
-      for (int k = max(0, K - nbuf); k < K; ++k)
-        if (!mbar_wait(full + (k % nbuf), (k / nbuf) & 1)) atomicExch(st, 2);
+  W w = weights;
+  if (L.global_scale) w.set_scale(__ldg(L.global_scale));
+  const uint64_t pol = evict_first_policy();
+  // Bulk L2 prefetch of one task's edges (lane 0 of a consumer warp).
+  auto prefetch_task = [&](const int4& m) {
+    if (m.y > 0) {
+      prefetch_l2(L.col + m.x, static_cast<uint32_t>(m.y) * kChunkSlots * 2u);
+      w.prefetch(m.x, m.y, m.w);
     }
-  } else {
-    const uint64_t pol = evict_first_policy();
-    int waited = -1;  // highest block whose full barrier this warp has observed
-    int current = 0;  // block of the tasks this warp works on
-    // Blocks are observed in order.  A warp leaves block `current` (arrives on
-    // its empty barrier) only after it has seen that block's full barrier, so an
-    // arrival can never be counted in the phase of an older block.
-    auto observe = [&](int k) {
-      if (waited < k) {
-        if (!mbar_wait(full + (k % nbuf), (k / nbuf) & 1)) atomicExch(st, 3);
-        waited = k;
-      }
-    };
-    auto leave_until = [&](int k) {
-      while (current < k) {
-        observe(current);
-        if (lane == 0 && current < K - nbuf) mbar_arrive(empty + (current % nbuf));
-        ++current;
-      }
-    };
-    while (true) {
-      int q = 0;
-      if (lane == 0) q = atomicAdd(next_task, 1);
-      q = __shfl_sync(0xffffffffu, q, 0);
-      if (q >= task_count) break;
-      const int task = task_first + q;
-      int k = current;  // tasks are ordered by block: find this task's block
-      while (L.task_ptr[c * K + k + 1] <= task) ++k;
-      leave_until(k);
-      observe(k);
-      __syncwarp();
-      const int row = L.task_rows[static_cast<int64_t>(task) * 32 + lane];
-      const int64_t base = static_cast<int64_t>(L.task_offset[task]) + lane;
-      const int len = L.task_len[task];
-      const float* sb = sbuf + (k % nbuf) * cb_pad;
-      float acc;
-      if (L.format == NSB_WEIGHT_NVFP4) {
-        acc = task_dot_nvfp4(L, L.col, sb, base, len,
-                             L.task_orig[static_cast<int64_t>(task) * 32 + lane], pol);
-      } else {
-        acc = task_dot(w, L.col, sb, base, len, pol);
-      }
-      if (row >= 0) jacc[(k % nbuf) * L.max_rows + row] += acc;
+  };
+  // Warp w starts every tick with task w; the rest are handed out in order by
+  // the shared counter.  The producer warp prefetches tasks into L2 ahead of
+  // that counter, and the next tick's first round before the tick ends, so
+  // DRAM keeps streaming through the barriers and the update.
+  int prefetched = 0;  // producer: tasks of the current tick already prefetched
+  // Consumer bookkeeping of stage uses (running over all ticks of the launch).
+  int waited = -1;  // highest use whose full barrier this warp has observed
+  int current = 0;  // lowest use this warp has not left yet
+  // Uses are observed in order.  A warp leaves use `current` (arrives on its
+  // empty barrier) only after it has seen that use's full barrier, so an
+  // arrival can never be counted in the phase of an older use.
+  auto observe = [&](int g) {
+    if (waited < g) {
+      if (!mbar_wait(full + (g % nbuf), (g / nbuf) & 1)) atomicExch(st, 3);
+      waited = g;
     }
-    leave_until(K);  // leave every remaining block (arrivals the producer may need)
-  }
-  __syncthreads();
+  };
+  auto leave_until = [&](int g) {
+    while (current < g) {
+      observe(current);
+      if (lane == 0 && current < uses - nbuf) mbar_arrive(empty + (current % nbuf));
+      ++current;
+    }
+  };
 
-  for (int r = threadIdx.x; r < rows; r += blockDim.x) {
-    const float j = nbuf == 2 ? jacc[r] + jacc[L.max_rows + r] : jacc[r];
-    const int64_t n = row0 + r;
-    if (update) {
-      const Update u = advance_at(t, j, 0, n);
-      out.s.put(0, n, u.s);
-      out.d.put(0, n, u.d);
-      out.a.put(0, n, u.a);
+  for (int tick = 0; tick < ticks; ++tick) {
+    const float* x = tick == 0 ? x0 : out.s.data;
+    const int use0 = tick * stages;
+    if (warp == kProducerWarp) {
+      // All 32 lanes prefetch tasks (each lane one task's metadata load and
+      // bulk L2 prefetches); lane 0 also stages the state blocks.
+      auto prefetch_upto = [&](int limit) {
+        for (; prefetched < limit; prefetched += 32)
+          if (prefetched + lane < limit) prefetch_task(__ldg(L.tasks + task_first + prefetched + lane));
+        prefetched = limit;
+      };
+      if (lane == 0) {
+        // The state was written by other CTAs' generic stores before the grid
+        // barrier; order those writes before this thread's async-proxy reads.
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        for (int s = 0; s < stages; ++s) {
+          const int g = use0 + s;
+          const int b = g % nbuf;
+          if (g >= nbuf && !mbar_wait(empty + b, ((g / nbuf) - 1) & 1)) atomicExch(st, 1);
+          fence_proxy_async_smem();
+          const int64_t first = static_cast<int64_t>(__ldg(L.stage_block + stage_first + s)) *
+                                L.block_cols;
+          const int count = static_cast<int>(min(static_cast<int64_t>(L.block_cols), L.cols - first));
+          const int bulk = count & ~3;  // 16-byte multiple, rest by plain stores
+          float* dst = sbuf + b * cb_pad;
+          for (int i = bulk; i < count; ++i) dst[i] = x[first + i];
+          mbar_arrive_expect_tx(full + b, static_cast<uint32_t>(bulk) * 4u);
+          if (bulk > 0) bulk_copy_to_smem(dst, x + first, static_cast<uint32_t>(bulk) * 4u, full + b);
+        }
+      }
+      __syncwarp();
+      if (tick == 0) prefetch_upto(min(task_count, L.prefetch_first));  // first round of tick 0
+      // L2 prefetch of this tick's tasks, kPrefetchAhead tasks ahead of the
+      // hand-out counter, then of the next tick's first round (one task per
+      // consumer warp), which keeps DRAM busy across the barriers and the update.
+      const volatile int* handed = next_task;
+      long long polls = 0;
+      while (prefetched < task_count) {
+        const int limit = min(task_count, __shfl_sync(0xffffffffu, *handed, 0) + L.prefetch_ahead);
+        if (prefetched >= limit) {
+          if (++polls > kWaitLimit) {  // consumers stalled: stop prefetching
+            if (lane == 0) atomicExch(st, 5);
+            break;
+          }
+          __nanosleep(256);
+          continue;
+        }
+        prefetch_upto(limit);
+      }
+      prefetched = 0;
+      if (tick + 1 < ticks) prefetch_upto(min(task_count, L.prefetch_first));
+      if (lane == 0) {
+        // Do not leave the tick while a copy into this CTA's shared memory may
+        // be in flight.
+        for (int g = max(use0, use0 + stages - nbuf); g < use0 + stages; ++g)
+          if (!mbar_wait(full + (g % nbuf), (g / nbuf) & 1)) atomicExch(st, 2);
+      }
     } else {
-      product.put(0, n, j);
+      // ---- load side: task cursor (the next task is fetched one task ahead) --
+      auto grab = [&]() {
+        int q = 0;
+        if (lane == 0) q = atomicAdd(next_task, 1);
+        return __shfl_sync(0xffffffffu, q, 0);
+      };
+      int next_q = warp < task_count ? warp : task_count;  // first task: static
+      int4 next_meta = make_int4(0, 0, 0, 0);
+      uint32_t next_row = kRowMask;
+      auto fetch = [&]() {
+        if (next_q < task_count) {
+          const int64_t task = task_first + next_q;
+          next_meta = __ldg(L.tasks + task);
+          next_row = static_cast<uint32_t>(__ldg(L.task_rows + task * 32 + lane));
+        }
+      };
+      fetch();
+      int slot = 0;          // next slot of this lane to load
+      int entry = 0;         // NVFP4: this lane's column in the task's scale table
+      int left = 0;          // chunks of the current task not yet loaded
+      int chunk = 0;         // index of the next chunk in its task
+      int phase = 0;         // NVFP4 phase of this lane's piece
+      uint32_t row = kRowMask;
+      uint32_t tag_base = 0;
+      // Issue the loads of the next chunk into one ring entry (tag 0: none left).
+      auto issue = [&](typename W::Raw& raw, uint2& cols, uint32_t& tag, uint32_t& tag_row) {
+        while (left == 0) {  // warp-uniform
+          if (next_q >= task_count) {
+            tag = 0;
+            return;
+          }
+          slot = next_meta.x + lane * kChunk;
+          left = next_meta.y;
+          chunk = 0;
+          entry = next_meta.w + lane;
+          phase = static_cast<int>(next_row >> 28);
+          row = next_row & kRowMask;
+          tag_base = kTagValid | (static_cast<uint32_t>(next_meta.z) << kTagStage);
+          next_q = grab();
+          fetch();
+        }
+        const int p = phase + chunk * kChunk;
+        raw = w.load(slot, entry + (p >> 4) * 32, pol);
+        cols = ld_stream_v2(L.col + slot, pol);
+        tag = tag_base | (static_cast<uint32_t>(p & 15) << kTagPhase) | (left == 1 ? kTagLast : 0u);
+        tag_row = row;
+        slot += kChunkSlots;
+        ++chunk;
+        --left;
+      };
+
+      // ---- the ring ---------------------------------------------------------
+      typename W::Raw raw[D];
+      uint2 cols[D];
+      uint32_t tag[D], rows[D];
+#pragma unroll
+      for (int u = 0; u < D; ++u) issue(raw[u], cols[u], tag[u], rows[u]);
+      int stage = -1;
+      const float* sb = sbuf;
+      float* part = L.part;
+      float acc = -0.0f;
+      // Entries are issued in order, so once entry 0 is empty all are.
+      while (tag[0] & kTagValid) {
+#pragma unroll
+        for (int u = 0; u < D; ++u) {
+          const uint32_t g = tag[u];
+          if (g & kTagValid) {
+            const int s = static_cast<int>(g >> kTagStage);
+            if (s != stage) {  // warp-uniform
+              leave_until(use0 + s);
+              observe(use0 + s);
+              stage = s;
+              sb = sbuf + ((use0 + s) % nbuf) * cb_pad;
+              part = L.part + static_cast<int64_t>(__ldg(L.stage_block + stage_first + s)) * L.rows;
+            }
+            float v[4];
+            w.decode(raw[u], g, v);
+            acc = fmaf(v[0], sb[cols[u].x & 0xFFFFu], acc);
+            acc = fmaf(v[1], sb[cols[u].x >> 16], acc);
+            acc = fmaf(v[2], sb[cols[u].y & 0xFFFFu], acc);
+            acc = fmaf(v[3], sb[cols[u].y >> 16], acc);
+            if (g & kTagLast) {
+              if (rows[u] != kRowMask) part[rows[u]] = acc;
+              acc = -0.0f;
+            }
+          }
+          issue(raw[u], cols[u], tag[u], rows[u]);
+        }
+      }
+      leave_until(use0 + stages);  // leave every remaining stage of this tick
     }
+    __syncthreads();
+    if (threadIdx.x == 0) *next_task = kConsumerWarps;
+    grid_barrier(L.barrier, st);  // every row sum of this tick is in part
+
+    // Update of rows [update_lo, update_hi), two rows per thread per round:
+    // every operand of both rows is loaded before any store, so a round costs
+    // one memory round trip.  The row sums and the state written by earlier
+    // ticks of this launch are read through L2.
+    const int planes = static_cast<int>((L.cols + L.block_cols - 1) / L.block_cols);
+    for (int64_t n0 = update_lo + threadIdx.x; n0 < update_hi; n0 += 2 * blockDim.x) {
+      float j[2], s0[2], d0[2], a0[2], u[2], v[2], pr[2][6];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int64_t n = n0 + r * blockDim.x;
+        const bool row = n < update_hi;
+        s0[r] = d0[r] = a0[r] = u[r] = v[r] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 6; ++i) pr[r][i] = 0.0f;
+        if (row && update) {  // tick operands exist only for a tick
+          if (tick == 0) {
+            s0[r] = t.s.at(0, n);
+            d0[r] = t.d.at(0, n);
+            a0[r] = t.a.at(0, n);
+          } else {
+            s0[r] = __ldcg(out.s.data + n * out.s.sn);
+            d0[r] = __ldcg(out.d.data + n * out.d.sn);
+            a0[r] = __ldcg(out.a.data + n * out.a.sn);
+          }
+          u[r] = t.u.at(0, n);
+          v[r] = t.v.at(0, n);
+#pragma unroll
+          for (int i = 0; i < 6; ++i) pr[r][i] = t.p.at(i, n);
+        }
+        j[r] = 0.0f;
+        if (row) {
+          const float* p = L.part + n;
+          for (int k0 = 0; k0 < planes; k0 += 8) {  // block order: ((p0 + p1) + p2) + ...
+            float sums[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sums[i] = k0 + i < planes ? __ldcg(p + (k0 + i) * L.rows) : 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              if (k0 + i < planes) j[r] = k0 + i == 0 ? sums[i] : j[r] + sums[i];
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int64_t n = n0 + r * blockDim.x;
+        if (n >= update_hi) continue;
+        for (int k = 0; k < planes; ++k) L.part[n + k * L.rows] = 0.0f;
+        if (update) {
+          const Update q = advance(j[r], s0[r], d0[r], a0[r], u[r], v[r], pr[r][0], pr[r][1],
+                                   pr[r][2], pr[r][3], pr[r][4], pr[r][5]);
+          out.s.put(0, n, q.s);
+          out.d.put(0, n, q.d);
+          out.a.put(0, n, q.a);
+        } else {
+          product.put(0, n, j[r]);
+        }
+      }
+    }
+    if (tick + 1 < ticks) grid_barrier(L.barrier, st);  // the new state is complete
   }
 }
 
-template <typename W>
+template <typename W, int D>
 cudaError_t launch_tiled_variant(const TiledArgs& L, const W& w, const TickArgs& t,
                                  const float* x, const TickOut& out, const Out& product,
-                                 bool update, int* status, int ctas, cudaStream_t stream) {
-  const size_t smem = tiled_smem_bytes(L.block_cols, L.max_rows, L.buffers);
-  auto kernel = tiled_tick_kernel<W>;
+                                 bool update, int ticks, int* status, int ctas,
+                                 cudaStream_t stream) {
+  const size_t smem = tiled_smem_bytes(L.block_cols, L.buffers);
+  auto kernel = tiled_tick_kernel<W, D>;
   static int configured[64] = {0};
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
@@ -344,53 +629,75 @@ cudaError_t launch_tiled_variant(const TiledArgs& L, const W& w, const TickArgs&
     if (err != cudaSuccess) return err;
     configured[device & 63] = static_cast<int>(smem);
   }
-  kernel<<<ctas, kTiledThreads, smem, stream>>>(L, w, t, x, out, product, update, status);
-  return cudaGetLastError();
+  // Cooperative launch: the grid barrier needs every CTA resident at once.
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(ctas);
+  config.blockDim = dim3(kTiledThreads);
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeCooperative;
+  attribute[0].val.cooperative = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  return cudaLaunchKernelEx(&config, kernel, L, w, t, x, out, product, update, ticks, status);
 }
 
 }  // namespace
 
-size_t tiled_smem_bytes(int block_cols, int max_rows, int buffers) {
-  return kTiledHeader + static_cast<size_t>(buffers) * (block_cols + 4) * 4 +
-         static_cast<size_t>(buffers) * max_rows * 4;
+size_t tiled_smem_bytes(int block_cols, int buffers) {
+  return kTiledHeader + static_cast<size_t>(buffers) * (block_cols + 4) * 4;
+}
+
+size_t tiled_workspace_bytes(const nsb_tiled_layout& layout) {
+  return 256 + static_cast<size_t>(layout.blocks) * static_cast<size_t>(layout.rows) * 4;
 }
 
 cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, const float* x,
-                         bool update, const TickOut& out, const Out& product, int* status,
-                         cudaStream_t stream) {
+                         bool update, int ticks, const TickOut& out, const Out& product,
+                         void* workspace, int* status, cudaStream_t stream) {
   TiledArgs L;
-  L.row_begin = layout.row_begin;
+  L.stage_ptr = layout.stage_ptr;
+  L.stage_block = layout.stage_block;
   L.task_ptr = layout.task_ptr;
-  L.task_offset = layout.task_offset;
-  L.task_len = layout.task_len;
+  L.tasks = reinterpret_cast<const int4*>(layout.tasks);
   L.task_rows = layout.task_rows;
-  L.task_orig = layout.task_orig;
   L.col = layout.col;
-  L.weight = layout.weight;
-  L.scales = layout.block_scales;
   L.global_scale = layout.global_scale;
-  L.n_scales = layout.n_block_scales;
-  L.format = layout.format;
-  L.blocks = layout.blocks;
+  L.barrier = static_cast<unsigned long long*>(workspace);
+  L.part = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + 256);
   L.block_cols = layout.block_cols;
   L.buffers = layout.buffers;
-  L.max_rows = layout.max_rows;
+  L.rows = layout.rows;
   L.cols = layout.cols;
+  // Prefetch window in tasks: kPrefetchBudget bytes of an average task.
+  static const double slot_bytes[4] = {6.0, 4.0, 3.0, 2.5};
+  const double task_bytes = layout.n_tasks > 0 ? static_cast<double>(layout.n_slots) *
+                                                     slot_bytes[layout.format & 3] / layout.n_tasks
+                                               : 1.0;
+  const bool prefetch = layout.format != NSB_WEIGHT_F32;
+  L.prefetch_ahead = prefetch ? static_cast<int32_t>(
+                                    std::min(4096.0, kPrefetchBudget / std::max(task_bytes, 1.0)))
+                              : 0;
+  L.prefetch_first = prefetch ? kConsumerWarps : 0;
   const int ctas = layout.ctas;
   switch (layout.format) {
     case NSB_WEIGHT_F16:
-      return launch_tiled_variant(L, TiledF16{static_cast<const __half*>(layout.weight)}, t, x,
-                                  out, product, update, status, ctas, stream);
+      return launch_tiled_variant<ChunkF16, 4>(L, ChunkF16{static_cast<const __half*>(layout.weight)},
+                                               t, x, out, product, update, ticks, status, ctas,
+                                               stream);
     case NSB_WEIGHT_E4M3:
-      return launch_tiled_variant(L, TiledE4M3{static_cast<const uint8_t*>(layout.weight),
-                                               layout.global_scale},
-                                  t, x, out, product, update, status, ctas, stream);
+      return launch_tiled_variant<ChunkE4M3, 4>(
+          L, ChunkE4M3{static_cast<const uint8_t*>(layout.weight), 0.0f}, t, x, out, product,
+          update, ticks, status, ctas, stream);
     case NSB_WEIGHT_NVFP4:
-      return launch_tiled_variant(L, TiledF32{nullptr}, t, x, out, product, update, status, ctas,
-                                  stream);
+      return launch_tiled_variant<ChunkNVFP4, 4>(
+          L, ChunkNVFP4{static_cast<const uint8_t*>(layout.weight), layout.scale_pairs, 0.0f}, t,
+          x, out, product, update, ticks, status, ctas, stream);
     default:
-      return launch_tiled_variant(L, TiledF32{static_cast<const float*>(layout.weight)}, t, x,
-                                  out, product, update, status, ctas, stream);
+      return launch_tiled_variant<ChunkF32, 4>(L, ChunkF32{static_cast<const float*>(layout.weight)},
+                                               t, x, out, product, update, ticks, status, ctas,
+                                               stream);
   }
 }
 

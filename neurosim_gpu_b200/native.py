@@ -76,14 +76,15 @@ class _OutCsr(ctypes.Structure):
 class _TiledLayout(ctypes.Structure):
     _fields_ = [("ctas", ctypes.c_int32), ("blocks", ctypes.c_int32),
                 ("block_cols", ctypes.c_int32), ("buffers", ctypes.c_int32),
-                ("max_rows", ctypes.c_int32), ("format", ctypes.c_int32),
-                ("n_tasks", ctypes.c_int64), ("n_slots", ctypes.c_int64),
-                ("n_block_scales", ctypes.c_int64), ("cols", ctypes.c_int64),
-                ("row_begin", ctypes.c_void_p), ("task_ptr", ctypes.c_void_p),
-                ("task_offset", ctypes.c_void_p), ("task_len", ctypes.c_void_p),
-                ("task_rows", ctypes.c_void_p), ("task_orig", ctypes.c_void_p),
-                ("col", ctypes.c_void_p), ("weight", ctypes.c_void_p),
-                ("block_scales", ctypes.c_void_p), ("global_scale", ctypes.c_void_p)]
+                ("format", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("n_stages", ctypes.c_int64), ("n_tasks", ctypes.c_int64),
+                ("n_slots", ctypes.c_int64), ("n_scale_pairs", ctypes.c_int64),
+                ("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
+                ("stage_ptr", ctypes.c_void_p), ("stage_block", ctypes.c_void_p),
+                ("task_ptr", ctypes.c_void_p), ("tasks", ctypes.c_void_p),
+                ("task_rows", ctypes.c_void_p), ("col", ctypes.c_void_p),
+                ("weight", ctypes.c_void_p), ("scale_pairs", ctypes.c_void_p),
+                ("global_scale", ctypes.c_void_p)]
 
 
 class EventCounters(ctypes.Structure):
@@ -96,7 +97,8 @@ class EventCounters(ctypes.Structure):
 
 EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_dendritic_event_workspace_size", "nsb_dendritic_event",
-                    "nsb_tiled_smem_bytes", "nsb_dendritic_step_tiled", "nsb_tiled_propagate",
+                    "nsb_tiled_smem_bytes", "nsb_tiled_workspace_size", "nsb_dendritic_step_tiled",
+                    "nsb_dendritic_run_tiled", "nsb_tiled_propagate",
                     "nsb_dendritic_event_noalloc", "nsb_dendritic_step_rows",
                     "nsb_last_error", "nsb_abi_version")
 
@@ -119,14 +121,21 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_dendritic_event.argtypes = [p(_Tick), ctypes.c_void_p, p(_View), ctypes.c_void_p,
                                         ctypes.c_int64, p(_OutCsr), p(_TickOut), p(_Out),
                                         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
-    lib.nsb_tiled_smem_bytes.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
+    lib.nsb_tiled_smem_bytes.argtypes = [ctypes.c_int32, ctypes.c_int32]
     lib.nsb_tiled_smem_bytes.restype = ctypes.c_size_t
+    lib.nsb_tiled_workspace_size.argtypes = [p(_TiledLayout)]
+    lib.nsb_tiled_workspace_size.restype = ctypes.c_size_t
     lib.nsb_dendritic_step_tiled.argtypes = [p(_Tick), p(_TiledLayout), ctypes.c_void_p,
-                                             p(_TickOut), ctypes.c_void_p, ctypes.c_void_p]
+                                             p(_TickOut), ctypes.c_void_p, ctypes.c_size_t,
+                                             ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_dendritic_run_tiled.argtypes = [p(_Tick), p(_TiledLayout), ctypes.c_int64,
+                                            p(_TickOut), ctypes.c_void_p, ctypes.c_size_t,
+                                            ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_dendritic_step_rows.argtypes = [p(_Tick), p(_Csr), p(_View), ctypes.c_int64,
                                             ctypes.c_int32, p(_TickOut), ctypes.c_void_p]
     lib.nsb_tiled_propagate.argtypes = [ctypes.c_int64, p(_TiledLayout), ctypes.c_void_p,
-                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                        ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_dendritic_event_noalloc.argtypes = [p(_Tick), ctypes.c_void_p, p(_View),
                                                 ctypes.c_void_p, ctypes.c_int64, p(_OutCsr),
                                                 p(_TickOut), p(_Out), ctypes.c_void_p]
@@ -134,7 +143,7 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
         getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
-    if lib.nsb_abi_version() != 1:
+    if lib.nsb_abi_version() != 3:
         raise RuntimeError("libneurosim_b200.so ABI version mismatch")
     return lib
 
@@ -299,11 +308,15 @@ class DendriticExtension:
 
     def prepare_step_tiled(self, state, dendrite, adaptation, params, layout, input,
                            input_scalar, dendritic_input, dendritic_scalar, *, out, status=None,
-                           source=None):
+                           source=None, ticks=None):
         """Like :meth:`prepare_step` for B = 1 over a :class:`~neurosim_gpu_b200.tiled.TiledLayout`.
 
         ``source`` (optional) is the full gathered state of ``layout.cols``
         floats when ``state`` holds only this layout's rows (row sharding).
+        With ``ticks`` = T the launch runs T ticks in one cooperative kernel
+        (``nsb_dendritic_run_tiled``): the first reads ``state`` / ``dendrite``
+        / ``adaptation``, the later ones update ``out`` in place.  The launch
+        uses the layout's own workspace (:meth:`TiledLayout.workspace`).
         """
         _check_state(state)
         _check(state.size(0) == 1, "the tiled tick takes B = 1")
@@ -312,6 +325,7 @@ class DendriticExtension:
                and gather.data_ptr() % 16 == 0 and gather.numel() == layout.cols,
                "the tiled tick needs a contiguous, 16-byte aligned state")
         _check(layout.neurons == state.size(1), "layout and state neuron counts differ")
+        _check(ticks is None or source is None, "multi-tick runs gather from their own state")
         tick = _tick(state, dendrite, adaptation, params, input, input_scalar,
                      dendritic_input, dendritic_scalar)
         for view in out:
@@ -319,18 +333,26 @@ class DendriticExtension:
             _check(view.shape == state.shape, "output shape mismatch")
         result = _TickOut(_out(out[0]), _out(out[1]), _out(out[2]))
         c_layout = layout.c_struct()
+        workspace = layout.workspace()
         status_ptr = status.data_ptr() if status is not None else None
         source_ptr = source.data_ptr() if source is not None else None
         lib, device = self.lib, state.device
         keep = (state, dendrite, adaptation, params, layout, input, dendritic_input, out, status,
-                source)
+                source, workspace)
 
         def launch() -> None:
             assert keep is not None
             with torch.cuda.device(device):
-                code = lib.nsb_dendritic_step_tiled(ctypes.byref(tick), ctypes.byref(c_layout),
-                                                    source_ptr, ctypes.byref(result), status_ptr,
-                                                    _stream(device))
+                if ticks is None:
+                    code = lib.nsb_dendritic_step_tiled(
+                        ctypes.byref(tick), ctypes.byref(c_layout), source_ptr,
+                        ctypes.byref(result), workspace.data_ptr(), workspace.numel(), status_ptr,
+                        _stream(device))
+                else:
+                    code = lib.nsb_dendritic_run_tiled(
+                        ctypes.byref(tick), ctypes.byref(c_layout), int(ticks),
+                        ctypes.byref(result), workspace.data_ptr(), workspace.numel(), status_ptr,
+                        _stream(device))
             _raise_on_status(lib, code)
 
         return launch
@@ -387,9 +409,11 @@ class DendriticExtension:
                "the tiled product needs a contiguous, 16-byte aligned [1,N] source")
         result = torch.empty_like(x, memory_format=torch.contiguous_format)
         c_layout = layout.c_struct()
+        workspace = layout.workspace()
         with torch.cuda.device(x.device):
             code = self.lib.nsb_tiled_propagate(x.size(1), ctypes.byref(c_layout), x.data_ptr(),
-                                                result.data_ptr(),
+                                                result.data_ptr(), workspace.data_ptr(),
+                                                workspace.numel(),
                                                 status.data_ptr() if status is not None else None,
                                                 _stream(x.device))
         _raise_on_status(self.lib, code)

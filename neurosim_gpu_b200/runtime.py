@@ -300,11 +300,13 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
             dendritic_drive: torch.Tensor | float = 0.0, graph_ticks: int = 64) -> torch.Tensor:
         """Advance ``ticks`` ticks with fixed drives; returns the final state.
 
-        The native tick is captured once into a CUDA graph of ``graph_ticks``
-        ticks over two resident state buffers and replayed, so the host issues
-        one launch per ``graph_ticks`` ticks.  Tensor drives are read at replay
-        time (their values may change between calls, their storage may not).
-        Results equal ``ticks`` calls of :meth:`step`.
+        On the tiled path (B = 1) one persistent cooperative launch runs all
+        ``ticks`` ticks.  Otherwise the native tick is captured once into a CUDA
+        graph of ``graph_ticks`` ticks over two resident state buffers and
+        replayed, so the host issues one launch per ``graph_ticks`` ticks;
+        tensor drives are read at replay time (their values may change between
+        calls, their storage may not).  Results equal ``ticks`` calls of
+        :meth:`step`.
         """
         if ticks < 0:
             raise ValueError("ticks must be non-negative")
@@ -315,7 +317,19 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         u, us = self._drive(drive)
         v, vs = self._drive(dendritic_drive, "dendritic_drive")
         weight, _, _, backend = self._weights()
-        self._tiled_layout()  # build outside any capture
+        layout = self._tiled_layout()  # build outside any capture
+        if layout is not None:
+            # One cooperative launch runs every tick (a persistent kernel).
+            s = self.state
+            if s.stride(1) != 1 or s.data_ptr() % 16:
+                s = s.contiguous().clone()
+            _, views = _native._outputs(3, s)
+            self.extension.prepare_step_tiled(s, self.dendritic_state, self.adaptation_state,
+                                              self._parameters(), layout, u, us, v, vs,
+                                              out=views, status=self._status, ticks=ticks)()
+            self.state, self.dendritic_state, self.adaptation_state = views
+            self.last_backend = backend
+            return self.state
         graph_ticks = max(1, min(graph_ticks, ticks))
         key = (graph_ticks, tuple(self.state.shape),
                None if u is None else (u.data_ptr(), u.stride()), us,

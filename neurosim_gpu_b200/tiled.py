@@ -2,37 +2,70 @@
 
 The layout re-arranges the edges of ``W[dst, src]`` (``in_rowptr``, ``in_col``
 and the weights in any storage format) so that the tick kernel
-(``nsb_dendritic_step_tiled``) can keep the gathered source state in shared
-memory:
+(``nsb_dendritic_step_tiled``) keeps the gathered source state in shared memory
+and streams the edges with vector loads:
 
-* CTA ``c`` (one per SM) owns destination rows ``[row_begin[c], row_begin[c+1])``,
-  cut so every CTA holds about the same number of edges plus rows.
-* Columns are split into ``blocks`` blocks of ``block_cols`` columns; one block
-  of the state fits in shared memory (two when ``buffers == 2``).
-* For each CTA and block, the rows' pieces (their edges inside the block, a
-  contiguous run of the original CSR row) are sorted by length and grouped 32 at
-  a time into tasks.  In a task, lane ``i`` owns one row and its ``j``-th edge
-  sits at slot ``task_offset + 32 j + i``: a warp's load covers 32 consecutive
-  slots.  Shorter pieces are padded to the task length with column
-  ``block_cols`` (a zero in shared memory) and weight 0.
+* The gathered columns are split into ``blocks`` blocks of ``block_cols``
+  columns, each small enough to sit in one CTA's shared memory.
+* A *stage* is one column block and a contiguous range of destination rows.
+  When there are at least as many CTAs as blocks, every CTA runs exactly one
+  stage: block ``k`` gets a share of the CTAs proportional to its edges, and
+  its rows are cut into that many ranges of about equal edge count.  The state
+  block is then staged once per tick.  (With more blocks than CTAs, CTA ``c``
+  runs the full-row stages of blocks ``c, c + ctas, ...``, double-buffered.)
+* For each stage, the rows' non-empty pieces (their edges inside the block, a
+  contiguous run of the original CSR row) are sorted by length and grouped 32
+  at a time into tasks.  A task has ``chunks`` chunks; lane ``i`` owns one row
+  and its edge ``j`` sits at slot ``first + 128 * (j // 4) + 4 * i + j % 4``,
+  so one lane reads four edges with one vector load and a warp's loads cover
+  128 consecutive slots.  Shorter pieces are padded with column ``block_cols``
+  (a zero in shared memory) and weight 0.
+* Columns are stored relative to their block as uint16 (2 bytes per edge
+  instead of the CSR's 4).
+* The per-(row, block) sums go to a workspace array ``part[block][row]``; after
+  a grid-wide barrier every CTA adds the sums of its share of the rows in block
+  order and applies the pointwise update.
+* NVFP4: codes are re-packed two per byte by slot.  Each task carries a table
+  of uint16 scale pairs (for lane ``i`` and row ``b``: the E4M3 scales of CSR
+  blocks ``o_i // 16 + b`` and ``+ b + 1``, ``o_i`` the CSR position of the
+  lane's first edge), and bits 28..31 of the lane's ``task_rows`` word hold
+  ``o_i % 16``, so the kernel applies the scale of each edge's ORIGINAL
+  16-edge block (``precision.py:52-73`` blocks the destination-major CSR).
 
-Edge order inside a row piece is the CSR order, so the sums equal a
-sequential dot product per (row, block) followed by a sum over blocks.
-The builder runs on the weights' device with PyTorch ops; it is cached by the
-runtime per ``weight_version``.
+Edge order inside a row piece is the CSR order, so a row's sum is a sequential
+dot product per (row, block) followed by a sum over blocks in block order; the
+column blocks depend only on the gathered length, so a row-sharded graph gives
+bit-identical sums.  The builder runs on the weights' device with PyTorch ops;
+it is cached by the runtime per ``weight_version``.
 """
 
 from __future__ import annotations
 
 import ctypes
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import torch
 
 from . import native
 
 LANES = 32
-MAX_CTA_ROWS = 32767  # row ids are int16 inside a CTA
+CHUNK = 4                     # slots of one lane per vector load
+CHUNK_SLOTS = LANES * CHUNK   # slots of one warp-wide chunk
+MAX_BLOCK_COLS = 65504        # 16-bit block-relative columns, block_cols = padding
+MAX_ROWS = (1 << 28) - 1      # 28-bit rows in task_rows; ROW_NONE marks a padding lane
+ROW_NONE = MAX_ROWS
+
+
+def _u16(values: torch.Tensor) -> torch.Tensor:
+    """Integers in [0, 65535] as the bit patterns of an int16 tensor (uint16 storage)."""
+    values = values.to(torch.int32)
+    return torch.where(values >= 32768, values - 65536, values).to(torch.int16)
+
+
+def _i32(values: torch.Tensor) -> torch.Tensor:
+    """Integers in [0, 2^32) as the bit patterns of an int32 tensor."""
+    values = values.to(torch.int64)
+    return torch.where(values >= 2**31, values - 2**32, values).to(torch.int32)
 
 
 @dataclass
@@ -43,27 +76,37 @@ class TiledLayout:
     blocks: int
     block_cols: int
     buffers: int
-    max_rows: int
     format: int
-    row_begin: torch.Tensor
-    task_ptr: torch.Tensor
-    task_offset: torch.Tensor
-    task_len: torch.Tensor
-    task_rows: torch.Tensor
-    task_orig: torch.Tensor | None
-    col: torch.Tensor
-    weight: torch.Tensor
-    block_scales: torch.Tensor | None
+    stage_ptr: torch.Tensor    # int32 [ctas+1]: stages of CTA c
+    stage_block: torch.Tensor  # int32 [stages]: column block of each stage
+    task_ptr: torch.Tensor     # int32 [ctas+1]: tasks of CTA c
+    tasks: torch.Tensor        # int32 [T, 4]: first slot, chunks, stage (CTA-local), first scale pair
+    task_rows: torch.Tensor    # int32 [T, 32]: row | phase << 28 (row ROW_NONE: padding lane)
+    col: torch.Tensor          # int16 storage of uint16 [S]
+    weight: torch.Tensor       # [S] in the storage format (NVFP4: uint8 [S/2])
+    scale_pairs: torch.Tensor | None  # int16 storage of uint16 (NVFP4)
     global_scale: torch.Tensor | None
     cols: int = 0         # length of the gathered source vector (0: same as neurons)
+    _workspace: torch.Tensor | None = field(default=None, repr=False)
 
     def __post_init__(self) -> None:
         if self.cols == 0:
             self.cols = self.neurons
 
+    def workspace(self) -> torch.Tensor:
+        """The layout's device workspace (zero-filled on first use; calls keep it zeroed)."""
+        if self._workspace is None:
+            self._workspace = torch.zeros(self.workspace_bytes(), dtype=torch.uint8,
+                                          device=self.col.device)
+        return self._workspace
+
     @property
     def n_tasks(self) -> int:
-        return self.task_len.numel()
+        return self.tasks.shape[0]
+
+    @property
+    def n_stages(self) -> int:
+        return self.stage_block.numel()
 
     @property
     def n_slots(self) -> int:
@@ -76,47 +119,85 @@ class TiledLayout:
     def stream_bytes(self) -> int:
         """Bytes one tick streams from this layout (indices, weights, task tables)."""
         tables = sum(t.numel() * t.element_size() for t in (
-            self.row_begin, self.task_ptr, self.task_offset, self.task_len, self.task_rows))
-        if self.task_orig is not None:
-            tables += self.task_orig.numel() * 4
-        return self.col.numel() * 4 + self.weight.numel() * self.weight.element_size() + tables
+            self.stage_ptr, self.stage_block, self.task_ptr, self.tasks, self.task_rows))
+        if self.scale_pairs is not None:
+            tables += self.scale_pairs.numel() * 2
+        return self.col.numel() * 2 + self.weight.numel() * self.weight.element_size() + tables
+
+    def workspace_bytes(self) -> int:
+        """Device workspace one launch needs (barrier words + per-block row sums)."""
+        return 256 + self.blocks * self.neurons * 4
 
     def c_struct(self) -> "native._TiledLayout":
         def ptr(t):
             return t.data_ptr() if t is not None and t.numel() else None
         return native._TiledLayout(
-            self.ctas, self.blocks, self.block_cols, self.buffers, self.max_rows, self.format,
-            self.n_tasks, self.n_slots,
-            self.block_scales.numel() if self.block_scales is not None else 0, self.cols,
-            ptr(self.row_begin), ptr(self.task_ptr), ptr(self.task_offset), ptr(self.task_len),
-            ptr(self.task_rows), ptr(self.task_orig), ptr(self.col), ptr(self.weight),
-            ptr(self.block_scales), ptr(self.global_scale))
+            self.ctas, self.blocks, self.block_cols, self.buffers, self.format, 0,
+            self.n_stages, self.n_tasks, self.n_slots,
+            self.scale_pairs.numel() if self.scale_pairs is not None else 0,
+            self.neurons, self.cols,
+            ptr(self.stage_ptr), ptr(self.stage_block), ptr(self.task_ptr), ptr(self.tasks),
+            ptr(self.task_rows), ptr(self.col), ptr(self.weight), ptr(self.scale_pairs),
+            ptr(self.global_scale))
 
 
-def plan_blocks(neurons: int, max_rows: int, smem_limit: int, smem_bytes) -> tuple[int, int, int]:
-    """(blocks, block_cols, buffers) that fit one CTA's shared memory."""
-    whole = -(-neurons // 4) * 4
-    if smem_bytes(whole, max_rows, 1) <= smem_limit:
-        return 1, whole, 1
-    per_buffer = (smem_limit - smem_bytes(0, max_rows, 2)) // 8 - 4
-    cap = (per_buffer // LANES) * LANES
-    if cap < LANES:
-        raise ValueError("shared memory too small for a tiled layout")
-    blocks = -(-neurons // cap)
-    block_cols = -(-(-(-neurons // blocks)) // LANES) * LANES
-    return blocks, block_cols, 2
+def plan_blocks(cols: int, ctas: int, smem_limit: int, smem_bytes) -> tuple[int, int, int]:
+    """(blocks, block_cols, buffers) that fit one CTA's shared memory.
+
+    Blocks are as large as one buffer allows when every CTA can hold a single
+    block; with more blocks than CTAs, two half-size buffers pipeline a CTA's
+    stages.
+    """
+    def cap(buffers: int) -> int:
+        per_buffer = (smem_limit - smem_bytes(0, buffers)) // (4 * buffers) - 4
+        return (min(per_buffer, MAX_BLOCK_COLS) // LANES) * LANES
+
+    for buffers in (1, 2):
+        width = cap(buffers)
+        if width < LANES:
+            raise ValueError("shared memory too small for a tiled layout")
+        blocks = -(-cols // width)
+        if blocks <= ctas or buffers == 2:
+            block_cols = -(-(-(-cols // blocks)) // LANES) * LANES
+            return blocks, block_cols, buffers
+    raise AssertionError("unreachable")
 
 
-def cta_row_ranges(rowptr: torch.Tensor, ctas: int) -> torch.Tensor:
-    """Row boundaries that give every CTA about (edges + rows) / ctas work."""
-    n = rowptr.numel() - 1
-    cost = rowptr.long() + torch.arange(n + 1, device=rowptr.device)
-    total = int(cost[-1])
-    targets = torch.arange(ctas + 1, device=rowptr.device, dtype=torch.int64) * total // ctas
-    begin = torch.searchsorted(cost, targets)
-    begin[0] = 0
-    begin[-1] = n
-    return torch.cummax(begin, 0).values
+def _apportion(weights: torch.Tensor, total: int) -> torch.Tensor:
+    """Integer shares >= 1 of ``total`` proportional to ``weights`` (largest remainder)."""
+    k = weights.numel()
+    w = weights.double().clamp(min=1e-9)
+    extra = total - k
+    raw = w / w.sum() * extra
+    share = raw.floor().long()
+    left = extra - int(share.sum())
+    if left > 0:
+        share[torch.argsort(raw - share, descending=True, stable=True)[:left]] += 1
+    return share + 1
+
+
+def _stages(piece_len: torch.Tensor, ctas: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(stage_cta, stage_block, stage_of_piece [n, blocks]) with stages sorted by CTA."""
+    n, blocks = piece_len.shape
+    device = piece_len.device
+    if blocks > ctas:
+        stage_block = torch.argsort(torch.arange(blocks, device=device) % ctas, stable=True)
+        stage_cta = stage_block % ctas
+        stage_of_block = torch.empty_like(stage_block)
+        stage_of_block[stage_block] = torch.arange(blocks, device=device)
+        return stage_cta, stage_block, stage_of_block.expand(n, blocks)
+    cost = piece_len.long() + 1                      # edges + a row's own overhead
+    share = _apportion(cost.sum(0), ctas)
+    first = torch.cumsum(share, 0) - share
+    stage_of = torch.empty((n, blocks), dtype=torch.int64, device=device)
+    for k in range(blocks):
+        before = torch.cumsum(cost[:, k], 0) - cost[:, k]   # cost of the rows above row r
+        r = int(share[k])
+        cuts = torch.arange(1, r, device=device) * int(cost[:, k].sum()) // r
+        stage_of[:, k] = int(first[k]) + torch.searchsorted(cuts, before, right=True)
+    stage_block = torch.repeat_interleave(torch.arange(blocks, device=device), share)
+    stage_cta = torch.arange(ctas, device=device)
+    return stage_cta, stage_block, stage_of
 
 
 def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: torch.Tensor,
@@ -130,14 +211,18 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
     destination rows (``in_rowptr`` has neurons + 1 entries, starting at 0);
     ``cols`` is the length of the gathered source (default: ``neurons``).  For a
     block of rows cut out of a larger NVFP4 CSR, ``scale_offset`` is the CSR
-    position of the block's first edge (it selects the original block scales).
+    position of the block's first edge (it selects the original block scales,
+    ``block_scales`` being those of the whole CSR).  ``ctas`` must not exceed
+    the device's SM count (the kernel is a cooperative launch).
     """
     device = in_col.device
     if smem_bytes is None:
         lib = native.load_library()
-        smem_bytes = lambda cols, rows, bufs: int(lib.nsb_tiled_smem_bytes(cols, rows, bufs))  # noqa: E731
+        smem_bytes = lambda cols, bufs: int(lib.nsb_tiled_smem_bytes(cols, bufs))  # noqa: E731
     n, m = neurons, in_col.numel()
     cols = n if cols is None else cols
+    if n > MAX_ROWS - 1:
+        raise ValueError("too many rows for the tiled layout")
     if block_scales is not None:
         fmt = native.NVFP4
     elif weight.dtype == torch.uint8:
@@ -146,125 +231,152 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
         fmt = native.F16
     else:
         fmt = native.F32
-    rowptr = in_rowptr.to(torch.int64)
-    row_begin = cta_row_ranges(rowptr, ctas)
-    rows_per_cta = row_begin[1:] - row_begin[:-1]
-    max_rows = int(rows_per_cta.max())
-    if max_rows > MAX_CTA_ROWS:
-        raise ValueError("too many rows per CTA for the tiled layout")
-    blocks, block_cols, buffers = plan_blocks(cols, max_rows, smem_limit, smem_bytes)
+    blocks, block_cols, buffers = plan_blocks(cols, ctas, smem_limit, smem_bytes)
 
+    arange = lambda k: torch.arange(k, device=device)  # noqa: E731
+    rowptr = in_rowptr.to(torch.int64)
     degree = rowptr[1:] - rowptr[:-1]
-    row_of_edge = torch.repeat_interleave(torch.arange(n, device=device), degree)
+    row_of_edge = torch.repeat_interleave(arange(n), degree)
     col64 = in_col.to(torch.int64)
     block_of_edge = col64 // block_cols
     piece = row_of_edge * blocks + block_of_edge                       # (row, block) pair id
     piece_len = torch.bincount(piece, minlength=n * blocks).view(n, blocks)
-    piece_start = rowptr[:-1, None] + torch.cumsum(piece_len, 1) - piece_len
+    piece_start = (rowptr[:-1, None] + torch.cumsum(piece_len, 1) - piece_len).flatten()
 
-    # Sort (row, block) pairs by (CTA, block), then by piece length (longest first).
-    cta_of_row = torch.searchsorted(row_begin, torch.arange(n, device=device), right=True) - 1
-    group = (cta_of_row[:, None] * blocks + torch.arange(blocks, device=device)).flatten()
+    stage_cta, stage_block, stage_of = _stages(piece_len, ctas)
+    n_stages = stage_block.numel()
+    stage_ptr = torch.zeros(ctas + 1, dtype=torch.int64, device=device)
+    torch.cumsum(torch.bincount(stage_cta, minlength=ctas), 0, out=stage_ptr[1:])
+
+    # Non-empty pieces sorted by stage, then by length (longest first).
+    group = stage_of.flatten()
     lengths = piece_len.flatten()
-    order = torch.sort(-lengths, stable=True).indices
+    order = torch.nonzero(lengths).flatten()
+    order = order[torch.sort(-lengths[order], stable=True).indices]
     order = order[torch.sort(group[order], stable=True).indices]
     sorted_group = group[order]
-    group_size = torch.bincount(sorted_group, minlength=ctas * blocks)
+    group_size = torch.bincount(sorted_group, minlength=n_stages)
     group_start = torch.cumsum(group_size, 0) - group_size
-    position = torch.arange(order.numel(), device=device) - group_start[sorted_group]
-    tasks_per_group = (group_size + LANES - 1) // LANES
-    task_ptr = torch.zeros(ctas * blocks + 1, dtype=torch.int64, device=device)
-    torch.cumsum(tasks_per_group, 0, out=task_ptr[1:])
-    pair_task = task_ptr[sorted_group] + position // LANES
+    position = arange(order.numel()) - group_start[sorted_group]
+    tasks_per_stage = (group_size + LANES - 1) // LANES
+    stage_task = torch.cumsum(tasks_per_stage, 0) - tasks_per_stage
+    pair_task = stage_task[sorted_group] + position // LANES
     pair_lane = position % LANES
-    n_tasks = int(task_ptr[-1])
+    n_tasks = int(tasks_per_stage.sum())
+    task_ptr = torch.zeros(ctas + 1, dtype=torch.int64, device=device)
+    tasks_per_cta = torch.zeros(ctas, dtype=torch.int64, device=device)
+    tasks_per_cta.index_add_(0, stage_cta, tasks_per_stage)
+    torch.cumsum(tasks_per_cta, 0, out=task_ptr[1:])
     task_len = torch.zeros(n_tasks, dtype=torch.int64, device=device)
     task_len.scatter_reduce_(0, pair_task, lengths[order], reduce="amax")
-    task_offset = torch.cumsum(task_len * LANES, 0) - task_len * LANES
-    slots = int((task_len * LANES).sum())
+    task_chunks = (task_len + CHUNK - 1) // CHUNK
+    task_first = torch.cumsum(task_chunks * CHUNK_SLOTS, 0) - task_chunks * CHUNK_SLOTS
+    slots = int((task_chunks * CHUNK_SLOTS).sum())
     if slots >= 2**31:
         raise ValueError("tiled layout exceeds 2^31 slots")
+    task_stage = torch.repeat_interleave(arange(n_stages), tasks_per_stage)
+    task_stage_local = task_stage - stage_ptr[stage_cta[task_stage]]
     pair_row = order // blocks
-    task_rows = torch.full((n_tasks, LANES), -1, dtype=torch.int16, device=device)
-    task_rows[pair_task, pair_lane] = (pair_row - row_begin[cta_of_row[pair_row]]).to(torch.int16)
 
     # Slot of every edge: its pair's task and lane, and its rank inside the piece.
-    rank_of_pair = torch.empty_like(order)
-    rank_of_pair[order] = torch.arange(order.numel(), device=device)
+    rank_of_pair = torch.full((n * blocks,), -1, dtype=torch.int64, device=device)
+    rank_of_pair[order] = arange(order.numel())
     r = rank_of_pair[piece]
-    within = torch.arange(m, device=device) - piece_start.flatten()[piece]
-    slot = task_offset[pair_task[r]] + within * LANES + pair_lane[r]
-    col = torch.full((slots,), block_cols, dtype=torch.int32, device=device)
-    col[slot] = (col64 - block_of_edge * block_cols).to(torch.int32)
+    within = arange(m) - piece_start[piece]
+    slot = (task_first[pair_task[r]] + (within // CHUNK) * CHUNK_SLOTS + pair_lane[r] * CHUNK
+            + within % CHUNK)
+    col = torch.full((slots,), block_cols, dtype=torch.int64, device=device)
+    col[slot] = col64 - block_of_edge * block_cols
 
-    task_orig = None
+    task_rows = torch.full((n_tasks, LANES), ROW_NONE, dtype=torch.int64, device=device)
+    scale_first = torch.zeros(n_tasks, dtype=torch.int64, device=device)
+    scale_pairs = None
     if fmt == native.NVFP4:
+        orig = piece_start[order] + scale_offset          # CSR position of each piece's first edge
+        task_rows[pair_task, pair_lane] = pair_row | ((orig % 16) << 28)
         nibbles = torch.stack((weight & 15, weight >> 4), dim=1).flatten()[:m]
         codes = torch.zeros(slots, dtype=torch.uint8, device=device)
         codes[slot] = nibbles
         tiled_weight = (codes[0::2] | (codes[1::2] << 4)).contiguous()
-        task_orig = torch.zeros((n_tasks, LANES), dtype=torch.int32, device=device)
-        task_orig[pair_task, pair_lane] = (piece_start.flatten()[order] + scale_offset).to(torch.int32)
+        # Chunk c of a lane with phase p reads pair row (p + 4c) // 16 <= (11 + 4C) // 16.
+        table_rows = ((11 + CHUNK * task_chunks) >> 4) + 1
+        entries = table_rows * LANES
+        scale_first = torch.cumsum(entries, 0) - entries
+        n_pairs = int(entries.sum())
+        # Blocks past a lane's last edge (its padding slots) get scale 0, so a
+        # padding code (+0) never meets a neighbouring block's NaN scale.
+        base = torch.zeros((n_tasks, LANES), dtype=torch.int64, device=device)
+        base[pair_task, pair_lane] = orig // 16
+        final = torch.full((n_tasks, LANES), -1, dtype=torch.int64, device=device)
+        final[pair_task, pair_lane] = (orig + lengths[order] - 1) // 16
+        task_of_entry = torch.repeat_interleave(arange(n_tasks), entries)
+        local = arange(n_pairs) - scale_first[task_of_entry]
+        lane_of_entry = local % LANES
+        block = base[task_of_entry, lane_of_entry] + local // LANES
+        final_of_entry = final[task_of_entry, lane_of_entry]
+        last = block_scales.numel() - 1
+        lo = torch.where(block <= final_of_entry, block_scales[block.clamp(max=last)], 0)
+        hi = torch.where(block + 1 <= final_of_entry, block_scales[(block + 1).clamp(max=last)], 0)
+        scale_pairs = _u16(lo.to(torch.int32) | (hi.to(torch.int32) << 8))
     else:
+        task_rows[pair_task, pair_lane] = pair_row
         tiled_weight = torch.zeros(slots, dtype=weight.dtype, device=device)
         tiled_weight[slot] = weight
+    tasks = torch.stack((task_first, task_chunks, task_stage_local, scale_first), dim=1)
     return TiledLayout(
         neurons=n, n_edges=m, ctas=ctas, blocks=blocks, block_cols=block_cols, buffers=buffers,
-        max_rows=max_rows, format=fmt, row_begin=row_begin.to(torch.int32),
-        task_ptr=task_ptr.to(torch.int32), task_offset=task_offset.to(torch.int32),
-        task_len=task_len.to(torch.int32), task_rows=task_rows.contiguous(), task_orig=task_orig,
-        col=col, weight=tiled_weight, block_scales=block_scales, global_scale=global_scale,
-        cols=cols)
+        format=fmt, stage_ptr=stage_ptr.to(torch.int32), stage_block=stage_block.to(torch.int32),
+        task_ptr=task_ptr.to(torch.int32), tasks=tasks.to(torch.int32).contiguous(),
+        task_rows=_i32(task_rows).contiguous(), col=_u16(col), weight=tiled_weight,
+        scale_pairs=scale_pairs, global_scale=global_scale, cols=cols)
 
 
 def emulate(layout: TiledLayout, source: torch.Tensor) -> torch.Tensor:
     """What the kernel computes, j = W @ source (B = 1), in float64 on any device.
 
-    Used by the tests to check a layout without a GPU.
+    Every slot is decoded the way the kernel decodes it (including the NVFP4
+    scale-pair lookup); used by the tests to check a layout without a GPU.
     """
     x = source.reshape(-1).double()
-    out = torch.zeros(layout.neurons, dtype=torch.float64, device=x.device)
-    w = _decoded_slots(layout).double()
-    blocks_of_task = torch.repeat_interleave(
-        torch.arange(layout.ctas * layout.blocks, device=x.device),
-        (layout.task_ptr[1:] - layout.task_ptr[:-1]).long())
-    cta = blocks_of_task // layout.blocks
-    block = blocks_of_task % layout.blocks
-    out = torch.zeros(layout.neurons, dtype=torch.float64, device=x.device)
+    dev = x.device
+    out = torch.zeros(layout.neurons, dtype=torch.float64, device=dev)
+    if layout.n_slots == 0:
+        return out
+    slots = torch.arange(layout.n_slots, device=dev)
+    first = layout.tasks[:, 0].long()
+    task = torch.searchsorted(first, slots, right=True) - 1
+    local = slots - first[task]
+    chunk, lane, e = local // CHUNK_SLOTS, (local % CHUNK_SLOTS) // CHUNK, local % CHUNK
+    word = layout.task_rows.long()[task, lane] & 0xFFFFFFFF
+    col = layout.col.long() & 0xFFFF
+    cta = torch.searchsorted(layout.task_ptr.long(), torch.arange(layout.n_tasks, device=dev),
+                             right=True) - 1
+    stage = layout.stage_ptr.long()[cta] + layout.tasks[:, 2].long()
+    block = layout.stage_block.long()[stage][task]
     padded = torch.cat([x, torch.zeros(layout.blocks * layout.block_cols + 1 - x.numel(),
-                                       dtype=x.dtype, device=x.device)])
-    for q in range(layout.n_tasks):
-        length = int(layout.task_len[q])
-        if length == 0:
-            continue
-        base = int(layout.task_offset[q])
-        cols = layout.col[base: base + length * LANES].view(length, LANES).long()
-        vals = w[base: base + length * LANES].view(length, LANES)
-        start = int(block[q]) * layout.block_cols
-        gathered = torch.where(cols == layout.block_cols, torch.zeros_like(vals),
-                               padded[(start + cols).clamp(max=padded.numel() - 1)])
-        dots = (vals * gathered).sum(0)
-        rows = layout.task_rows[q].long()
-        keep = rows >= 0
-        out[(int(layout.row_begin[cta[q]]) + rows[keep])] += dots[keep]
+                                       dtype=x.dtype, device=dev)])
+    gathered = torch.where(col == layout.block_cols, torch.zeros_like(x[:1]),
+                           padded[block * layout.block_cols + col.clamp(max=layout.block_cols - 1)])
+    value = _decoded_slots(layout, task, chunk, lane, e, word).double() * gathered
+    row = word & MAX_ROWS
+    keep = row != ROW_NONE
+    out.index_add_(0, row[keep], value[keep])
     return out
 
 
-def _decoded_slots(layout: TiledLayout) -> torch.Tensor:
+def _decoded_slots(layout: TiledLayout, task, chunk, lane, e, word) -> torch.Tensor:
     if layout.format == native.F32 or layout.format == native.F16:
         return layout.weight.float()
-    from .precision import e4m3_to_float, e2m1_to_float
+    from .precision import e2m1_to_float, e4m3_to_float
+    g = layout.global_scale.float()
     if layout.format == native.E4M3:
-        return e4m3_to_float(layout.weight) * layout.global_scale.float()
+        return e4m3_to_float(layout.weight) * g
     codes = torch.stack((layout.weight & 15, layout.weight >> 4), dim=1).flatten()
-    slots = torch.arange(codes.numel(), device=codes.device)
-    task = torch.searchsorted(layout.task_offset.long(), slots, right=True) - 1
-    j = (slots - layout.task_offset.long()[task]) // LANES
-    lane = slots % LANES
-    orig = layout.task_orig.long()[task, lane] + j
-    block = orig.clamp(max=layout.block_scales.numel() * 16 - 1) // 16
-    factor = e4m3_to_float(layout.block_scales[block]) * layout.global_scale.float()
-    return e2m1_to_float(codes) * factor
+    p = (word >> 28) + CHUNK * chunk
+    entry = layout.tasks[:, 3].long()[task] + (p >> 4) * LANES + lane
+    pair = layout.scale_pairs.long()[entry] & 0xFFFF
+    scale = torch.where((p & 15) + e >= 16, pair >> 8, pair & 0xFF).to(torch.uint8)
+    return e2m1_to_float(codes) * (e4m3_to_float(scale) * g)
 
 
 def smem_limit(device: torch.device) -> int:

@@ -25,12 +25,14 @@ def _packed(graph, fmt):
 
 def _smem_bytes():
     lib = native.load_library()
-    return lambda cols, rows, bufs: int(lib.nsb_tiled_smem_bytes(cols, rows, bufs))
+    return lambda cols, bufs: int(lib.nsb_tiled_smem_bytes(cols, bufs))
 
 
 @pytest.mark.parametrize("fmt", ["fp32", "fp16", "fp8", "nvfp4"])
 @pytest.mark.parametrize("n,m,ctas,smem", [(97, 600, 4, 232448), (2000, 60000, 8, 8000),
-                                           (5000, 100000, 16, 6000), (3001, 40001, 5, 232448)])
+                                           (5000, 100000, 16, 6000), (3001, 40001, 5, 232448),
+                                           (5000, 100000, 2, 6000), (1, 0, 3, 232448),
+                                           (300, 9000, 148, 232448)])
 def test_layout_emulation_matches_oracle_cpu(fmt, n, m, ctas, smem):
     """The layout builder alone, emulated on CPU (no GPU needed)."""
     graph = random_topology(n, m, device="cpu", seed=3)
@@ -48,7 +50,7 @@ def test_layout_emulation_matches_oracle_cpu(fmt, n, m, ctas, smem):
 @pytest.mark.parametrize("fmt", ["fp32", "fp16", "fp8", "nvfp4"])
 @pytest.mark.parametrize("n,m,ctas,smem", [(97, 600, 4, 232448), (2000, 60000, 8, 8000),
                                            (5000, 100000, 16, 6000), (3001, 40001, 5, 232448),
-                                           (20000, 400000, 148, 24000)])
+                                           (20000, 400000, 148, 24000), (5000, 100000, 2, 6000)])
 def test_tiled_tick_matches_oracle(fmt, n, m, ctas, smem):
     ext = load_native_extension()
     graph = random_topology(n, m, device="cpu", seed=3).to("cuda")
@@ -110,3 +112,64 @@ def test_tiled_rejects_bad_inputs():
     with pytest.raises(RuntimeError, match="aligned"):
         odd = torch.zeros(1, 501, device="cuda")[:, 1:]
         ext.dendritic_step_tiled(odd, one, one, model.parameters(), layout, None, 0., None, 0.)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["fp32", "nvfp4"])
+def test_multi_tick_run_equals_single_ticks_bitwise(fmt):
+    """nsb_dendritic_run_tiled (one persistent launch) == repeated nsb_dendritic_step_tiled."""
+    ext = load_native_extension()
+    graph = random_topology(6000, 150000, device="cpu", seed=11).to("cuda")
+    weight, scales, scale, _ = _packed(graph, fmt)
+    layout = build_tiled_layout(graph.in_rowptr, graph.in_col, weight, neurons=6000, ctas=24,
+                                smem_limit=12000, block_scales=scales, global_scale=scale)
+    assert layout.blocks > 1
+    model = bench_model(6000)
+    s0 = torch.rand(1, 6000, generator=torch.Generator().manual_seed(2)).cuda()
+    d0 = torch.zeros_like(s0)
+    a0 = torch.zeros_like(s0)
+    drive = torch.rand(1, 6000, generator=torch.Generator().manual_seed(9)).cuda() * 0.4
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s, d, a = s0, d0, a0
+    for _ in range(17):
+        s, d, a = ext.dendritic_step_tiled(s, d, a, model.parameters(), layout, drive, 0.0,
+                                           None, 0.1, status=status)
+    out = [torch.empty_like(s0) for _ in range(3)]
+    ext.prepare_step_tiled(s0, d0, a0, model.parameters(), layout, drive, 0.0, None, 0.1,
+                           out=out, status=status, ticks=17)()
+    torch.cuda.synchronize()
+    for got, want in zip(out, (s, d, a)):
+        assert torch.equal(got, want)
+    assert int(status.item()) == 0
+    assert int(layout.workspace()[256:].count_nonzero().item()) == 0  # row sums left cleared
+
+
+@pytest.mark.gpu
+def test_in_kernel_decoders_exhaustive():
+    """Every E4M3 code and every (E2M1 code, E4M3 block scale) pair decodes to the
+    reference quantizer's dequantized value, bit for bit (one edge per row, source 1)."""
+    from neurosim_gpu_b200.precision import e2m1_to_float, e4m3_to_float
+    ext = load_native_extension()
+    g = torch.tensor([0.0371], device="cuda")
+    # E4M3: 256 rows, row i has one edge of code i.
+    n = 256
+    rowptr = torch.arange(n + 1, dtype=torch.int32, device="cuda")
+    col = torch.arange(n, dtype=torch.int32, device="cuda")
+    codes = torch.arange(n, dtype=torch.uint8, device="cuda")
+    layout = build_tiled_layout(rowptr, col, codes, neurons=n, ctas=4, smem_limit=232448,
+                                global_scale=g)
+    got = ext.tiled_propagate(layout, torch.ones(1, n, device="cuda"))
+    want = e4m3_to_float(codes) * g
+    np.testing.assert_array_equal(npy(got)[0], npy(want))
+    # NVFP4: 4096 rows; edge e has E2M1 code e % 16 and lies in block e // 16 with scale code e // 16.
+    n = 4096
+    rowptr = torch.arange(n + 1, dtype=torch.int32, device="cuda")
+    col = torch.arange(n, dtype=torch.int32, device="cuda")
+    nib = torch.arange(n, device="cuda") % 16
+    packed = (nib[0::2] | (nib[1::2] << 4)).to(torch.uint8)
+    scales = torch.arange(256, dtype=torch.uint8, device="cuda")
+    layout = build_tiled_layout(rowptr, col, packed, neurons=n, ctas=8, smem_limit=232448,
+                                block_scales=scales, global_scale=g)
+    got = ext.tiled_propagate(layout, torch.ones(1, n, device="cuda"))
+    want = e2m1_to_float(nib.to(torch.uint8)) * (e4m3_to_float(scales).repeat_interleave(16) * g)
+    np.testing.assert_array_equal(npy(got)[0], npy(want))
