@@ -4,15 +4,19 @@ Workload (BASELINE.json metric): N=166,000 neurons, M=24,988,875 edges
 (``random_topology(166000, 25_000_000, seed=0)``, the reference generator's
 stream), B=1, fp32 weights, constant drives 0.2 / 0.1.  A step is one tick.
 
-* ``value``     synapse-updates/s = M*B / tick time, inputs resident in HBM,
-                ticks replayed from a captured CUDA graph (the multi-tick path).
+* ``value``     synapse-updates/s = M*B / tick time, inputs resident in HBM.
+                B = 1: all K ticks run in ONE persistent cooperative launch of the
+                tiled kernel (the multi-tick path); other batches replay a
+                captured CUDA graph of 64 ticks.
 * ``e2e``       the same metric through the public API: every step copies the
                 step's drive [B,N] from pinned host memory to the device, calls
                 ``NativeDendriticMatrixRuntime.step`` and copies the new state
                 back to pinned host memory.
 * ``roofline``  HBM roofline of the tick kernel: algorithmic bytes
-                M*(w+4) + 4*(N+1) + 24*B*N per launch over the measured launch
-                duration, against MEASURED_PEAKS.json's hbm_gbs.
+                M*(w+4) + 4*(N+1) + 24*B*N per tick over the measured tick
+                time, against MEASURED_PEAKS.json's hbm_gbs.  The tiled layout
+                stores 2-byte column indices, so it streams fewer bytes than
+                the algorithmic count (``streamed_bytes_per_tick``).
 * ``cpu_baseline``  the CPU oracle (a C restatement of the reference tick,
                 OpenMP over all host cores) on a bounded sample of the same ticks.
 
@@ -210,10 +214,13 @@ def run_native(args, workload: str) -> dict:
     runtime = NativeDendriticMatrixRuntime(graph, model, torch.zeros(batch, neurons, device=device),
                                            precision=precision)
     chunk = 64
+    tiled = runtime.kernel_path == "tiled"
     with torch.inference_mode():
-        # Warm-up (includes graph capture and weight packing).
+        # Warm-up (includes graph capture or the layout build, and weight packing).
         runtime.run(max(args.warmup, 1) * 1, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
-        steps = max(args.steps - args.steps % chunk, chunk)
+        # B = 1 (tiled): one persistent cooperative launch runs all K ticks; other
+        # batches replay a CUDA graph of `chunk` ticks.
+        steps = max(args.steps, 1) if tiled else max(args.steps - args.steps % chunk, chunk)
         runtime.run(chunk, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
         torch.cuda.synchronize()
         sampler = ClockSampler(torch.cuda.current_device())
@@ -280,7 +287,7 @@ def run_native(args, workload: str) -> dict:
         "config": {"workload": workload, "neurons": neurons, "edges": m, "batch": batch,
                    "weights": precision, "parallelism": "single GPU",
                    "l2": "inputs larger than L2 (edge stream %.0f MB vs 126 MB)" % (algo / 1e6),
-                   "ticks_per_graph": chunk,
+                   **({"ticks_per_launch": steps} if tiled else {"ticks_per_graph": chunk}),
                    "kernel_path": runtime.kernel_path,
                    "column_blocks": layout.blocks if layout is not None else None,
                    "padding_fraction": round(layout.padding_fraction, 4) if layout is not None
@@ -289,13 +296,15 @@ def run_native(args, workload: str) -> dict:
                      "frac": achieved / peak, "traffic": ncu_traffic(workload),
                      "algorithmic_bytes_per_launch": algo, "peak_source": peak_kind,
                      "kernel": "tiled_tick_kernel" if layout is not None else "csr_tick_kernel",
-                     "streamed_bytes_per_launch": (layout.stream_bytes() + 28 * batch * neurons
-                                                   if layout is not None else None),
-                     "launch_ms_graph": tick_ms, "launch_ms_eager_median": launch_ms},
+                     "per": "tick",
+                     "streamed_bytes_per_tick": (layout.stream_bytes() + 28 * batch * neurons
+                                                 + 8 * layout.blocks * layout.splits * neurons
+                                                 if layout is not None else None),
+                     "tick_ms": tick_ms, "single_tick_launch_ms_median": launch_ms},
         "e2e": {"value": m * batch / (e2e_ms * 1e-3), "unit": "synapse-updates/s",
                 "h2d_bytes_per_step": 4 * batch * neurons, "d2h_bytes_per_step": 4 * batch * neurons,
                 "ms_per_step": e2e_ms},
-        "gpu_launches": steps,
+        "gpu_launches": 1 if tiled else steps,
         "clocks": sampler.summary(),
     }
     if not args.skip_cpu_baseline:

@@ -207,25 +207,30 @@ NSB_API int nsb_dendritic_event_noalloc(const nsb_tick* tick, float* current,
  *    and a range of destination rows; CTA c runs stages stage_ptr[c] ..
  *    stage_ptr[c+1]-1 (block stage_block[s]) with `buffers` (1 or 2) state
  *    blocks in shared memory.
- *  - Tasks of CTA c are task_ptr[c] .. task_ptr[c+1]-1.  tasks[4q..4q+3] =
- *    first slot, chunks C, stage (index among the CTA's stages), first scale
- *    pair.  Lane i owns row task_rows[32q+i] & 0x0FFFFFFF (0x0FFFFFFF: no
- *    row); its j-th edge in the stage's block sits at slot
- *    first + 128*(j/4) + 4*i + j%4, j < 4C.
+ *  - Tasks of CTA c are task_ptr[c] .. task_ptr[c+1]-1.  A task is split h
+ *    (h < splits) of 32 rows' pieces in the stage's block: the lanes' edges
+ *    16*split_chunks*h + j, j < 4C.  tasks[4q..4q+3] = first slot, chunks C,
+ *    stage (index among the CTA's stages) | h << 16, first scale pair.  Lane i
+ *    owns row task_rows[32q+i] & 0x0FFFFFFF (0x0FFFFFFF: no row); its edge
+ *    16*split_chunks*h + j sits at slot first + 128*(j/4) + 4*i + j%4.
  *  - col[slot] is the column minus the block start (uint16); padding slots
  *    hold block_cols and weight 0.  n_slots is a multiple of 128.
  *  - NVFP4: codes are packed two per byte by slot (even slot in the low
- *    nibble).  If lane i's first edge is at CSR position o, its edge j takes
- *    the E4M3 scale of CSR block (o + j) / 16; bits 28..31 of task_rows[32q+i]
- *    hold o % 16, and scale_pairs[first scale pair + 32*b + i] holds the
- *    scales of CSR blocks o/16 + b (low byte) and o/16 + b + 1 (high byte).
+ *    nibble).  If lane i's first edge in the block is at CSR position o, its
+ *    edge j takes the E4M3 scale of CSR block (o + j) / 16; bits 28..31 of
+ *    task_rows[32q+i] hold o % 16, and scale_pairs[first scale pair + 32*b + i]
+ *    holds the scales of CSR blocks o/16 + b (low byte) and o/16 + b + 1 (high
+ *    byte); past the lane's last edge both are 0.
  *  - Pointer alignment: tasks 16 B; col 8 B; weight 16 B (f32), 8 B (f16),
  *    4 B (E4M3), 2 B (NVFP4).
  *  - The kernels trust the layout's contents (offsets, lengths, rows): pass
  *    layouts made by the builder.  `ctas` must not exceed the SM count: the
  *    tick is a cooperative launch with one CTA per SM. */
 typedef struct nsb_tiled_layout {
-  int32_t ctas, blocks, block_cols, buffers, format, reserved;
+  int32_t ctas, blocks, block_cols, buffers, format;
+  int32_t splits;              /* sub-task splits per block (row-sum planes per block) */
+  int32_t split_chunks;        /* chunks of one sub-task                    */
+  int32_t reserved;
   int64_t n_stages, n_tasks, n_slots, n_scale_pairs;
   int64_t rows;                /* destination rows                          */
   int64_t cols;                /* length of the gathered source vector      */
@@ -244,7 +249,7 @@ typedef struct nsb_tiled_layout {
 NSB_API size_t nsb_tiled_smem_bytes(int32_t block_cols, int32_t buffers);
 
 /* Device workspace of the tiled calls, in bytes (256-byte aligned, caller-owned):
- * a grid-barrier head and the per-block row sums.  It must be zero-filled
+ * a grid-barrier counter and the row sums of every (block, split) plane.  It must be zero-filled
  * before its first use; every call leaves it zero-filled again, so one
  * workspace serves any number of calls on one stream.  After a call reported
  * a timeout in `status`, zero-fill it again.  Calls that overlap on the GPU

@@ -180,7 +180,8 @@ bool aligned(const void* p, uintptr_t bytes) {
 bool check_tiled(const nsb_tiled_layout* L) {
   if (!L) return fail(NSB_ERR_ARGUMENT, "tiled layout is required"), false;
   if (L->ctas <= 0 || L->blocks <= 0 || L->block_cols <= 0 || L->block_cols % 32 != 0 ||
-      L->block_cols > 65504 || (L->buffers != 1 && L->buffers != 2) || L->n_stages < 0 ||
+      L->block_cols > 65504 || (L->buffers != 1 && L->buffers != 2) || L->splits < 1 ||
+      L->splits > 1023 || L->split_chunks < 1 || L->n_stages < 0 ||
       L->n_stages >= (int64_t{1} << 24) || L->n_tasks < 0 || L->n_slots < 0 ||
       L->n_slots % 128 != 0 || L->n_slots >= (int64_t{1} << 31) || L->rows <= 0 ||
       L->rows >= (int64_t{1} << 28) - 1 || L->cols <= 0 ||
@@ -259,7 +260,7 @@ int check_tiled_tick(const nsb_tick* tick, const nsb_tiled_layout* layout, const
 }  // namespace
 
 size_t nsb_tiled_workspace_size(const nsb_tiled_layout* layout) {
-  if (!layout || layout->blocks <= 0 || layout->rows <= 0) return 0;
+  if (!layout || layout->blocks <= 0 || layout->splits <= 0 || layout->rows <= 0) return 0;
   return nsb::tiled_workspace_bytes(*layout);
 }
 

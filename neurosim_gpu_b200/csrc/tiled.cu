@@ -29,16 +29,19 @@
 //      buffer with a TMA bulk copy (cp.async.bulk, completion on mbarrier
 //      full[b]); with two buffers it reuses one after mbarrier empty[b] says all
 //      consumer warps left its stage.
-//   2. warps 0..30 (consumers) take tasks from a shared counter.  Each warp
+//   2. warps 0..30 (consumers) take tasks (sub-tasks: one split of 32 rows'
+//      pieces) from a shared counter.  Each warp
 //      keeps a ring of D chunks in registers: the loads of a chunk are issued D
 //      chunks before it is used, across task and stage boundaries, so a warp
 //      always has D chunks of edges in flight (also while the state block is
-//      still being staged).  A lane's sum over its piece (sequential, CSR
-//      order) is stored to part[block][row].
+//      still being staged).  A lane's sum over its split of the piece
+//      (sequential, CSR order) is stored to part[block][split][row].
 //   3. grid barrier; every CTA takes rows [c*R/C, (c+1)*R/C), adds their sums
-//      in block order (clearing part for the next tick), applies the pointwise
-//      update and writes s', d', a'.
-//   4. for the next tick (in place on the outputs): grid barrier, back to 1.
+//      in (block, split) order (clearing part for the next tick), applies the
+//      pointwise update and writes s', d', a'.
+//   4. for the next tick (in place on the outputs): back to 1; the producer
+//      waits at a grid barrier (every CTA's update done) before it stages the
+//      new state, while the consumers already load the next tick's edges.
 // Every wait (mbarrier or grid barrier) is bounded; on timeout the kernel
 // records an error code in `status` and continues, so a fault in the pipeline
 // never hangs the GPU.
@@ -68,7 +71,8 @@ constexpr uint32_t kRowMask = 0x0FFFFFFFu;   // task_rows: row bits; kRowMask = 
 constexpr uint32_t kTagValid = 1u;
 constexpr uint32_t kTagLast = 2u;   // last chunk of its task
 constexpr int kTagPhase = 2;        // NVFP4: (phase + 4c) % 16, 4 bits
-constexpr int kTagStage = 8;        // CTA-local stage, 24 bits
+constexpr int kTagStage = 6;        // CTA-local stage, 16 bits
+constexpr int kTagSplit = 22;       // split of the sub-task, 10 bits
 
 // Error word used when the caller passes no status pointer.
 __device__ int g_tiled_status;
@@ -194,7 +198,7 @@ __device__ __forceinline__ void e2m1x4_to_float(uint32_t four, float (&v)[4]) {
 struct ChunkF32 {
   using Raw = uint4;
   const float* w;
-  __device__ __forceinline__ void prefetch(int first, int chunks, int) const {
+  __device__ __forceinline__ void prefetch(int first, int chunks, int, int) const {
     prefetch_l2(w + first, static_cast<uint32_t>(chunks) * kChunkSlots * 4u);
   }
   __device__ __forceinline__ void set_scale(float) {}
@@ -212,7 +216,7 @@ struct ChunkF32 {
 struct ChunkF16 {
   using Raw = uint2;
   const __half* w;
-  __device__ __forceinline__ void prefetch(int first, int chunks, int) const {
+  __device__ __forceinline__ void prefetch(int first, int chunks, int, int) const {
     prefetch_l2(w + first, static_cast<uint32_t>(chunks) * kChunkSlots * 2u);
   }
   __device__ __forceinline__ void set_scale(float) {}
@@ -233,7 +237,7 @@ struct ChunkE4M3 {
   using Raw = uint32_t;
   const uint8_t* codes;
   float g;
-  __device__ __forceinline__ void prefetch(int first, int chunks, int) const {
+  __device__ __forceinline__ void prefetch(int first, int chunks, int, int) const {
     prefetch_l2(codes + first, static_cast<uint32_t>(chunks) * kChunkSlots);
   }
   __device__ __forceinline__ void set_scale(float s) { g = s; }
@@ -255,10 +259,13 @@ struct ChunkNVFP4 {
   const uint8_t* codes;
   const uint16_t* pairs;
   float g;
-  // Codes and the task's scale table ((11 + 4C) / 16 + 1 rows of 32 pairs).
-  __device__ __forceinline__ void prefetch(int first, int chunks, int entry) const {
+  // Codes and the scale-table rows a split of C chunks starting at chunk c0
+  // of the lanes' pieces reads: rows (4 c0) / 16 .. (4 (c0 + C) + 11) / 16.
+  __device__ __forceinline__ void prefetch(int first, int chunks, int entry, int c0) const {
     prefetch_l2(codes + (first >> 1), static_cast<uint32_t>(chunks) * (kChunkSlots / 2));
-    prefetch_l2(pairs + entry, static_cast<uint32_t>(((11 + kChunk * chunks) >> 4) + 1) * 64u);
+    const int r0 = (kChunk * c0) >> 4;
+    const int r1 = (kChunk * (c0 + chunks) + 11) >> 4;
+    prefetch_l2(pairs + entry + r0 * 32, static_cast<uint32_t>(r1 - r0 + 1) * 64u);
   }
   __device__ __forceinline__ void set_scale(float s) { g = s; }
   __device__ __forceinline__ Raw load(int64_t slot, int64_t entry, uint64_t pol) const {
@@ -279,16 +286,18 @@ struct TiledArgs {
   const int32_t* stage_ptr;    // [C+1]
   const int32_t* stage_block;  // [stages]
   const int32_t* task_ptr;     // [C+1]
-  const int4* tasks;           // [T]: first slot, chunks, stage (CTA-local), first scale pair
+  const int4* tasks;           // [T]: first slot, chunks, stage | split << 16, first scale pair
   const int32_t* task_rows;    // [T*32]: row | phase << 28
   const uint16_t* col;         // [S] column relative to the block, block_cols = padding
   const float* global_scale;   // E4M3 / NVFP4: one float
-  float* part;                 // workspace: [blocks][rows] per-block row sums (zero between launches)
+  float* part;                 // workspace: [blocks][splits][rows] row sums (zero between launches)
   unsigned long long* barrier; // workspace: grid-barrier arrival counter
   int32_t block_cols;          // CB
   int32_t buffers;             // NBUF (1 or 2)
   int32_t prefetch_ahead;      // tasks prefetched beyond the hand-out counter
   int32_t prefetch_first;      // tasks of the next tick's first round prefetched (0 or warps)
+  int32_t splits;              // sub-task planes per block
+  int32_t split_chunks;        // chunks of one sub-task
   int64_t rows;                // destination rows
   int64_t cols;                // length of the gathered source vector
 };
@@ -300,30 +309,34 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long
 }
 
 // Grid-wide barrier of a cooperative launch over a monotonic 64-bit arrival
-// counter: the CTA whose arrival is number a (0-based) waits until the counter
-// reaches the next multiple of the grid size above a.  Nothing is reset, so the
-// critical path is one atomic and the pollers' next read.  Every launch that
-// uses a workspace has the same grid size and passes every barrier, so the
-// counter is a multiple of the grid size between launches.  The wait is
-// bounded: on timeout it records code 4.
+// counter, for one thread per CTA (after a __syncthreads that orders the CTA's
+// writes before it): the CTA whose arrival is number a (0-based) waits until
+// the counter reaches the next multiple of the grid size above a.  Nothing is
+// reset, so the critical path is one atomic and the pollers' next read.
+// Every launch that uses a workspace has the same grid size and passes every
+// barrier, so the counter is a multiple of the grid size between launches.
+// The wait is bounded: on timeout it records code 4.
+__device__ void grid_arrive_wait(unsigned long long* count, int* st) {
+  __threadfence();
+  const unsigned long long arrival = atomicAdd(count, 1ull);
+  const unsigned long long target = (arrival / gridDim.x + 1) * gridDim.x;
+  long long polls = 0;
+  while (ld_acquire_gpu(count) < target) {
+    if (++polls > (1 << 16)) {
+      if (polls > kGridWaitLimit) {
+        atomicExch(st, 4);
+        break;
+      }
+      __nanosleep(256);
+    }
+  }
+  __threadfence();
+}
+
+// The same barrier for the whole CTA.
 __device__ void grid_barrier(unsigned long long* count, int* st) {
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned long long arrival = atomicAdd(count, 1ull);
-    const unsigned long long target = (arrival / gridDim.x + 1) * gridDim.x;
-    long long polls = 0;
-    while (ld_acquire_gpu(count) < target) {
-      if (++polls > (1 << 16)) {
-        if (polls > kGridWaitLimit) {
-          atomicExch(st, 4);
-          break;
-        }
-        __nanosleep(256);
-      }
-    }
-    __threadfence();
-  }
+  if (threadIdx.x == 0) grid_arrive_wait(count, st);
   __syncthreads();
 }
 
@@ -369,7 +382,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
   auto prefetch_task = [&](const int4& m) {
     if (m.y > 0) {
       prefetch_l2(L.col + m.x, static_cast<uint32_t>(m.y) * kChunkSlots * 2u);
-      w.prefetch(m.x, m.y, m.w);
+      w.prefetch(m.x, m.y, m.w, (m.z >> 16) * L.split_chunks);
     }
   };
   // Warp w starts every tick with task w; the rest are handed out in order by
@@ -409,6 +422,13 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
         prefetched = limit;
       };
       if (lane == 0) {
+        // From the second tick on, the state block must wait until every CTA
+        // has written its rows of the previous tick (and read and cleared its
+        // row sums): a grid barrier that only this thread of the CTA takes.
+        // The consumer warps meanwhile start loading the tick's edges; they
+        // touch the row sums only after the staged block arrives, so they
+        // are ordered after the barrier through the block's mbarrier.
+        if (tick > 0) grid_arrive_wait(L.barrier, st);
         // The state was written by other CTAs' generic stores before the grid
         // barrier; order those writes before this thread's async-proxy reads.
         asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -448,6 +468,25 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
       }
       prefetched = 0;
       if (tick + 1 < ticks) prefetch_upto(min(task_count, L.prefetch_first));
+      // The operands of this CTA's update rows, so the update after the grid
+      // barrier reads them from L2 (contiguous interior 16-byte spans only).
+      if (update && lane < 9) {
+        const float* base = nullptr;
+        int64_t stride = 0;
+        if (lane < 6) {
+          base = t.p.data[lane];
+          stride = t.p.stride[lane];
+        } else {
+          const View v = lane == 6 ? (tick == 0 ? t.s : View{out.s.data, out.s.sb, out.s.sn, 0.0f})
+                       : lane == 7 ? (tick == 0 ? t.d : View{out.d.data, out.d.sb, out.d.sn, 0.0f})
+                                   : (tick == 0 ? t.a : View{out.a.data, out.a.sb, out.a.sn, 0.0f});
+          base = v.data;
+          stride = v.sn;
+        }
+        const int64_t lo = (update_lo + 3) & ~int64_t{3}, hi = update_hi & ~int64_t{3};
+        if (base && stride == 1 && reinterpret_cast<uintptr_t>(base) % 16 == 0 && hi > lo)
+          prefetch_l2(base + lo, static_cast<uint32_t>((hi - lo) * 4));
+      }
       if (lane == 0) {
         // Do not leave the tick while a copy into this CTA's shared memory may
         // be in flight.
@@ -488,11 +527,12 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
           }
           slot = next_meta.x + lane * kChunk;
           left = next_meta.y;
-          chunk = 0;
+          chunk = (next_meta.z >> 16) * L.split_chunks;  // chunk index within the lane's piece
           entry = next_meta.w + lane;
           phase = static_cast<int>(next_row >> 28);
           row = next_row & kRowMask;
-          tag_base = kTagValid | (static_cast<uint32_t>(next_meta.z) << kTagStage);
+          tag_base = kTagValid | (static_cast<uint32_t>(next_meta.z & 0xFFFF) << kTagStage) |
+                     (static_cast<uint32_t>(next_meta.z >> 16) << kTagSplit);
           next_q = grab();
           fetch();
         }
@@ -522,13 +562,14 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
         for (int u = 0; u < D; ++u) {
           const uint32_t g = tag[u];
           if (g & kTagValid) {
-            const int s = static_cast<int>(g >> kTagStage);
+            const int s = static_cast<int>((g >> kTagStage) & 0xFFFFu);
             if (s != stage) {  // warp-uniform
               leave_until(use0 + s);
               observe(use0 + s);
               stage = s;
               sb = sbuf + ((use0 + s) % nbuf) * cb_pad;
-              part = L.part + static_cast<int64_t>(__ldg(L.stage_block + stage_first + s)) * L.rows;
+              part = L.part + static_cast<int64_t>(__ldg(L.stage_block + stage_first + s)) *
+                                  L.splits * L.rows;
             }
             float v[4];
             w.decode(raw[u], g, v);
@@ -537,7 +578,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
             acc = fmaf(v[2], sb[cols[u].y & 0xFFFFu], acc);
             acc = fmaf(v[3], sb[cols[u].y >> 16], acc);
             if (g & kTagLast) {
-              if (rows[u] != kRowMask) part[rows[u]] = acc;
+              if (rows[u] != kRowMask) part[(g >> kTagSplit) * L.rows + rows[u]] = acc;
               acc = -0.0f;
             }
           }
@@ -554,7 +595,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
     // every operand of both rows is loaded before any store, so a round costs
     // one memory round trip.  The row sums and the state written by earlier
     // ticks of this launch are read through L2.
-    const int planes = static_cast<int>((L.cols + L.block_cols - 1) / L.block_cols);
+    const int planes = static_cast<int>((L.cols + L.block_cols - 1) / L.block_cols) * L.splits;
     for (int64_t n0 = update_lo + threadIdx.x; n0 < update_hi; n0 += 2 * blockDim.x) {
       float j[2], s0[2], d0[2], a0[2], u[2], v[2], pr[2][6];
 #pragma unroll
@@ -582,12 +623,12 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
         j[r] = 0.0f;
         if (row) {
           const float* p = L.part + n;
-          for (int k0 = 0; k0 < planes; k0 += 8) {  // block order: ((p0 + p1) + p2) + ...
-            float sums[8];
+          for (int k0 = 0; k0 < planes; k0 += 16) {  // (block, split) order: ((p0 + p1) + p2) + ...
+            float sums[16];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) sums[i] = k0 + i < planes ? __ldcg(p + (k0 + i) * L.rows) : 0.0f;
+            for (int i = 0; i < 16; ++i) sums[i] = k0 + i < planes ? __ldcg(p + (k0 + i) * L.rows) : 0.0f;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int i = 0; i < 16; ++i)
               if (k0 + i < planes) j[r] = k0 + i == 0 ? sums[i] : j[r] + sums[i];
           }
         }
@@ -608,7 +649,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
         }
       }
     }
-    if (tick + 1 < ticks) grid_barrier(L.barrier, st);  // the new state is complete
+    __syncthreads();  // this CTA's update is done (the producer's barrier orders it)
   }
 }
 
@@ -650,7 +691,8 @@ size_t tiled_smem_bytes(int block_cols, int buffers) {
 }
 
 size_t tiled_workspace_bytes(const nsb_tiled_layout& layout) {
-  return 256 + static_cast<size_t>(layout.blocks) * static_cast<size_t>(layout.rows) * 4;
+  return 256 + static_cast<size_t>(layout.blocks) * static_cast<size_t>(layout.splits) *
+                   static_cast<size_t>(layout.rows) * 4;
 }
 
 cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, const float* x,
@@ -670,6 +712,8 @@ cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, cons
   L.buffers = layout.buffers;
   L.rows = layout.rows;
   L.cols = layout.cols;
+  L.splits = layout.splits;
+  L.split_chunks = layout.split_chunks;
   // Prefetch window in tasks: kPrefetchBudget bytes of an average task.
   static const double slot_bytes[4] = {6.0, 4.0, 3.0, 2.5};
   const double task_bytes = layout.n_tasks > 0 ? static_cast<double>(layout.n_slots) *

@@ -76,7 +76,8 @@ class _OutCsr(ctypes.Structure):
 class _TiledLayout(ctypes.Structure):
     _fields_ = [("ctas", ctypes.c_int32), ("blocks", ctypes.c_int32),
                 ("block_cols", ctypes.c_int32), ("buffers", ctypes.c_int32),
-                ("format", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("format", ctypes.c_int32), ("splits", ctypes.c_int32),
+                ("split_chunks", ctypes.c_int32), ("reserved", ctypes.c_int32),
                 ("n_stages", ctypes.c_int64), ("n_tasks", ctypes.c_int64),
                 ("n_slots", ctypes.c_int64), ("n_scale_pairs", ctypes.c_int64),
                 ("rows", ctypes.c_int64), ("cols", ctypes.c_int64),

@@ -22,9 +22,13 @@ and streams the edges with vector loads:
   (a zero in shared memory) and weight 0.
 * Columns are stored relative to their block as uint16 (2 bytes per edge
   instead of the CSR's 4).
-* The per-(row, block) sums go to a workspace array ``part[block][row]``; after
-  a grid-wide barrier every CTA adds the sums of its share of the rows in block
-  order and applies the pointwise update.
+* A task is cut into sub-tasks of ``split_chunks`` chunks (edges
+  ``16 * split_chunks * h ...`` of every lane's piece form split ``h``), so the
+  CTA's work comes in pieces small enough to balance over its warps.  Each
+  sub-task's per-row sums go to a workspace plane ``part[block][h][row]``;
+  after a grid-wide barrier every CTA adds the planes of its share of the rows
+  in (block, split) order and applies the pointwise update.  The split points
+  depend only on a row's own piece, not on how rows are grouped into tasks.
 * NVFP4: codes are re-packed two per byte by slot.  Each task carries a table
   of uint16 scale pairs (for lane ``i`` and row ``b``: the E4M3 scales of CSR
   blocks ``o_i // 16 + b`` and ``+ b + 1``, ``o_i`` the CSR position of the
@@ -54,6 +58,13 @@ CHUNK_SLOTS = LANES * CHUNK   # slots of one warp-wide chunk
 MAX_BLOCK_COLS = 65504        # 16-bit block-relative columns, block_cols = padding
 MAX_ROWS = (1 << 28) - 1      # 28-bit rows in task_rows; ROW_NONE marks a padding lane
 ROW_NONE = MAX_ROWS
+WARPS = 31                    # consumer warps of a CTA
+# Target number of sub-tasks each consumer warp runs per tick, by weight format
+# (0: tasks are not split).  Splitting shortens the tail of a tick but adds
+# row-sum planes that the update reads; measured at 166k / 25M it pays off for
+# fp32 (39.7 vs 42.6 us) and costs the narrower formats (fp16 30.6 vs 33.7 us).
+SUBTASKS_PER_WARP = {native.F32: 5, native.F16: 0, native.E4M3: 0, native.NVFP4: 0}
+MAX_PLANES = 12               # cap on blocks x splits (row-sum planes of the workspace)
 
 
 def _u16(values: torch.Tensor) -> torch.Tensor:
@@ -80,13 +91,15 @@ class TiledLayout:
     stage_ptr: torch.Tensor    # int32 [ctas+1]: stages of CTA c
     stage_block: torch.Tensor  # int32 [stages]: column block of each stage
     task_ptr: torch.Tensor     # int32 [ctas+1]: tasks of CTA c
-    tasks: torch.Tensor        # int32 [T, 4]: first slot, chunks, stage (CTA-local), first scale pair
+    tasks: torch.Tensor        # int32 [T, 4]: first slot, chunks, stage | split << 16, first scale pair
     task_rows: torch.Tensor    # int32 [T, 32]: row | phase << 28 (row ROW_NONE: padding lane)
     col: torch.Tensor          # int16 storage of uint16 [S]
     weight: torch.Tensor       # [S] in the storage format (NVFP4: uint8 [S/2])
     scale_pairs: torch.Tensor | None  # int16 storage of uint16 (NVFP4)
     global_scale: torch.Tensor | None
     cols: int = 0         # length of the gathered source vector (0: same as neurons)
+    splits: int = 1       # sub-task planes per block
+    split_chunks: int = 1 << 20  # chunks of one sub-task
     _workspace: torch.Tensor | None = field(default=None, repr=False)
 
     def __post_init__(self) -> None:
@@ -126,14 +139,14 @@ class TiledLayout:
 
     def workspace_bytes(self) -> int:
         """Device workspace one launch needs (barrier words + per-block row sums)."""
-        return 256 + self.blocks * self.neurons * 4
+        return 256 + self.blocks * self.splits * self.neurons * 4
 
     def c_struct(self) -> "native._TiledLayout":
         def ptr(t):
             return t.data_ptr() if t is not None and t.numel() else None
         return native._TiledLayout(
-            self.ctas, self.blocks, self.block_cols, self.buffers, self.format, 0,
-            self.n_stages, self.n_tasks, self.n_slots,
+            self.ctas, self.blocks, self.block_cols, self.buffers, self.format, self.splits,
+            self.split_chunks, 0, self.n_stages, self.n_tasks, self.n_slots,
             self.scale_pairs.numel() if self.scale_pairs is not None else 0,
             self.neurons, self.cols,
             ptr(self.stage_ptr), ptr(self.stage_block), ptr(self.task_ptr), ptr(self.tasks),
@@ -322,13 +335,39 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
         task_rows[pair_task, pair_lane] = pair_row
         tiled_weight = torch.zeros(slots, dtype=weight.dtype, device=device)
         tiled_weight[slot] = weight
-    tasks = torch.stack((task_first, task_chunks, task_stage_local, scale_first), dim=1)
+    # Sub-tasks: chunks [h * split, (h + 1) * split) of a task.
+    longest = int(task_chunks.max()) if n_tasks else 1
+    target = SUBTASKS_PER_WARP.get(fmt, 0)
+    if target > 0:
+        per_cta = slots // CHUNK_SLOTS / max(ctas, 1)
+        split = max(1, round(per_cta / (WARPS * target)))
+        split = max(split, -(-longest // max(1, MAX_PLANES // blocks)))
+    else:
+        split = longest
+    split = max(1, min(split, longest))
+    splits = max(1, -(-longest // split))
+    n_sub = (task_chunks + split - 1) // split
+    sub_task = torch.repeat_interleave(arange(n_tasks), n_sub)
+    sub_h = arange(sub_task.numel()) - (torch.cumsum(n_sub, 0) - n_sub)[sub_task]
+    sub_chunks = torch.clamp(task_chunks[sub_task] - sub_h * split, max=split)
+    # Within a stage: longest sub-tasks first (tasks keep their order otherwise).
+    sub_stage = task_stage[sub_task]
+    sub_order = torch.sort(-sub_chunks, stable=True).indices
+    sub_order = sub_order[torch.sort(sub_stage[sub_order], stable=True).indices]
+    sub_task, sub_h, sub_chunks = sub_task[sub_order], sub_h[sub_order], sub_chunks[sub_order]
+    tasks = torch.stack((task_first[sub_task] + sub_h * split * CHUNK_SLOTS, sub_chunks,
+                         task_stage_local[sub_task] | (sub_h << 16), scale_first[sub_task]), dim=1)
+    subs_per_cta = torch.zeros(ctas, dtype=torch.int64, device=device)
+    subs_per_cta.index_add_(0, stage_cta[sub_stage], torch.ones_like(sub_stage))
+    torch.cumsum(subs_per_cta, 0, out=task_ptr[1:])
+    task_rows = task_rows[sub_task]
     return TiledLayout(
         neurons=n, n_edges=m, ctas=ctas, blocks=blocks, block_cols=block_cols, buffers=buffers,
         format=fmt, stage_ptr=stage_ptr.to(torch.int32), stage_block=stage_block.to(torch.int32),
         task_ptr=task_ptr.to(torch.int32), tasks=tasks.to(torch.int32).contiguous(),
         task_rows=_i32(task_rows).contiguous(), col=_u16(col), weight=tiled_weight,
-        scale_pairs=scale_pairs, global_scale=global_scale, cols=cols)
+        scale_pairs=scale_pairs, global_scale=global_scale, cols=cols, splits=splits,
+        split_chunks=split)
 
 
 def emulate(layout: TiledLayout, source: torch.Tensor) -> torch.Tensor:
@@ -344,15 +383,17 @@ def emulate(layout: TiledLayout, source: torch.Tensor) -> torch.Tensor:
         return out
     slots = torch.arange(layout.n_slots, device=dev)
     first = layout.tasks[:, 0].long()
-    task = torch.searchsorted(first, slots, right=True) - 1
+    by_slot = torch.argsort(first)           # (sub-)tasks are not stored in slot order
+    task = by_slot[torch.searchsorted(first[by_slot], slots, right=True) - 1]
     local = slots - first[task]
     chunk, lane, e = local // CHUNK_SLOTS, (local % CHUNK_SLOTS) // CHUNK, local % CHUNK
     word = layout.task_rows.long()[task, lane] & 0xFFFFFFFF
     col = layout.col.long() & 0xFFFF
     cta = torch.searchsorted(layout.task_ptr.long(), torch.arange(layout.n_tasks, device=dev),
                              right=True) - 1
-    stage = layout.stage_ptr.long()[cta] + layout.tasks[:, 2].long()
+    stage = layout.stage_ptr.long()[cta] + (layout.tasks[:, 2].long() & 0xFFFF)
     block = layout.stage_block.long()[stage][task]
+    chunk = chunk + (layout.tasks[:, 2].long() >> 16)[task] * layout.split_chunks
     padded = torch.cat([x, torch.zeros(layout.blocks * layout.block_cols + 1 - x.numel(),
                                        dtype=x.dtype, device=dev)])
     gathered = torch.where(col == layout.block_cols, torch.zeros_like(x[:1]),
