@@ -16,6 +16,19 @@
 //     (b mod G) of the group then applies the pointwise update for batch row b
 //     and writes s', d', a' (or the bare product for nsb_csr_propagate).
 //   * The grid is persistent over rows: SMs x resident blocks, grid-stride.
+//
+// Batched variant (csr_batch_kernel, every B >= 2; fastest when the batch rows
+// of a source are contiguous, the [N, B] state layout the runtime keeps):
+//   * One warp per destination row.  Lane l works on batch row b = l % BT of
+//     edge slot l / BT, so one gather instruction of the warp fetches the BT
+//     contiguous floats of 32 / BT edges (for BT = 8: four 32-byte sectors in
+//     one request) instead of one load per (edge, batch row).
+//   * The warp loads 32 edges' columns and weights with one coalesced load
+//     each and hands them to the (edge, batch) lanes with shuffles; all of a
+//     batch's gathers are issued before its FMAs.
+//   * Lane sums (edges l / BT, l / BT + 32/BT, ... in order) are reduced over
+//     the lanes of a batch row with a fixed xor tree; lanes 0..BT-1 then apply
+//     the pointwise update for their batch row.
 #include <algorithm>
 
 #include "nsb_launch.h"
@@ -118,6 +131,64 @@ csr_tick_kernel(TickArgs t, View x, const int32_t* __restrict__ rowptr,
   }
 }
 
+template <int BT, bool UPDATE, typename W>
+__global__ void __launch_bounds__(kThreads)
+csr_batch_kernel(TickArgs t, View x, const int32_t* __restrict__ rowptr,
+                 const int32_t* __restrict__ col, W weights, TickOut out, Out product) {
+  constexpr int kEdgesPerStep = 32 / BT;
+  const int lane = threadIdx.x & 31;
+  const int b = lane % BT;
+  const int slot = lane / BT;
+  const int64_t neurons = t.neurons;
+  const int64_t batch = t.batch;
+  const int64_t b0 = static_cast<int64_t>(blockIdx.y) * BT;
+  const bool active = b0 + b < batch;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const uint64_t pol = evict_first_policy();
+  const float* __restrict__ xb = x.data + (active ? (b0 + b) * x.sb : 0);
+
+  for (int64_t n = warp; n < neurons; n += n_warps) {
+    const int64_t e0 = rowptr[n];
+    const int64_t e1 = rowptr[n + 1];
+    float acc = -0.0f;  // -0.0 is the exact additive identity
+    for (int64_t e = e0; e < e1; e += 32) {
+      const int count = static_cast<int>(e1 - e < 32 ? e1 - e : 32);
+      int c = 0;
+      float w = 0.0f;
+      if (lane < count) {
+        c = static_cast<int>(stream_load_u32(reinterpret_cast<const uint32_t*>(col + e + lane), pol));
+        w = weights.one(e + lane);
+      }
+      float v[BT];
+#pragma unroll
+      for (int i = 0; i < BT; ++i) {  // gathers first: BT independent loads in flight
+        const int k = i * kEdgesPerStep + slot;
+        const int ck = __shfl_sync(0xffffffffu, c, k);
+        v[i] = (k < count && active) ? __ldg(xb + static_cast<int64_t>(ck) * x.sn) : 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < BT; ++i) {
+        const int k = i * kEdgesPerStep + slot;
+        const float wk = __shfl_sync(0xffffffffu, w, k);
+        if (k < count) acc = fmaf(wk, v[i], acc);
+      }
+    }
+#pragma unroll
+    for (int off = BT; off < 32; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane < BT && active) {
+      if constexpr (UPDATE) {
+        const Update r = advance_at(t, acc, b0 + b, n);
+        out.s.put(b0 + b, n, r.s);
+        out.d.put(b0 + b, n, r.d);
+        out.a.put(b0 + b, n, r.a);
+      } else {
+        product.put(b0 + b, n, acc);
+      }
+    }
+  }
+}
+
 template <typename K>
 int resident_blocks(K kernel) {
   int blocks = 0;
@@ -150,16 +221,52 @@ cudaError_t launch_variant(const TickArgs& t, const View& x, const Csr& csr, con
   return cudaGetLastError();
 }
 
+template <int BT, bool UPDATE, typename W>
+cudaError_t launch_batch_variant(const TickArgs& t, const View& x, const Csr& csr, const W& weights,
+                                 const TickOut& out, const Out& product, cudaStream_t stream) {
+  auto kernel = csr_batch_kernel<BT, UPDATE, W>;
+  static int occupancy[64] = {0};
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return err;
+  DeviceInfo info;
+  err = device_info(&info);
+  if (err != cudaSuccess) return err;
+  int& occ = occupancy[device & 63];
+  if (occ == 0) occ = resident_blocks(kernel);
+  const int64_t rows_per_block = kThreads / 32;
+  const int64_t needed = (t.neurons + rows_per_block - 1) / rows_per_block;
+  const int64_t cap = static_cast<int64_t>(info.sm_count) * occ;
+  const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, std::min(needed, cap))),
+                  static_cast<unsigned>((t.batch + BT - 1) / BT));
+  kernel<<<grid, kThreads, 0, stream>>>(t, x, csr.rowptr, csr.col, weights, out, product);
+  return cudaGetLastError();
+}
+
+template <bool UPDATE, typename W>
+cudaError_t dispatch_batch(const TickArgs& t, const View& x, const Csr& csr, const W& w,
+                           const TickOut& out, const Out& product, cudaStream_t stream) {
+  if (t.batch <= 2) return launch_batch_variant<2, UPDATE>(t, x, csr, w, out, product, stream);
+  if (t.batch <= 4) return launch_batch_variant<4, UPDATE>(t, x, csr, w, out, product, stream);
+  return launch_batch_variant<8, UPDATE>(t, x, csr, w, out, product, stream);
+}
+
 template <bool UPDATE, typename W>
 cudaError_t dispatch_group(const TickArgs& t, const View& x, const Csr& csr, const W& w,
                            bool vec, int width, const TickOut& out, const Out& product,
                            cudaStream_t stream) {
   const int64_t batch = t.batch;
+  // B >= 2: the batch-cooperative kernel, whatever the source strides, so the
+  // summation order (and the result) does not depend on the state's layout.
+  // With the [N, B] layout (batch stride 1) its gathers are one sector per edge.
+  if (batch >= 2 && x.data)
+    return dispatch_batch<UPDATE>(t, x, csr, w, out, product, stream);
 #define NSB_BT(G)                                                                      \
   if (batch <= 1) return launch_variant<G, 1, UPDATE>(t, x, csr, w, vec, out, product, stream); \
   if (batch <= 2) return launch_variant<G, 2, UPDATE>(t, x, csr, w, vec, out, product, stream); \
   if (batch <= 4) return launch_variant<G, 4, UPDATE>(t, x, csr, w, vec, out, product, stream); \
   return launch_variant<G, 8, UPDATE>(t, x, csr, w, vec, out, product, stream);
+  if (width == 0) width = choose_group_width(csr.n_edges, t.neurons);
   switch (width) {
     case 4: { NSB_BT(4) }
     case 8: { NSB_BT(8) }
@@ -200,7 +307,6 @@ int choose_group_width(int64_t n_edges, int64_t neurons) {
 
 cudaError_t launch_csr(const TickArgs& t, const View& x, const Csr& csr, int width, bool update,
                        const TickOut& out, const Out& product, cudaStream_t stream) {
-  if (width == 0) width = choose_group_width(csr.n_edges, t.neurons);
   const bool col_ok = aligned(csr.col, 16);
   switch (csr.format) {
     case NSB_WEIGHT_F16: {
