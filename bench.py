@@ -396,7 +396,10 @@ def run_sharded(args, explicit_workload: bool) -> dict:
         "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (reference random_topology stream, seed 0; drives 0.2/0.1)",
         "config": {"workload": name, "neurons": neurons, "edges": m, "batch": batch,
-                   "weights": precision, "parallelism": f"row-sharded x{world}, NCCL all-gather",
+                   "weights": precision,
+                   "parallelism": f"row-sharded x{world}, " + (
+                       "soma exchange by peer stores inside the tick kernel (NVLink)"
+                       if runtime.exchange == "peer" else "NCCL all-gather"),
                    "l2": "inputs larger than L2", "kernel_path": runtime.kernel_path,
                    "column_blocks": layout.blocks if layout is not None else None,
                    "ticks_per_graph": chunk},
@@ -407,10 +410,11 @@ def run_sharded(args, explicit_workload: bool) -> dict:
         "e2e": {"value": m * batch / (e2e_ms * 1e-3), "unit": "synapse-updates/s",
                 "h2d_bytes_per_step": 4 * batch * neurons, "d2h_bytes_per_step": 4 * batch * neurons,
                 "ms_per_step": e2e_ms},
-        "gpu_launches": steps * world,
+        "gpu_launches": world if runtime.exchange == "peer" else steps * world,
         "clocks": sampler.summary() if sampler else None,
     }
     runtime.release_graphs()
+    runtime.close()
     torch.cuda.synchronize()
     dist.barrier()
     dist.destroy_process_group()

@@ -45,7 +45,7 @@ extern "C" {
 #define NSB_API
 #endif
 
-#define NSB_ABI_VERSION 3
+#define NSB_ABI_VERSION 4
 
 enum nsb_status {
   NSB_OK = 0,
@@ -276,6 +276,53 @@ NSB_API int nsb_dendritic_step_tiled(const nsb_tick* tick, const nsb_tiled_layou
 NSB_API int nsb_dendritic_run_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
                                     int64_t ticks, const nsb_tick_out* out, void* workspace,
                                     size_t workspace_bytes, int* status, void* stream);
+
+/* Up to this many GPUs take part in a peer exchange. */
+#define NSB_MAX_PEERS 8
+
+/* The soma exchange of a row-sharded tiled run, done inside the kernel over
+ * NVLink instead of an all-gather between launches (no counterpart in the
+ * reference, whose runtimes are single-GPU).  Rank r owns global rows
+ * [row_offset, row_offset + layout->rows) of a graph whose gathered state has
+ * layout->cols floats.  Every rank keeps two gathered buffers; every pointer
+ * below is as mapped in THIS process (peers' buffers through CUDA IPC, see
+ * nsb_ipc_export / nsb_ipc_import), [rank] being this rank's own. */
+typedef struct nsb_peer_exchange {
+  int32_t world;               /* ranks, 1..NSB_MAX_PEERS                    */
+  int32_t rank;
+  int64_t row_offset;
+  float* gathered[NSB_MAX_PEERS][2];         /* each rank's two buffers [cols]  */
+  unsigned long long* counters[NSB_MAX_PEERS]; /* each rank's arrival counter */
+  uint64_t epoch;              /* peer barriers these counters completed before
+                                  this call (counter value / world)          */
+} nsb_peer_exchange;
+
+/* `ticks` (>= 1) row-sharded matrix ticks in ONE cooperative launch per rank,
+ * the soma exchange fused into the kernel: tick t reads the full state from
+ * this rank's gathered[rank][t % 2], and the update writes each new s of this
+ * rank's rows into gathered[p][(t + 1) % 2] of EVERY rank p (peer stores over
+ * NVLink), then waits at a cross-GPU barrier (each rank's counter reaches
+ * world * (epoch + t + 1)); after the call every rank's gathered[*][ticks % 2]
+ * holds the full new state.  tick->state is ignored (the state comes from the
+ * gathered buffer); dendrite / adaptation are read from the tick for the first
+ * tick and kept in out->dendrite / out->adaptation (in place) after that;
+ * out->state is ignored.  All ranks must make the call with the same ticks,
+ * epoch and layout geometry; their kernels wait for each other (bounded: a
+ * missing rank ends the call with code 6 in `status`).  The counters must be
+ * zero-filled before their first use and the epoch advanced by `ticks` after
+ * each call. */
+NSB_API int nsb_dendritic_run_tiled_peers(const nsb_tick* tick, const nsb_tiled_layout* layout,
+                                          int64_t ticks, const nsb_peer_exchange* exchange,
+                                          const nsb_tick_out* out, void* workspace,
+                                          size_t workspace_bytes, int* status, void* stream);
+
+/* CUDA IPC for the peer exchange: export a device pointer of this process as a
+ * 64-byte handle plus the pointer's offset in its allocation, and import such
+ * a handle into the current device (peer access enabled) as the allocation's
+ * base address.  Release an imported base with nsb_ipc_release. */
+NSB_API int nsb_ipc_export(const void* device_ptr, void* handle, uint64_t* offset);
+NSB_API int nsb_ipc_import(const void* handle, void** base);
+NSB_API int nsb_ipc_release(void* base);
 
 /* Matrix tick of a block of destination rows (any B): the CSR holds those rows
  * (rowptr rebased to 0, col indexing the full source), `source` is the full

@@ -6,6 +6,7 @@
 // negative status, leaves the stream untouched and records a message for
 // nsb_last_error().
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "nsb_launch.h"
@@ -300,6 +301,79 @@ int nsb_dendritic_run_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout
                                             nsb::Out{nullptr, 0, 0}, workspace, status,
                                             static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_run_tiled launch");
+  return NSB_OK;
+}
+
+int nsb_dendritic_run_tiled_peers(const nsb_tick* tick, const nsb_tiled_layout* layout,
+                                  int64_t ticks, const nsb_peer_exchange* x,
+                                  const nsb_tick_out* out, void* workspace,
+                                  size_t workspace_bytes, int* status, void* stream) {
+  if (ticks < 1 || ticks > (int64_t{1} << 24))
+    return fail(NSB_ERR_ARGUMENT, "ticks must be in [1, 2^24]");
+  if (!x || x->world < 1 || x->world > NSB_MAX_PEERS || x->rank < 0 || x->rank >= x->world)
+    return fail(NSB_ERR_ARGUMENT, "invalid peer exchange: world / rank");
+  for (int p = 0; p < x->world; ++p)
+    if (!x->gathered[p][0] || !x->gathered[p][1] || !x->counters[p] ||
+        !aligned(x->gathered[p][0], 16) || !aligned(x->gathered[p][1], 16) ||
+        !aligned(x->counters[p], 8))
+      return fail(NSB_ERR_ARGUMENT, "invalid peer exchange: buffers missing or misaligned");
+  nsb::TickArgs t;
+  nsb::TickOut o;
+  const float* source = x->gathered[x->rank][0];
+  const int code = check_tiled_tick(tick, layout, &source, out, workspace, workspace_bytes, &t, &o);
+  if (code != NSB_OK) return code;
+  if (x->row_offset < 0 || x->row_offset + layout->rows > layout->cols)
+    return fail(NSB_ERR_ARGUMENT, "invalid peer exchange: rows outside the gathered state");
+  g_error.clear();
+  const cudaError_t err = nsb::launch_tiled(*layout, t, source, true, static_cast<int>(ticks), o,
+                                            nsb::Out{nullptr, 0, 0}, workspace, status,
+                                            static_cast<cudaStream_t>(stream), x);
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_run_tiled_peers launch");
+  return NSB_OK;
+}
+
+namespace {
+// cuMemGetAddressRange through the runtime's driver entry point (no -lcuda).
+using AddressRange = int (*)(unsigned long long*, size_t*, unsigned long long);
+}  // namespace
+
+int nsb_ipc_export(const void* device_ptr, void* handle, uint64_t* offset) {
+  if (!device_ptr || !handle || !offset) return fail(NSB_ERR_ARGUMENT, "ipc export: null argument");
+  static AddressRange range = nullptr;
+  if (!range) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult found;
+    const cudaError_t err = cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault,
+                                                    &found);
+    if (err != cudaSuccess || found != cudaDriverEntryPointSuccess || !fn)
+      return fail(NSB_ERR_CUDA, "ipc export: cuMemGetAddressRange is unavailable");
+    range = reinterpret_cast<AddressRange>(fn);
+  }
+  unsigned long long base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<unsigned long long>(device_ptr)) != 0)
+    return fail(NSB_ERR_ARGUMENT, "ipc export: not a device allocation");
+  cudaIpcMemHandle_t h;
+  const cudaError_t err = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (err != cudaSuccess) return cuda_fail(err, "ipc export");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = reinterpret_cast<unsigned long long>(device_ptr) - base;
+  return NSB_OK;
+}
+
+int nsb_ipc_import(const void* handle, void** base) {
+  if (!handle || !base) return fail(NSB_ERR_ARGUMENT, "ipc import: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t err = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) return cuda_fail(err, "ipc import");
+  return NSB_OK;
+}
+
+int nsb_ipc_release(void* base) {
+  if (!base) return fail(NSB_ERR_ARGUMENT, "ipc release: null base");
+  const cudaError_t err = cudaIpcCloseMemHandle(base);
+  if (err != cudaSuccess) return cuda_fail(err, "ipc release");
   return NSB_OK;
 }
 

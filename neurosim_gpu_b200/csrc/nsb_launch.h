@@ -54,7 +54,8 @@ size_t tiled_smem_bytes(int block_cols, int buffers);
 size_t tiled_workspace_bytes(const nsb_tiled_layout& layout);
 cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, const float* x,
                          bool update, int ticks, const TickOut& out, const Out& product,
-                         void* workspace, int* status, cudaStream_t stream);
+                         void* workspace, int* status, cudaStream_t stream,
+                         const nsb_peer_exchange* exchange = nullptr);
 
 cudaError_t launch_event(const TickArgs& t, const EventArgs& e, const TickOut& out,
                          const Out& out_emitted, void* workspace, cudaStream_t stream);

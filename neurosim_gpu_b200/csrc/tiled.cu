@@ -340,10 +340,51 @@ __device__ void grid_barrier(unsigned long long* count, int* st) {
   __syncthreads();
 }
 
+// The peer exchange of a row-sharded run (world == 0: none).
+struct Peers {
+  int32_t world, rank;
+  int64_t row_offset;
+  float* gathered[NSB_MAX_PEERS][2];
+  unsigned long long* counters[NSB_MAX_PEERS];
+  unsigned long long epoch;
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// End-of-tick barrier across ranks, for one thread per CTA after a
+// __syncthreads that follows the CTA's peer stores (each storing thread has
+// fenced them at system scope): all CTAs of this rank meet at the local grid
+// barrier, CTA 0 then adds one to every rank's counter, and every CTA waits
+// until its rank's counter shows all ranks' arrivals for this tick.  Bounded:
+// on timeout it records code 6.
+__device__ void peer_barrier(const Peers& px, unsigned long long* local, int tick, int* st) {
+  grid_arrive_wait(local, st);
+  if (blockIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < px.world; ++p) atomicAdd_system(px.counters[p], 1ull);
+  }
+  const unsigned long long target =
+      static_cast<unsigned long long>(px.world) * (px.epoch + static_cast<unsigned long long>(tick) + 1);
+  long long polls = 0;
+  while (ld_acquire_sys(px.counters[px.rank]) < target) {
+    if (++polls > (1 << 16)) {
+      if (polls > kGridWaitLimit) {
+        atomicExch(st, 6);
+        break;
+      }
+      __nanosleep(256);
+    }
+  }
+}
+
 template <typename W, int D>
 __global__ void __launch_bounds__(kTiledThreads, 1)
 tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ x0, TickOut out,
-                  Out product, bool update, int ticks, int* status) {
+                  Out product, bool update, int ticks, int* status, Peers px) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int nbuf = L.buffers;
   const int cb_pad = L.block_cols + 4;
@@ -411,7 +452,8 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
   };
 
   for (int tick = 0; tick < ticks; ++tick) {
-    const float* x = tick == 0 ? x0 : out.s.data;
+    const bool exchange = px.world > 0;
+    const float* x = exchange ? px.gathered[px.rank][tick & 1] : tick == 0 ? x0 : out.s.data;
     const int use0 = tick * stages;
     if (warp == kProducerWarp) {
       // All 32 lanes prefetch tasks (each lane one task's metadata load and
@@ -428,7 +470,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
         // The consumer warps meanwhile start loading the tick's edges; they
         // touch the row sums only after the staged block arrives, so they
         // are ordered after the barrier through the block's mbarrier.
-        if (tick > 0) grid_arrive_wait(L.barrier, st);
+        if (tick > 0 && !exchange) grid_arrive_wait(L.barrier, st);
         // The state was written by other CTAs' generic stores before the grid
         // barrier; order those writes before this thread's async-proxy reads.
         asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -477,7 +519,8 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
           base = t.p.data[lane];
           stride = t.p.stride[lane];
         } else {
-          const View v = lane == 6 ? (tick == 0 ? t.s : View{out.s.data, out.s.sb, out.s.sn, 0.0f})
+          const View v = lane == 6 ? (exchange ? View{px.gathered[px.rank][tick & 1] + px.row_offset, 0, 1, 0.0f}
+                                     : tick == 0 ? t.s : View{out.s.data, out.s.sb, out.s.sn, 0.0f})
                        : lane == 7 ? (tick == 0 ? t.d : View{out.d.data, out.d.sb, out.d.sn, 0.0f})
                                    : (tick == 0 ? t.a : View{out.a.data, out.a.sb, out.a.sn, 0.0f});
           base = v.data;
@@ -606,7 +649,11 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
 #pragma unroll
         for (int i = 0; i < 6; ++i) pr[r][i] = 0.0f;
         if (row && update) {  // tick operands exist only for a tick
-          if (tick == 0) {
+          if (exchange) {
+            s0[r] = __ldcg(px.gathered[px.rank][tick & 1] + px.row_offset + n);
+            d0[r] = tick == 0 ? t.d.at(0, n) : __ldcg(out.d.data + n * out.d.sn);
+            a0[r] = tick == 0 ? t.a.at(0, n) : __ldcg(out.a.data + n * out.a.sn);
+          } else if (tick == 0) {
             s0[r] = t.s.at(0, n);
             d0[r] = t.d.at(0, n);
             a0[r] = t.a.at(0, n);
@@ -641,7 +688,11 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
         if (update) {
           const Update q = advance(j[r], s0[r], d0[r], a0[r], u[r], v[r], pr[r][0], pr[r][1],
                                    pr[r][2], pr[r][3], pr[r][4], pr[r][5]);
-          out.s.put(0, n, q.s);
+          if (exchange) {  // the new soma value of row n goes to every rank's next buffer
+            for (int p = 0; p < px.world; ++p) px.gathered[p][(tick + 1) & 1][px.row_offset + n] = q.s;
+          } else {
+            out.s.put(0, n, q.s);
+          }
           out.d.put(0, n, q.d);
           out.a.put(0, n, q.a);
         } else {
@@ -649,7 +700,13 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
         }
       }
     }
-    __syncthreads();  // this CTA's update is done (the producer's barrier orders it)
+    if (exchange) {
+      __threadfence_system();  // this thread's peer stores, before the ranks' barrier
+      __syncthreads();
+      if (warp == kProducerWarp && lane == 0) peer_barrier(px, L.barrier, tick, st);
+    } else {
+      __syncthreads();  // this CTA's update is done (the producer's barrier orders it)
+    }
   }
 }
 
@@ -657,7 +714,7 @@ template <typename W, int D>
 cudaError_t launch_tiled_variant(const TiledArgs& L, const W& w, const TickArgs& t,
                                  const float* x, const TickOut& out, const Out& product,
                                  bool update, int ticks, int* status, int ctas,
-                                 cudaStream_t stream) {
+                                 cudaStream_t stream, const Peers& px) {
   const size_t smem = tiled_smem_bytes(L.block_cols, L.buffers);
   auto kernel = tiled_tick_kernel<W, D>;
   static int configured[64] = {0};
@@ -681,7 +738,7 @@ cudaError_t launch_tiled_variant(const TiledArgs& L, const W& w, const TickArgs&
   attribute[0].val.cooperative = 1;
   config.attrs = attribute;
   config.numAttrs = 1;
-  return cudaLaunchKernelEx(&config, kernel, L, w, t, x, out, product, update, ticks, status);
+  return cudaLaunchKernelEx(&config, kernel, L, w, t, x, out, product, update, ticks, status, px);
 }
 
 }  // namespace
@@ -697,7 +754,20 @@ size_t tiled_workspace_bytes(const nsb_tiled_layout& layout) {
 
 cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, const float* x,
                          bool update, int ticks, const TickOut& out, const Out& product,
-                         void* workspace, int* status, cudaStream_t stream) {
+                         void* workspace, int* status, cudaStream_t stream,
+                         const nsb_peer_exchange* exchange) {
+  Peers px{};
+  if (exchange) {
+    px.world = exchange->world;
+    px.rank = exchange->rank;
+    px.row_offset = exchange->row_offset;
+    for (int p = 0; p < exchange->world; ++p) {
+      px.gathered[p][0] = exchange->gathered[p][0];
+      px.gathered[p][1] = exchange->gathered[p][1];
+      px.counters[p] = exchange->counters[p];
+    }
+    px.epoch = exchange->epoch;
+  }
   TiledArgs L;
   L.stage_ptr = layout.stage_ptr;
   L.stage_block = layout.stage_block;
@@ -729,19 +799,19 @@ cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, cons
     case NSB_WEIGHT_F16:
       return launch_tiled_variant<ChunkF16, 4>(L, ChunkF16{static_cast<const __half*>(layout.weight)},
                                                t, x, out, product, update, ticks, status, ctas,
-                                               stream);
+                                               stream, px);
     case NSB_WEIGHT_E4M3:
       return launch_tiled_variant<ChunkE4M3, 4>(
           L, ChunkE4M3{static_cast<const uint8_t*>(layout.weight), 0.0f}, t, x, out, product,
-          update, ticks, status, ctas, stream);
+          update, ticks, status, ctas, stream, px);
     case NSB_WEIGHT_NVFP4:
       return launch_tiled_variant<ChunkNVFP4, 4>(
           L, ChunkNVFP4{static_cast<const uint8_t*>(layout.weight), layout.scale_pairs, 0.0f}, t,
-          x, out, product, update, ticks, status, ctas, stream);
+          x, out, product, update, ticks, status, ctas, stream, px);
     default:
       return launch_tiled_variant<ChunkF32, 4>(L, ChunkF32{static_cast<const float*>(layout.weight)},
                                                t, x, out, product, update, ticks, status, ctas,
-                                               stream);
+                                               stream, px);
   }
 }
 

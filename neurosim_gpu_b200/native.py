@@ -88,6 +88,17 @@ class _TiledLayout(ctypes.Structure):
                 ("global_scale", ctypes.c_void_p)]
 
 
+MAX_PEERS = 8
+
+
+class _PeerExchange(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("row_offset", ctypes.c_int64),
+                ("gathered", (ctypes.c_void_p * 2) * MAX_PEERS),
+                ("counters", ctypes.c_void_p * MAX_PEERS),
+                ("epoch", ctypes.c_uint64)]
+
+
 class EventCounters(ctypes.Structure):
     """Head of the nsb_dendritic_event workspace (nsb_event_counters)."""
 
@@ -99,7 +110,8 @@ class EventCounters(ctypes.Structure):
 EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_dendritic_event_workspace_size", "nsb_dendritic_event",
                     "nsb_tiled_smem_bytes", "nsb_tiled_workspace_size", "nsb_dendritic_step_tiled",
-                    "nsb_dendritic_run_tiled", "nsb_tiled_propagate",
+                    "nsb_dendritic_run_tiled", "nsb_dendritic_run_tiled_peers",
+                    "nsb_ipc_export", "nsb_ipc_import", "nsb_ipc_release", "nsb_tiled_propagate",
                     "nsb_dendritic_event_noalloc", "nsb_dendritic_step_rows",
                     "nsb_last_error", "nsb_abi_version")
 
@@ -132,6 +144,12 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_dendritic_run_tiled.argtypes = [p(_Tick), p(_TiledLayout), ctypes.c_int64,
                                             p(_TickOut), ctypes.c_void_p, ctypes.c_size_t,
                                             ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_dendritic_run_tiled_peers.argtypes = [p(_Tick), p(_TiledLayout), ctypes.c_int64,
+                                                  p(_PeerExchange), p(_TickOut), ctypes.c_void_p,
+                                                  ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_ipc_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]
+    lib.nsb_ipc_import.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+    lib.nsb_ipc_release.argtypes = [ctypes.c_void_p]
     lib.nsb_dendritic_step_rows.argtypes = [p(_Tick), p(_Csr), p(_View), ctypes.c_int64,
                                             ctypes.c_int32, p(_TickOut), ctypes.c_void_p]
     lib.nsb_tiled_propagate.argtypes = [ctypes.c_int64, p(_TiledLayout), ctypes.c_void_p,
@@ -144,9 +162,35 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
         getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
-    if lib.nsb_abi_version() != 3:
+    if lib.nsb_abi_version() != 4:
         raise RuntimeError("libneurosim_b200.so ABI version mismatch")
     return lib
+
+
+def ipc_export(tensor: torch.Tensor) -> tuple[bytes, int]:
+    """(64-byte CUDA IPC handle of the tensor's allocation, byte offset of the tensor)."""
+    lib = load_library()
+    handle = ctypes.create_string_buffer(64)
+    offset = ctypes.c_uint64()
+    with torch.cuda.device(tensor.device):
+        _raise_on_status(lib, lib.nsb_ipc_export(tensor.data_ptr(), handle, ctypes.byref(offset)))
+    return handle.raw, int(offset.value)
+
+
+def ipc_import(handle: bytes, device: torch.device) -> int:
+    """Map another process's allocation into ``device`` (peer access on); its base address."""
+    lib = load_library()
+    base = ctypes.c_void_p()
+    with torch.cuda.device(device):
+        _raise_on_status(lib, lib.nsb_ipc_import(ctypes.create_string_buffer(handle, 64),
+                                                 ctypes.byref(base)))
+    return int(base.value)
+
+
+def ipc_release(base: int, device: torch.device) -> None:
+    lib = load_library()
+    with torch.cuda.device(device):
+        _raise_on_status(lib, lib.nsb_ipc_release(base))
 
 
 def _check(ok: bool, message: str) -> None:
@@ -354,6 +398,42 @@ class DendriticExtension:
                         ctypes.byref(tick), ctypes.byref(c_layout), int(ticks),
                         ctypes.byref(result), workspace.data_ptr(), workspace.numel(), status_ptr,
                         _stream(device))
+            _raise_on_status(lib, code)
+
+        return launch
+
+    def prepare_run_tiled_peers(self, state, dendrite, adaptation, params, layout, input,
+                                input_scalar, dendritic_input, dendritic_scalar, *, out, ticks,
+                                exchange, status=None):
+        """A launch callable for ``ticks`` row-sharded ticks with the exchange in the kernel.
+
+        ``exchange`` is a :class:`_PeerExchange` (see ``nsb_dendritic_run_tiled_peers``);
+        ``state`` is this rank's rows of the current gathered buffer, ``out`` the
+        rows' dendrite / adaptation outputs (``out[0]`` is not written).
+        """
+        _check_state(state)
+        _check(state.size(0) == 1, "the tiled tick takes B = 1")
+        _check(layout.neurons == state.size(1), "layout and state neuron counts differ")
+        tick = _tick(state, dendrite, adaptation, params, input, input_scalar,
+                     dendritic_input, dendritic_scalar)
+        for view in out:
+            _float_on(view, state)
+            _check(view.shape == state.shape, "output shape mismatch")
+        result = _TickOut(_out(out[0]), _out(out[1]), _out(out[2]))
+        c_layout = layout.c_struct()
+        workspace = layout.workspace()
+        status_ptr = status.data_ptr() if status is not None else None
+        lib, device = self.lib, state.device
+        keep = (state, dendrite, adaptation, params, layout, input, dendritic_input, out, status,
+                workspace, exchange)
+
+        def launch() -> None:
+            assert keep is not None
+            with torch.cuda.device(device):
+                code = lib.nsb_dendritic_run_tiled_peers(
+                    ctypes.byref(tick), ctypes.byref(c_layout), int(ticks), ctypes.byref(exchange),
+                    ctypes.byref(result), workspace.data_ptr(), workspace.numel(), status_ptr,
+                    _stream(device))
             _raise_on_status(lib, code)
 
         return launch

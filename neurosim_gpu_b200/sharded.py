@@ -109,7 +109,8 @@ class ShardedDendriticMatrixRuntime:
     def __init__(self, graph, dynamics: DendriticDynamics, initial_state: torch.Tensor, *,
                  group=None, precision: str = "fp32", kernel: str = "auto",
                  threads_per_row: int | None = None, extension=None,
-                 rank: int | None = None, world: int | None = None) -> None:
+                 rank: int | None = None, world: int | None = None,
+                 exchange: str = "auto") -> None:
         if isinstance(graph, tuple):
             in_rowptr, in_col, in_weight = graph
         else:
@@ -118,6 +119,8 @@ class ShardedDendriticMatrixRuntime:
             raise ValueError("native compartment runtime requires CUDA float32")
         if kernel not in ("auto", "csr", "tiled"):
             raise ValueError("kernel must be 'auto', 'csr' or 'tiled'")
+        if exchange not in ("auto", "nccl", "peer"):
+            raise ValueError("exchange must be 'auto', 'nccl' or 'peer'")
         self.group = group
         # rank / world may be given explicitly to build one rank's share without a
         # process group (the exchange is then up to the caller).
@@ -166,6 +169,66 @@ class ShardedDendriticMatrixRuntime:
         degree = self.n_edges / max(neurons, 1)
         self.threads_per_row = threads_per_row or (8 if degree <= 16 else 16 if degree <= 48
                                                    else 32)
+        # In-kernel peer exchange (run() at B = 1): every rank maps every other
+        # rank's gathered buffers and arrival counter through CUDA IPC.
+        self._peer = None
+        self._peer_epoch = 0
+        self._peer_bases: list[int] = []
+        wants_peer = exchange == "peer" or (exchange == "auto" and rank is None)
+        if (wants_peer and self.world > 1 and self.world <= _native.MAX_PEERS
+                and self.layout is not None and dist.is_initialized()):
+            self._setup_peer_exchange()
+        elif exchange == "peer" and self.world > 1:
+            raise ValueError("the peer exchange needs B = 1, the tiled path, <= 8 ranks and "
+                             "a process group")
+
+    def _setup_peer_exchange(self) -> None:
+        """Map the other ranks' gathered buffers and counters (collective)."""
+        device = self.shard.device
+        self._counters = torch.zeros(32, dtype=torch.int64, device=device)  # [0] is the counter
+        mine = [_native.ipc_export(t) for t in (*self.shard.buffers, self._counters)]
+        table = [None] * self.world
+        dist.all_gather_object(table, (self.rank, torch.cuda.current_device(), mine),
+                               group=self.group)
+        if len({entry[1] for entry in table}) != self.world:
+            raise RuntimeError("the peer exchange needs one GPU per rank")
+        pointers = [[0, 0, 0] for _ in range(self.world)]
+        for rank, _, handles in table:
+            if rank == self.rank:
+                pointers[rank] = [t.data_ptr() for t in (*self.shard.buffers, self._counters)]
+                continue
+            for i, (handle, offset) in enumerate(handles):
+                base = _native.ipc_import(handle, device)
+                self._peer_bases.append(base)
+                pointers[rank][i] = base + offset
+        self._peer = pointers
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)
+
+    def _exchange(self) -> "_native._PeerExchange":
+        x = _native._PeerExchange()
+        x.world, x.rank, x.row_offset = self.world, self.rank, self.shard.lo
+        cur = self.shard.current
+        for p, (b0, b1, counter) in enumerate(self._peer):
+            x.gathered[p][0], x.gathered[p][1] = (b0, b1) if cur == 0 else (b1, b0)
+            x.counters[p] = counter
+        x.epoch = self._peer_epoch
+        return x
+
+    @property
+    def exchange(self) -> str:
+        """'peer' (soma exchange inside the tick kernel) or 'nccl' (all-gather)."""
+        return "peer" if self._peer is not None else "nccl"
+
+    def close(self) -> None:
+        """Unmap the other ranks' buffers (collective: every rank calls it)."""
+        if self._peer is not None:
+            torch.cuda.synchronize(self.shard.device)
+            dist.barrier(group=self.group)
+            for base in self._peer_bases:
+                _native.ipc_release(base, self.shard.device)
+            self._peer_bases, self._peer = [], None
+            dist.barrier(group=self.group)
 
     @property
     def kernel_path(self) -> str:
@@ -228,6 +291,38 @@ class ShardedDendriticMatrixRuntime:
 
     def run(self, ticks: int, drive=0.0, *, dendritic_drive=0.0, graph_ticks: int = 32
             ) -> torch.Tensor:
+        """``ticks`` ticks with fixed drives (every rank calls it); the full state.
+
+        With the peer exchange, one persistent kernel per rank runs all ticks;
+        otherwise a CUDA graph of ``graph_ticks`` ticks + NCCL all-gathers is
+        replayed.  Either way the result equals ``ticks`` calls of :meth:`step`.
+        """
+        if self._peer is not None and ticks > 0:
+            return self._run_peer(ticks, drive, dendritic_drive)
+        return self._run_graph(ticks, drive, dendritic_drive, graph_ticks)
+
+    def _run_peer(self, ticks: int, drive, dendritic_drive) -> torch.Tensor:
+        """All ``ticks`` ticks in one cooperative launch per rank, exchanging the
+        soma vector inside the kernel (peer stores + a cross-GPU barrier)."""
+        u, us, v, vs = self._drives(drive, dendritic_drive)
+        # Every rank's earlier work on the gathered buffers (NCCL exchanges of
+        # step()) must be finished before any rank's kernel writes into them.
+        torch.cuda.current_stream(self.shard.device).synchronize()
+        dist.barrier(group=self.group)
+        s_rows = self.shard.own(self.shard.current)
+        out_d = torch.empty_like(self.dendritic_state)
+        out_a = torch.empty_like(self.adaptation_state)
+        self.extension.prepare_run_tiled_peers(
+            s_rows, self.dendritic_state, self.adaptation_state, self.params, self.layout,
+            u, us, v, vs, out=(s_rows, out_d, out_a), ticks=ticks, exchange=self._exchange(),
+            status=self.status)()
+        self.dendritic_state, self.adaptation_state = out_d, out_a
+        self.shard.current = (self.shard.current + ticks) % 2
+        self._peer_epoch += ticks
+        self._tick += ticks
+        return self.state
+
+    def _run_graph(self, ticks: int, drive, dendritic_drive, graph_ticks: int) -> torch.Tensor:
         """``ticks`` ticks with fixed drives, replaying a CUDA graph of ticks + all-gathers."""
         graph_ticks = max(2, min(graph_ticks, ticks) // 2 * 2)
         if ticks < graph_ticks:
