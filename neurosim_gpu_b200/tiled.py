@@ -59,12 +59,14 @@ MAX_BLOCK_COLS = 65504        # 16-bit block-relative columns, block_cols = padd
 MAX_ROWS = (1 << 28) - 1      # 28-bit rows in task_rows; ROW_NONE marks a padding lane
 ROW_NONE = MAX_ROWS
 WARPS = 31                    # consumer warps of a CTA
-# Target number of sub-tasks each consumer warp runs per tick, by weight format
-# (0: tasks are not split).  Splitting shortens the tail of a tick but adds
-# row-sum planes that the update reads; measured at 166k / 25M it pays off for
-# fp32 (39.7 vs 42.6 us) and costs the narrower formats (fp16 30.6 vs 33.7 us).
-SUBTASKS_PER_WARP = {native.F32: 5, native.F16: 0, native.E4M3: 0, native.NVFP4: 0}
-MAX_PLANES = 12               # cap on blocks x splits (row-sum planes of the workspace)
+# Split length of sub-tasks in chunks (4 edges), by weight format (0: tasks
+# are not split).  Splitting shortens the tail of a tick but adds row-sum
+# planes that the update reads; measured at 166k / 25M it pays off for fp32
+# (39.7 vs 42.6 us with splits of 9 chunks) and costs the narrower formats
+# (fp16 30.6 vs 33.7 us).  A constant length cuts every row at the same edges
+# whatever rows a layout holds, so sharded sums stay bit-identical.
+SPLIT_CHUNKS = {native.F32: 9, native.F16: 0, native.E4M3: 0, native.NVFP4: 0}
+MAX_PLANES = 32               # cap on blocks x splits (only degree-skewed graphs reach it)
 
 
 def _u16(values: torch.Tensor) -> torch.Tensor:
@@ -337,15 +339,15 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
         tiled_weight[slot] = weight
     # Sub-tasks: chunks [h * split, (h + 1) * split) of a task.
     longest = int(task_chunks.max()) if n_tasks else 1
-    target = SUBTASKS_PER_WARP.get(fmt, 0)
-    if target > 0:
-        per_cta = slots // CHUNK_SLOTS / max(ctas, 1)
-        split = max(1, round(per_cta / (WARPS * target)))
-        split = max(split, -(-longest // max(1, MAX_PLANES // blocks)))
+    split = SPLIT_CHUNKS.get(fmt, 0)
+    if split > 0:
+        if blocks * -(-longest // split) > MAX_PLANES:  # a degree-skewed graph
+            split = -(-longest // max(1, MAX_PLANES // blocks))
     else:
-        split = longest
-    split = max(1, min(split, longest))
+        split = 1 << 30
+    split = max(1, min(split, 1 << 30))
     splits = max(1, -(-longest // split))
+    split = min(split, max(longest, 1))
     n_sub = (task_chunks + split - 1) // split
     sub_task = torch.repeat_interleave(arange(n_tasks), n_sub)
     sub_h = arange(sub_task.numel()) - (torch.cumsum(n_sub, 0) - n_sub)[sub_task]

@@ -173,3 +173,22 @@ def test_in_kernel_decoders_exhaustive():
     got = ext.tiled_propagate(layout, torch.ones(1, n, device="cuda"))
     want = e2m1_to_float(nib.to(torch.uint8)) * (e4m3_to_float(scales).repeat_interleave(16) * g)
     np.testing.assert_array_equal(npy(got)[0], npy(want))
+
+
+def test_sharded_layouts_split_rows_like_the_whole_graph_cpu():
+    """Split points depend only on the graph, not on which rows a layout holds."""
+    n, m = 9001, 600000
+    graph = random_topology(n, m, device="cpu", seed=6)
+    rowptr = graph.in_rowptr.long()
+    smem = _smem_bytes()
+    whole = build_tiled_layout(graph.in_rowptr, graph.in_col, graph.in_weight, neurons=n, ctas=20,
+                               smem_limit=12000, smem_bytes=smem)
+    assert whole.splits > 1
+    for lo, hi in ((0, 4501), (4501, 9001)):
+        e0, e1 = int(rowptr[lo]), int(rowptr[hi])
+        part = build_tiled_layout((rowptr[lo:hi + 1] - e0).to(torch.int32),
+                                  graph.in_col[e0:e1].contiguous(), graph.in_weight[e0:e1],
+                                  neurons=hi - lo, cols=n, ctas=20, smem_limit=12000,
+                                  smem_bytes=smem)
+        assert (part.blocks, part.block_cols, part.split_chunks) == \
+            (whole.blocks, whole.block_cols, whole.split_chunks)
