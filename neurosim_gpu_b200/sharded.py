@@ -133,6 +133,7 @@ class ShardedDendriticMatrixRuntime:
         self.shard = RowShard(neurons, batch, self.rank, self.world, device)
         lo, hi = self.shard.lo, self.shard.hi
         self.compartment_dynamics = dynamics
+        self._source_csr = (in_rowptr, in_col, in_weight.detach())
         self.params = [p[lo:hi] for p in dynamics.parameters()]
         self.shard.load(initial_state)
         self.dendritic_state = torch.zeros(batch, hi - lo, device=device)
@@ -214,6 +215,13 @@ class ShardedDendriticMatrixRuntime:
             x.counters[p] = counter
         x.epoch = self._peer_epoch
         return x
+
+    def same_weights(self, in_rowptr: torch.Tensor, in_col: torch.Tensor,
+                     in_weight: torch.Tensor) -> bool:
+        """Whether a destination CSR equals the one this run was built from."""
+        mine = self._source_csr
+        return all(a.numel() == b.numel() and torch.equal(a.to(b.device), b)
+                   for a, b in zip((in_rowptr, in_col, in_weight), mine))
 
     @property
     def exchange(self) -> str:

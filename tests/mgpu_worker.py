@@ -5,6 +5,9 @@ Modes (argv[1]):
            the single-GPU runtime on rank 0: prints "PARITY <case> <bool>".
   timeout  rank 1 stays alive but does not launch; rank 0's kernel must end
            with status code 6 (its cross-GPU barrier gave up): prints "STATUS <code>".
+  checkpoint  a sharded run is captured into one payload and restored into a
+           fresh sharded run and into a single-GPU runtime; both continue bit
+           for bit like the original: prints "CHECKPOINT <case> <bool>".
 """
 
 from __future__ import annotations
@@ -82,13 +85,50 @@ def timeout(device, rank):
     rt.close()
 
 
+def checkpoint(device, rank):
+    from neurosim_gpu_b200.checkpoint import (capture_sharded_runtime, restore_runtime,
+                                              restore_sharded_runtime)
+    n, m = 20011, 500000
+    graph = broadcast_graph(n, m, seed=4, device=device)
+    dyn = model(n, device)
+    init = torch.rand(1, n, generator=torch.Generator().manual_seed(3)).to(device)
+    rt = ShardedDendriticMatrixRuntime(graph, dyn, init)
+    with torch.inference_mode():
+        rt.run(6, 0.2, dendritic_drive=0.1)
+    topology = random_topology(n, m, device="cpu", seed=4) if rank == 0 else None
+    payload = capture_sharded_runtime(rt, topology)
+    with torch.inference_mode():
+        rt.run(5, 0.2, dendritic_drive=0.1)
+    want = rt.state.clone()
+    box = [payload]
+    dist.broadcast_object_list(box, src=0)
+    again = ShardedDendriticMatrixRuntime(graph, dyn, torch.zeros(1, n, device=device))
+    restore_sharded_runtime(again, box[0])
+    with torch.inference_mode():
+        again.run(5, 0.2, dendritic_drive=0.1)
+    same_sharded = torch.equal(again.state, want)
+    for runtime in (rt, again):
+        runtime.release_graphs()
+        runtime.close()
+    if rank == 0:
+        print(f"CHECKPOINT sharded {same_sharded}", flush=True)
+        single = NativeDendriticMatrixRuntime(topology.to(device), dyn,
+                                              torch.zeros(1, n, device=device))
+        restore_runtime(single, payload)
+        with torch.inference_mode():
+            single.run(5, 0.2, dendritic_drive=0.1)
+        print(f"CHECKPOINT single {torch.equal(single.state, want)}", flush=True)
+    dist.barrier()
+
+
 def main():
     local = int(os.environ["LOCAL_RANK"])
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     try:
-        {"parity": parity, "timeout": timeout}[sys.argv[1]](device, dist.get_rank())
+        {"parity": parity, "timeout": timeout, "checkpoint": checkpoint}[sys.argv[1]](
+            device, dist.get_rank())
     finally:
         dist.destroy_process_group()
 

@@ -57,3 +57,13 @@ def test_missing_rank_ends_the_cross_gpu_barrier_with_a_status():
     out = _run("timeout")
     codes = [int(line.split()[1]) for line in out.splitlines() if line.startswith("STATUS")]
     assert codes == [6], out
+
+
+@pytest.mark.gpu
+@needs_two
+def test_sharded_checkpoint_restores_sharded_and_single_gpu():
+    out = _run("checkpoint")
+    lines = [line.split() for line in out.splitlines() if line.startswith("CHECKPOINT")]
+    assert [case for _, case, _ in lines] == ["sharded", "single"], out
+    for _, case, ok in lines:
+        assert ok == "True", case
