@@ -36,6 +36,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -64,7 +65,13 @@ WORKLOADS = {
     "matrix_n50k_m1M_b8_fp32": (50_000, 1_000_000, 8, "fp32"),
     "matrix_n4096_m65k_b1_fp32": (4096, 65_536, 1, "fp32"),
     "matrix_n1330k_m200M_b1_fp32": (1_330_000, 200_000_000, 1, "fp32"),
+    # PELS (event) ticks, theta = 0.02 (166k / 25M for the
+    # reference's published PELS number)
+    "pels_n50k_m1M_b1_t0.02": (50_000, 1_000_000, 1, "fp32"),
+    "pels_n50k_m1M_b8_t0.02": (50_000, 1_000_000, 8, "fp32"),
+    "pels_n166k_m25M_b1_t0.02": (166_000, 25_000_000, 1, "fp32"),
 }
+PELS_THETA = 0.02
 DEFAULT_WORKLOAD = "matrix_n166k_m25M_b1_fp32"
 WEIGHT_BYTES = {"fp32": 4.0, "fp16": 2.0, "fp8": 1.0, "nvfp4": 0.5 + 1.0 / 16.0}
 FALLBACK_HBM_GBS = 6650.0
@@ -205,7 +212,70 @@ def run_reference(args, workload: str, explicit_workload: bool, world: int) -> d
     }
 
 
+def run_pels(args, workload: str) -> dict:
+    """PELS ticks (advance + emit, active-edge scatter) replayed from a CUDA graph."""
+    from neurosim_gpu_b200 import NativeDendriticPELSRuntime
+
+    neurons, edges, batch, _ = WORKLOADS[workload]
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    graph = build_graph(neurons, edges, device)
+    model = bench_model(neurons, device)
+    # The reference's PELS benchmark drive, 0.2 + 0.1 sin(0.11 t) (benchmarks/compartmental.py),
+    # as a 64-tick cycle; at B = 8 each batch row adds its own offset drawn U[0, 0.4] - 0.2.
+    chunk = 64
+    offset = 0.0 if batch == 1 else ((torch.rand(batch, 1, generator=torch.Generator()
+                                                 .manual_seed(0)) * 0.4 - 0.2).to(device))
+    drive = [offset + 0.2 + 0.1 * math.sin(0.11 * t) for t in range(chunk)]
+    runtime = NativeDendriticPELSRuntime(graph, model, torch.zeros(batch, neurons, device=device),
+                                         theta=PELS_THETA)
+    steps = max(args.steps - args.steps % chunk, chunk)
+    with torch.inference_mode():
+        runtime.run(max(args.warmup, chunk), drive, dendritic_drive=0.1, graph_ticks=chunk)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        runtime.run(steps, drive, dendritic_drive=0.1, graph_ticks=chunk)
+        e1.record()
+        e1.synchronize()
+        tick_ms = e0.elapsed_time(e1) / steps
+        # Activity over one drive cycle after the timed ticks (eager, with statistics).
+        active_neurons = active_edges = 0
+        for t in range(chunk):
+            _, stats = runtime.step(drive[t], dendritic_drive=0.1, collect_stats=True)
+            active_neurons += stats.active_neurons
+            active_edges += stats.active_edges
+        active_neurons, active_edges = active_neurons / chunk, active_edges / chunk
+    m = graph.n_edges
+    # Bytes of one event tick: the advance reads s, d, a, emitted, current and
+    # writes s, d, a, emitted (36 B per pair); the scatter reads dst and weight
+    # and read-modify-writes the current for every active edge (16 B).
+    algo = 36 * batch * neurons + 16 * active_edges
+    peak, peak_kind = hbm_peak()
+    achieved = algo / (tick_ms * 1e-3) / 1e9
+    return {
+        "metric": "synapse-updates/s (M*B/tick)", "value": m * batch / (tick_ms * 1e-3),
+        "unit": "synapse-updates/s", "n_gpus": 1, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": tick_ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (reference random_topology stream, seed 0; drive 0.2 + 0.1 sin(0.11 t) "
+                "over a 64-tick cycle, dendritic 0.1)",
+        "config": {"workload": workload, "neurons": neurons, "edges": m, "batch": batch,
+                   "theta": PELS_THETA, "active_neurons_per_tick": active_neurons,
+                   "active_edges_per_tick": active_edges,
+                   "active_edge_fraction": active_edges / max(m * batch, 1),
+                   "kernel_path": "pels", "ticks_per_graph": chunk},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "algorithmic_bytes_per_launch": algo, "peak_source": peak_kind,
+                     "kernel": "event_advance_kernel + event_scatter_kernel", "per": "tick"},
+        "gpu_launches": 2 * steps,
+    }
+
+
 def run_native(args, workload: str) -> dict:
+    if workload.startswith("pels_"):
+        return run_pels(args, workload)
     neurons, edges, batch, precision = WORKLOADS[workload]
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)

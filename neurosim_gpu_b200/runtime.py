@@ -388,6 +388,65 @@ class _TickGraph:
         return tuple(b.clone() for b in self.buffers[0])
 
 
+class _EventGraph:
+    """A CUDA graph of ``ticks`` PELS ticks from static state buffers."""
+
+    def __init__(self, runtime, ticks: int, u, us, v, vs) -> None:
+        state = runtime.state
+        device = state.device
+        ext, topology = runtime.extension, runtime.topology
+        self.inputs = [torch.empty_like(state, memory_format=torch.contiguous_format)
+                       for _ in range(4)]
+        workspace = runtime._workspace_for(state)
+        params = runtime._parameters()
+        current = runtime.persistent_current
+
+        # u / us: one drive per graph tick, or one for all of them.
+        drive_at = (lambda k: (u[k % len(u)], us[k % len(us)]))
+
+        def ticks_from(inputs):
+            s, d, a, e = inputs
+            for k in range(ticks):
+                uk, usk = drive_at(k)
+                s, d, a, e = ext.dendritic_event(
+                    s, d, a, params, current, e, runtime.theta, topology.out_rowptr,
+                    topology.dst, None, topology.weight.detach(), uk, usk, v, vs,
+                    workspace=workspace)
+            return s, d, a, e
+
+        # Warm-up outside capture must not advance the simulation: run it on
+        # copies and put the current back.
+        saved = current.clone()
+        stream = torch.cuda.Stream(device=device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(stream):
+            for buffer, value in zip(self.inputs, (runtime.state, runtime.dendritic_state,
+                                                   runtime.adaptation_state,
+                                                   runtime.emitted_state)):
+                buffer.copy_(value)
+            ext.dendritic_event(*self.inputs[:3], params, current, self.inputs[3],
+                                runtime.theta, topology.out_rowptr, topology.dst, None,
+                                topology.weight.detach(), *drive_at(0), v, vs,
+                                workspace=workspace)
+            current.copy_(saved)
+        torch.cuda.current_stream(device).wait_stream(stream)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self.final = ticks_from(self.inputs)
+
+    def load(self, s, d, a, e) -> None:
+        for buffer, value in zip(self.inputs, (s, d, a, e)):
+            buffer.copy_(value)
+
+    def replay(self) -> None:
+        self.graph.replay()
+        for target, source in zip(self.inputs, self.final):
+            target.copy_(source)
+
+    def result(self):
+        return tuple(b.clone() for b in self.inputs)
+
+
 class NativeDendriticPELSRuntime(_NativeCompartments):
     """Two CUDA launches per tick: advance + emission, then the active-edge scatter.
 
@@ -475,6 +534,61 @@ class NativeDendriticPELSRuntime(_NativeCompartments):
             workspace[: ctypes.sizeof(_native.EventCounters)].cpu().numpy().tobytes())
         active, edges = int(counters.active_neurons), int(counters.active_edges)
         return self.state, RuntimeStats("event" if active else "idle", active, edges)
+
+    def run(self, ticks: int, drive: torch.Tensor | float = 0.0, *,
+            dendritic_drive: torch.Tensor | float = 0.0, graph_ticks: int = 64) -> torch.Tensor:
+        """Advance ``ticks`` ticks; returns the final state.
+
+        ``graph_ticks`` event ticks (advance + emit, scatter) are captured once
+        into a CUDA graph over static state buffers and replayed; the
+        persistent current is updated in place.  ``drive`` is a float, a
+        tensor broadcastable to [B, N], or a list of ``graph_ticks`` such drives
+        (tick t of every replay uses ``drive[t % graph_ticks]``: a periodic
+        drive).  Equal to ``ticks`` calls of :meth:`step` with the same drives
+        up to the summation order of the scatter's float atomics.
+        """
+        if ticks < 0:
+            raise ValueError("ticks must be non-negative")
+        cycle = list(drive) if isinstance(drive, (list, tuple)) else None
+        if cycle is not None and len(cycle) != graph_ticks:
+            raise ValueError("a drive cycle needs one drive per graph tick")
+        if self._needs_autograd(drive if cycle is None else 0.0, dendritic_drive):
+            raise RuntimeError("run() is inference-only; use step() for autograd")
+        self._refresh_current()
+        if cycle is None and ticks < graph_ticks or ticks == 0:
+            for _ in range(ticks):
+                self.step(drive, dendritic_drive=dendritic_drive)
+            return self.state
+        if cycle is not None and ticks % graph_ticks:
+            raise ValueError("with a drive cycle, ticks must be a multiple of graph_ticks")
+        graph_ticks = min(graph_ticks, ticks)
+        if not self.persistent_current.is_contiguous():
+            self.persistent_current = self.persistent_current.contiguous()
+        drives = [self._drive(x) for x in (cycle if cycle is not None else [drive])]
+        u = [d[0] for d in drives]
+        us = [d[1] for d in drives]
+        v, vs = self._drive(dendritic_drive, "dendritic_drive")
+        key = (graph_ticks, tuple(self.state.shape),
+               tuple(None if x is None else (x.data_ptr(), x.stride()) for x in u), tuple(us),
+               None if v is None else (v.data_ptr(), v.stride()), vs,
+               self.persistent_current.data_ptr(), self.topology.weight_version)
+        graphs = getattr(self, "_graphs", None)
+        if graphs is None:
+            graphs = self._graphs = {}
+        entry = graphs.get(key)
+        if entry is None:
+            graphs.clear()
+            entry = graphs[key] = _EventGraph(self, graph_ticks, u, us, v, vs)
+        entry.load(self.state, self.dendritic_state, self.adaptation_state, self.emitted_state)
+        for _ in range(ticks // graph_ticks):
+            entry.replay()
+        (self.state, self.dendritic_state, self.adaptation_state,
+         self.emitted_state) = entry.result()
+        self._tick += ticks // graph_ticks * graph_ticks
+        for _ in range(ticks % graph_ticks):
+            self.step(drive, dendritic_drive=dendritic_drive)
+        self.last_backend = "native"
+        return self.state
 
     def _autograd_step(self, drive, dendritic_drive, collect_stats: bool):
         """Differentiable PELS tick (runtime.py:264-314 with the emit rule above)."""

@@ -197,3 +197,41 @@ def test_config2_theta_002_teacher_forced(ext):
         assert active > 0
         total_flips += flips
     assert total_flips <= 10
+
+
+@pytest.mark.parametrize("batch", [1, 4])
+def test_run_graph_equals_steps(ext, batch):
+    """PELS run() (a CUDA graph of event ticks) against step(): equal up to the
+    rounding of the scatter's float atomics; at theta = 0 equal to the matrix path."""
+    from neurosim_gpu_b200 import NativeDendriticMatrixRuntime
+    graph, model, state = make(2000, batch, 60000)
+    stepped = NativeDendriticPELSRuntime(graph, model, state.clone(), theta=0.02)
+    replayed = NativeDendriticPELSRuntime(graph, model, state.clone(), theta=0.02)
+    exact = NativeDendriticPELSRuntime(graph, model, state.clone(), theta=0.0)
+    matrix = NativeDendriticMatrixRuntime(graph, model, state.clone())
+    with torch.inference_mode():
+        for _ in range(70):
+            stepped.step(0.2, dendritic_drive=0.1)
+        replayed.run(70, 0.2, dendritic_drive=0.1, graph_ticks=16)
+        exact.run(70, 0.2, dendritic_drive=0.1, graph_ticks=16)
+        matrix.run(70, 0.2, dendritic_drive=0.1)
+    assert replayed._tick == 70
+    torch.testing.assert_close(replayed.state, stepped.state, atol=1e-5, rtol=0)
+    torch.testing.assert_close(replayed.emitted_state, stepped.emitted_state, atol=1e-5, rtol=0)
+    torch.testing.assert_close(exact.state, matrix.state, atol=2e-5, rtol=0)
+
+
+def test_run_with_a_drive_cycle_equals_steps(ext):
+    """A periodic drive: run() replays the cycle; step() with the same drives agrees."""
+    import math
+    graph, model, state = make(2000, 2, 60000)
+    cycle = [0.2 + 0.1 * math.sin(0.11 * t) for t in range(16)]
+    stepped = NativeDendriticPELSRuntime(graph, model, state.clone(), theta=0.02)
+    replayed = NativeDendriticPELSRuntime(graph, model, state.clone(), theta=0.02)
+    with torch.inference_mode():
+        for t in range(48):
+            stepped.step(cycle[t % 16], dendritic_drive=0.1)
+        replayed.run(48, cycle, dendritic_drive=0.1, graph_ticks=16)
+    torch.testing.assert_close(replayed.state, stepped.state, atol=1e-5, rtol=0)
+    with pytest.raises(ValueError, match="cycle"):
+        replayed.run(20, cycle, dendritic_drive=0.1, graph_ticks=16)
