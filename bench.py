@@ -64,6 +64,7 @@ WORKLOADS = {
     "matrix_n166k_m25M_b8_fp32": (166_000, 25_000_000, 8, "fp32"),
     "matrix_n50k_m1M_b8_fp32": (50_000, 1_000_000, 8, "fp32"),
     "matrix_n4096_m65k_b1_fp32": (4096, 65_536, 1, "fp32"),
+    "matrix_n1000_m20k_b1_fp32": (1000, 20_000, 1, "fp32"),
     "matrix_n1330k_m200M_b1_fp32": (1_330_000, 200_000_000, 1, "fp32"),
     # PELS (event) ticks, theta = 0.02 (166k / 25M for the
     # reference's published PELS number)
@@ -282,13 +283,14 @@ def run_native(args, workload: str) -> dict:
     graph = build_graph(neurons, edges, device)
     model = bench_model(neurons, device)
     runtime = NativeDendriticMatrixRuntime(graph, model, torch.zeros(batch, neurons, device=device),
-                                           precision=precision)
+                                           precision=precision, kernel=args.kernel)
     chunk = 64
-    tiled = runtime.kernel_path == "tiled"
+    path = runtime.kernel_path
+    tiled = path in ("tiled", "cluster")  # one launch runs every tick
     with torch.inference_mode():
         # Warm-up (includes graph capture or the layout build, and weight packing).
         runtime.run(max(args.warmup, 1) * 1, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
-        # B = 1 (tiled): one persistent cooperative launch runs all K ticks; other
+        # B = 1 (tiled / cluster): one launch runs all K ticks; other
         # batches replay a CUDA graph of `chunk` ticks.
         steps = max(args.steps, 1) if tiled else max(args.steps - args.steps % chunk, chunk)
         runtime.run(chunk, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
@@ -365,7 +367,8 @@ def run_native(args, workload: str) -> dict:
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": ncu_traffic(workload),
                      "algorithmic_bytes_per_launch": algo, "peak_source": peak_kind,
-                     "kernel": "tiled_tick_kernel" if layout is not None else "csr_tick_kernel",
+                     "kernel": {"tiled": "tiled_tick_kernel", "cluster": "cluster_tick_kernel"}
+                     .get(path, "csr_tick_kernel"),
                      "per": "tick",
                      "streamed_bytes_per_tick": (layout.stream_bytes() + 28 * batch * neurons
                                                  + 8 * layout.blocks * layout.splits * neurons
@@ -527,6 +530,8 @@ def main() -> None:
     parser.add_argument("--workload", choices=sorted(WORKLOADS), default=None)
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--skip-cpu-baseline", action="store_true")
+    parser.add_argument("--kernel", choices=("auto", "csr", "tiled", "cluster"), default="auto",
+                        help="matrix tick path (auto: cluster for small graphs, tiled at B = 1)")
     parser.add_argument("--profile", action="store_true",
                         help="eager launches only, for ncu captures (prints no bench line)")
     parser.add_argument("--launch-ticks", type=int, default=1,

@@ -45,7 +45,7 @@ extern "C" {
 #define NSB_API
 #endif
 
-#define NSB_ABI_VERSION 4
+#define NSB_ABI_VERSION 5
 
 enum nsb_status {
   NSB_OK = 0,
@@ -276,6 +276,27 @@ NSB_API int nsb_dendritic_step_tiled(const nsb_tick* tick, const nsb_tiled_layou
 NSB_API int nsb_dendritic_run_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
                                     int64_t ticks, const nsb_tick_out* out, void* workspace,
                                     size_t workspace_bytes, int* status, void* stream);
+
+/* Small graphs: `ticks` (>= 1) matrix ticks at B = 1 on ONE thread-block
+ * cluster of 8 CTAs (no counterpart in the reference).  Every CTA keeps the
+ * whole state vector and its rows' edges (weights decoded to float32) in
+ * shared memory; each tick a CTA updates its rows (each row summed
+ * sequentially in CSR order) and writes the new soma values into all 8 CTAs'
+ * shared memory (distributed shared memory), then the cluster meets at its
+ * hardware barrier.  Nothing goes through global memory between ticks.  The
+ * first tick reads the tick's state views, the last writes `out` (any
+ * strides).  A CTA stores its rows' edges interleaved by warp, padded to the
+ * widest row of each 32 rows: `max_slots` = nsb_cluster_slots(N, host copy of
+ * csr->rowptr).  The graph fits when nsb_cluster_smem_bytes(N, max_slots) is
+ * at most the device's opt-in shared memory per block (N = 4,096 / M = 65k:
+ * about 140 KB).  A `max_slots` below the real value is detected in the
+ * kernel, which then writes nothing and sets code 7 in `status` (device int,
+ * may be NULL). */
+NSB_API int64_t nsb_cluster_slots(int64_t neurons, const int32_t* host_rowptr);
+NSB_API size_t nsb_cluster_smem_bytes(int64_t neurons, int64_t max_slots);
+NSB_API int nsb_dendritic_run_cluster(const nsb_tick* tick, const nsb_csr* csr, int64_t max_slots,
+                                      int64_t ticks, const nsb_tick_out* out, int* status,
+                                      void* stream);
 
 /* Up to this many GPUs take part in a peer exchange. */
 #define NSB_MAX_PEERS 8

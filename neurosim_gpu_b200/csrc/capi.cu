@@ -332,6 +332,48 @@ int nsb_dendritic_run_tiled_peers(const nsb_tick* tick, const nsb_tiled_layout* 
   return NSB_OK;
 }
 
+int64_t nsb_cluster_slots(int64_t neurons, const int32_t* host_rowptr) {
+  if (neurons <= 0 || neurons >= (int64_t{1} << 31) || !host_rowptr) return -1;
+  return nsb::cluster_slots(neurons, host_rowptr);
+}
+
+size_t nsb_cluster_smem_bytes(int64_t neurons, int64_t max_slots) {
+  if (neurons <= 0 || neurons >= (int64_t{1} << 31) || max_slots < 0 ||
+      max_slots >= (int64_t{1} << 31))
+    return 0;
+  return nsb::cluster_smem_bytes(neurons, max_slots);
+}
+
+int nsb_dendritic_run_cluster(const nsb_tick* tick, const nsb_csr* csr, int64_t max_slots,
+                              int64_t ticks, const nsb_tick_out* out, int* status,
+                              void* stream) {
+  if (ticks < 1 || ticks > (int64_t{1} << 30))
+    return fail(NSB_ERR_ARGUMENT, "ticks must be in [1, 2^30]");
+  nsb::TickArgs t;
+  if (!check_tick(tick, &t)) return NSB_ERR_ARGUMENT;
+  if (t.batch != 1) return fail(NSB_ERR_ARGUMENT, "the cluster tick takes B = 1");
+  nsb::Csr c;
+  if (!check_csr(csr, &c)) return NSB_ERR_ARGUMENT;
+  if (!out || !check_out(out->state, "state") || !check_out(out->dendrite, "dendrite") ||
+      !check_out(out->adaptation, "adaptation"))
+    return NSB_ERR_ARGUMENT;
+  if (max_slots < 0 || max_slots >= (int64_t{1} << 31))
+    return fail(NSB_ERR_ARGUMENT, "max_slots must be in [0, 2^31)");
+  int device = 0, optin = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err == cudaSuccess)
+    err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  if (err != cudaSuccess) return cuda_fail(err, "device attribute query");
+  if (nsb::cluster_smem_bytes(t.neurons, max_slots) > static_cast<size_t>(optin))
+    return fail(NSB_ERR_ARGUMENT, "the graph does not fit the cluster tick's shared memory");
+  g_error.clear();
+  const nsb::TickOut o{to_out(out->state), to_out(out->dendrite), to_out(out->adaptation)};
+  err = nsb::launch_cluster(t, c, max_slots, static_cast<int>(ticks), o, status,
+                            static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_run_cluster launch");
+  return NSB_OK;
+}
+
 namespace {
 // cuMemGetAddressRange through the runtime's driver entry point (no -lcuda).
 using AddressRange = int (*)(unsigned long long*, size_t*, unsigned long long);

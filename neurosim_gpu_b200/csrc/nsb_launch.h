@@ -57,6 +57,13 @@ cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, cons
                          void* workspace, int* status, cudaStream_t stream,
                          const nsb_peer_exchange* exchange = nullptr);
 
+// Small-graph tick on one thread-block cluster (cluster.cu): `ticks` ticks of
+// B = 1 with the state and the edges in the cluster's shared memory.
+int64_t cluster_slots(int64_t neurons, const int32_t* host_rowptr);
+size_t cluster_smem_bytes(int64_t neurons, int64_t max_slots);
+cudaError_t launch_cluster(const TickArgs& t, const Csr& csr, int64_t max_slots, int ticks,
+                           const TickOut& out, int* status, cudaStream_t stream);
+
 cudaError_t launch_event(const TickArgs& t, const EventArgs& e, const TickOut& out,
                          const Out& out_emitted, void* workspace, cudaStream_t stream);
 

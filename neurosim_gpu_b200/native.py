@@ -113,6 +113,7 @@ EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_dendritic_run_tiled", "nsb_dendritic_run_tiled_peers",
                     "nsb_ipc_export", "nsb_ipc_import", "nsb_ipc_release", "nsb_tiled_propagate",
                     "nsb_dendritic_event_noalloc", "nsb_dendritic_step_rows",
+                    "nsb_cluster_slots", "nsb_cluster_smem_bytes", "nsb_dendritic_run_cluster",
                     "nsb_last_error", "nsb_abi_version")
 
 
@@ -158,11 +159,17 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_dendritic_event_noalloc.argtypes = [p(_Tick), ctypes.c_void_p, p(_View),
                                                 ctypes.c_void_p, ctypes.c_int64, p(_OutCsr),
                                                 p(_TickOut), p(_Out), ctypes.c_void_p]
+    lib.nsb_cluster_slots.argtypes = [ctypes.c_int64, ctypes.c_void_p]
+    lib.nsb_cluster_slots.restype = ctypes.c_int64
+    lib.nsb_cluster_smem_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
+    lib.nsb_cluster_smem_bytes.restype = ctypes.c_size_t
+    lib.nsb_dendritic_run_cluster.argtypes = [p(_Tick), p(_Csr), ctypes.c_int64, ctypes.c_int64,
+                                              p(_TickOut), ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_last_error.restype = ctypes.c_char_p
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
         getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
-    if lib.nsb_abi_version() != 4:
+    if lib.nsb_abi_version() != 5:
         raise RuntimeError("libneurosim_b200.so ABI version mismatch")
     return lib
 
@@ -398,6 +405,51 @@ class DendriticExtension:
                         ctypes.byref(tick), ctypes.byref(c_layout), int(ticks),
                         ctypes.byref(result), workspace.data_ptr(), workspace.numel(), status_ptr,
                         _stream(device))
+            _raise_on_status(lib, code)
+
+        return launch
+
+    def cluster_plan(self, rowptr: torch.Tensor) -> tuple[int, int]:
+        """``(max_slots, shared bytes per CTA)`` of the small-graph cluster tick."""
+        host = rowptr.detach().to("cpu", torch.int32).contiguous()
+        neurons = host.numel() - 1
+        _check(neurons > 0, "invalid CSR geometry")
+        slots = int(self.lib.nsb_cluster_slots(neurons, host.data_ptr()))
+        _check(slots >= 0, "invalid CSR geometry")
+        return slots, int(self.lib.nsb_cluster_smem_bytes(neurons, slots))
+
+    def prepare_run_cluster(self, state, dendrite, adaptation, params, rowptr, source, weight,
+                            input, input_scalar, dendritic_input, dendritic_scalar,
+                            block_scales=None, global_scale=None, *, out, ticks, max_slots,
+                            status=None):
+        """A launch callable for ``ticks`` B = 1 ticks on one thread-block cluster.
+
+        ``max_slots`` comes from :meth:`cluster_plan` of the same ``rowptr``.
+        The first tick reads ``state`` / ``dendrite`` / ``adaptation``, the last
+        writes ``out``; nothing else touches global memory in between.
+        """
+        _check_state(state)
+        _check(state.size(0) == 1, "the cluster tick takes B = 1")
+        _check(int(ticks) >= 1, "ticks must be positive")
+        tick = _tick(state, dendrite, adaptation, params, input, input_scalar,
+                     dendritic_input, dendritic_scalar)
+        csr = csr_arguments(rowptr, source, weight, block_scales, global_scale, state)
+        _check(len(out) == 3, "three output tensors are required")
+        for view in out:
+            _float_on(view, state)
+            _check(view.shape == state.shape, "output shape mismatch")
+        result = _TickOut(_out(out[0]), _out(out[1]), _out(out[2]))
+        status_ptr = status.data_ptr() if status is not None else None
+        lib, device, slots, count = self.lib, state.device, int(max_slots), int(ticks)
+        keep = (state, dendrite, adaptation, params, rowptr, source, weight, input,
+                dendritic_input, block_scales, global_scale, out, status)
+
+        def launch() -> None:
+            assert keep is not None
+            with torch.cuda.device(device):
+                code = lib.nsb_dendritic_run_cluster(ctypes.byref(tick), ctypes.byref(csr), slots,
+                                                     count, ctypes.byref(result), status_ptr,
+                                                     _stream(device))
             _raise_on_status(lib, code)
 
         return launch

@@ -169,13 +169,15 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
             raise ValueError("weight_format must be None, 'fp8' or 'nvfp4'")
         if weight_format is not None and weight_dtype != torch.float32:
             raise ValueError("weight_format and non-default weight_dtype conflict")
-        if kernel not in ("auto", "csr", "tiled"):
-            raise ValueError("kernel must be 'auto', 'csr' or 'tiled'")
+        if kernel not in ("auto", "csr", "tiled", "cluster"):
+            raise ValueError("kernel must be 'auto', 'csr', 'tiled' or 'cluster'")
         self.kernel = kernel
         self._init_compartments(topology, dynamics, initial_state, extension)
         self._status = _tiled.status_word(initial_state.device)
         self._layout = None
         self._layout_key = None
+        self._cluster = None
+        self._cluster_key = None
         degree = topology.n_edges / max(topology.n_neurons, 1)
         # Lanes per row; each lane reads 4-edge chunks, so 32 lanes cover 128 edges.
         self.threads_per_row = threads_per_row or (8 if degree <= 16 else 16 if degree <= 48
@@ -195,18 +197,49 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
 
     @property
     def kernel_path(self) -> str:
-        """'tiled' (B = 1, state gathered from shared memory) or 'csr' (any B)."""
+        """'cluster' (B = 1 small graph on one thread-block cluster), 'tiled'
+        (B = 1, state gathered from shared memory) or 'csr' (any B)."""
+        if self._cluster_slots() is not None:
+            return "cluster"
         return "tiled" if self._tiled_layout() is not None else "csr"
 
+    def _cluster_slots(self) -> int | None:
+        """Edge slots per CTA of the cluster tick, or None if it is not used.
+
+        ``kernel='auto'`` takes the cluster tick at B = 1 whenever the graph
+        fits one cluster's shared memory (it keeps all state on chip between
+        ticks, so it beats the grid-wide kernels on small graphs).
+        """
+        if self.kernel not in ("auto", "cluster") or self.state.shape[0] != 1:
+            if self.kernel == "cluster":
+                raise ValueError("the cluster tick takes B = 1")
+            return None
+        rowptr = self.topology.in_rowptr
+        key = (rowptr.data_ptr(), self.topology.n_edges, self.state.device)
+        if self._cluster_key != key:
+            slots, smem = self.extension.cluster_plan(rowptr)
+            fits = smem <= _tiled.smem_limit(self.state.device)
+            if not fits and self.kernel == "cluster":
+                raise ValueError(f"the graph needs {smem} bytes of shared memory per CTA; "
+                                 "it does not fit the cluster tick")
+            self._cluster = slots if fits else None
+            self._cluster_key = key
+        return self._cluster
+
     def check_status(self) -> None:
-        """Raise if a tiled launch reported an internal pipeline timeout (reads the device)."""
+        """Raise if a tiled or cluster launch reported an error (reads the device):
+        codes 1-6 are bounded-wait timeouts of the tiled kernel, 7 a cluster
+        launch whose edge-slot count was too small (it wrote nothing)."""
         code = int(self._status.item())
+        if code == 7:
+            raise RuntimeError("cluster tick: edge slots exceed max_slots (code 7)")
         if code:
             raise RuntimeError(f"tiled tick pipeline timeout (code {code})")
 
     def _tiled_layout(self):
         """The column-blocked layout of the current weights, or None if not used."""
-        if self.kernel == "csr" or self.state.shape[0] != 1 or self.topology.n_edges == 0:
+        if (self.kernel in ("csr", "cluster") or self.state.shape[0] != 1
+                or self.topology.n_edges == 0):
             return None
         key = (self.topology.weight_version, self.checkpoint_precision, self.state.device)
         if self._layout_key != key:
@@ -225,14 +258,25 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
             self._layout_key = key
         return self._layout
 
-    def _prepare(self, s, d, a, u, us, v, vs, out):
-        """A launch callable for one tick from (s, d, a) into the three `out` tensors."""
+    def _prepare(self, s, d, a, u, us, v, vs, out, ticks: int = 1):
+        """A launch callable for one tick from (s, d, a) into the three `out` tensors
+        (``ticks`` > 1: that many ticks in one launch; cluster and tiled paths only)."""
+        slots = self._cluster_slots()
+        if slots is not None:
+            weight, scales, scale, _ = self._weights()
+            topology = self.topology
+            return self.extension.prepare_run_cluster(
+                s, d, a, self._parameters(), topology.in_rowptr, topology.in_col, weight, u, us,
+                v, vs, scales, scale, out=out, ticks=ticks, max_slots=slots, status=self._status)
         layout = self._tiled_layout()
         if layout is not None:
             if s.stride(1) != 1 or s.data_ptr() % 16:
                 s = s.contiguous().clone()
             return self.extension.prepare_step_tiled(s, d, a, self._parameters(), layout, u, us,
-                                                     v, vs, out=out, status=self._status)
+                                                     v, vs, out=out, status=self._status,
+                                                     ticks=None if ticks == 1 else ticks)
+        if ticks != 1:
+            raise ValueError("the CSR path runs one tick per launch")
         weight, scales, scale, _ = self._weights()
         topology = self.topology
         return self.extension.prepare_step(s, d, a, self._parameters(), topology.in_rowptr,
@@ -317,16 +361,12 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         u, us = self._drive(drive)
         v, vs = self._drive(dendritic_drive, "dendritic_drive")
         weight, _, _, backend = self._weights()
-        layout = self._tiled_layout()  # build outside any capture
-        if layout is not None:
-            # One cooperative launch runs every tick (a persistent kernel).
-            s = self.state
-            if s.stride(1) != 1 or s.data_ptr() % 16:
-                s = s.contiguous().clone()
-            _, views = _native._outputs(3, s)
-            self.extension.prepare_step_tiled(s, self.dendritic_state, self.adaptation_state,
-                                              self._parameters(), layout, u, us, v, vs,
-                                              out=views, status=self._status, ticks=ticks)()
+        # Build the plan outside any capture.
+        if self._cluster_slots() is not None or self._tiled_layout() is not None:
+            # One launch runs every tick (a cluster or a persistent kernel).
+            _, views = _native._outputs(3, self.state)
+            self._prepare(self.state, self.dendritic_state, self.adaptation_state, u, us, v, vs,
+                          views, ticks=ticks)()
             self.state, self.dendritic_state, self.adaptation_state = views
             self.last_backend = backend
             return self.state

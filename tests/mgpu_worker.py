@@ -54,7 +54,8 @@ def parity(device, rank):
         rt.close()
         if rank == 0:
             topo = random_topology(n, m, device="cpu", seed=4, build_device=device)
-            single = NativeDendriticMatrixRuntime(topo, dyn, init.clone(), precision=precision)
+            single = NativeDendriticMatrixRuntime(topo, dyn, init.clone(), precision=precision,
+                                                  kernel="tiled")
             with torch.inference_mode():
                 for k in range(17):
                     single.step(0.2 if k < 10 else 0.25, dendritic_drive=0.1)
@@ -113,7 +114,7 @@ def checkpoint(device, rank):
     if rank == 0:
         print(f"CHECKPOINT sharded {same_sharded}", flush=True)
         single = NativeDendriticMatrixRuntime(topology.to(device), dyn,
-                                              torch.zeros(1, n, device=device))
+                                              torch.zeros(1, n, device=device), kernel="tiled")
         restore_runtime(single, payload)
         with torch.inference_mode():
             single.run(5, 0.2, dendritic_drive=0.1)

@@ -93,7 +93,8 @@ def test_sharded_ranks_emulated_on_one_gpu_match_single_gpu(precision, batch, wo
     initial = torch.rand(batch, n, generator=torch.Generator().manual_seed(2)).cuda()
     ranks = [ShardedDendriticMatrixRuntime(graph, model, initial, precision=precision,
                                            rank=r, world=world) for r in range(world)]
-    single = NativeDendriticMatrixRuntime(graph, model, initial.clone(), precision=precision)
+    single = NativeDendriticMatrixRuntime(graph, model, initial.clone(), precision=precision,
+                                          kernel="tiled")
     with torch.inference_mode():
         for _ in range(12):
             dsts = [rt.local_step(0.2, dendritic_drive=0.1) for rt in ranks]

@@ -80,7 +80,8 @@ def test_tiled_tick_matches_oracle(fmt, n, m, ctas, smem):
 @pytest.mark.parametrize("fmt", ["fp32", "nvfp4"])
 def test_runtime_uses_tiled_path_for_single_batch(fmt):
     graph, model, state = make(3000, 1, 90000)
-    tiled = NativeDendriticMatrixRuntime(graph, model, state.clone(), precision=fmt)
+    tiled = NativeDendriticMatrixRuntime(graph, model, state.clone(), precision=fmt,
+                                         kernel="tiled")
     csr = NativeDendriticMatrixRuntime(graph, model, state.clone(), precision=fmt, kernel="csr")
     decoded = quantize_dequantize(graph.in_weight, fmt)
     reference = OracleMatrix(graph, model, state, weight=decoded)
