@@ -381,7 +381,9 @@ __device__ void peer_barrier(const Peers& px, unsigned long long* local, int tic
   }
 }
 
-template <typename W, int D>
+// X: the row-sharded variant with the peer exchange (nsb_dendritic_run_tiled_peers);
+// the single-GPU instantiation carries none of its code.
+template <typename W, int D, bool X>
 __global__ void __launch_bounds__(kTiledThreads, 1)
 tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ x0, TickOut out,
                   Out product, bool update, int ticks, int* status, Peers px) {
@@ -452,7 +454,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
   };
 
   for (int tick = 0; tick < ticks; ++tick) {
-    const bool exchange = px.world > 0;
+    const bool exchange = X && px.world > 0;
     const float* x = exchange ? px.gathered[px.rank][tick & 1] : tick == 0 ? x0 : out.s.data;
     const int use0 = tick * stages;
     if (warp == kProducerWarp) {
@@ -710,13 +712,13 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
   }
 }
 
-template <typename W, int D>
-cudaError_t launch_tiled_variant(const TiledArgs& L, const W& w, const TickArgs& t,
-                                 const float* x, const TickOut& out, const Out& product,
-                                 bool update, int ticks, int* status, int ctas,
-                                 cudaStream_t stream, const Peers& px) {
+template <typename W, int D, bool X>
+cudaError_t launch_tiled_kernel(const TiledArgs& L, const W& w, const TickArgs& t,
+                                const float* x, const TickOut& out, const Out& product,
+                                bool update, int ticks, int* status, int ctas,
+                                cudaStream_t stream, const Peers& px) {
   const size_t smem = tiled_smem_bytes(L.block_cols, L.buffers);
-  auto kernel = tiled_tick_kernel<W, D>;
+  auto kernel = tiled_tick_kernel<W, D, X>;
   static int configured[64] = {0};
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
@@ -739,6 +741,18 @@ cudaError_t launch_tiled_variant(const TiledArgs& L, const W& w, const TickArgs&
   config.attrs = attribute;
   config.numAttrs = 1;
   return cudaLaunchKernelEx(&config, kernel, L, w, t, x, out, product, update, ticks, status, px);
+}
+
+template <typename W, int D>
+cudaError_t launch_tiled_variant(const TiledArgs& L, const W& w, const TickArgs& t,
+                                 const float* x, const TickOut& out, const Out& product,
+                                 bool update, int ticks, int* status, int ctas,
+                                 cudaStream_t stream, const Peers& px) {
+  if (px.world > 0)
+    return launch_tiled_kernel<W, D, true>(L, w, t, x, out, product, update, ticks, status, ctas,
+                                           stream, px);
+  return launch_tiled_kernel<W, D, false>(L, w, t, x, out, product, update, ticks, status, ctas,
+                                          stream, px);
 }
 
 }  // namespace
