@@ -389,6 +389,100 @@ def run_native(args, workload: str) -> dict:
     return result
 
 
+def run_sharded_pels(args) -> dict:
+    """Row-sharded PELS ticks on every rank of the torchrun job (strong scaling)."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from neurosim_gpu_b200.sharded import broadcast_graph
+    from neurosim_gpu_b200.sharded_pels import ShardedDendriticPELSRuntime
+
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    neurons, edges, batch, _ = WORKLOADS[args.workload]
+    graph = broadcast_graph(neurons, edges, seed=0, device=device)
+    m = int(graph[1].numel())
+    model = bench_model(neurons, device)
+    chunk = 64
+    offset = 0.0 if batch == 1 else ((torch.rand(batch, 1, generator=torch.Generator()
+                                                 .manual_seed(0)) * 0.4 - 0.2).to(device))
+    drive = [offset + 0.2 + 0.1 * math.sin(0.11 * t) for t in range(chunk)]
+    runtime = ShardedDendriticPELSRuntime(graph, model, torch.zeros(batch, neurons, device=device),
+                                          theta=PELS_THETA)
+    steps = max(args.steps - args.steps % chunk, chunk)
+
+    def timed(fn) -> float:
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1)], device=device)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    with torch.inference_mode():
+        runtime.run(max(args.warmup - args.warmup % chunk, chunk), drive, dendritic_drive=0.1,
+                    graph_ticks=chunk)
+        torch.cuda.synchronize()
+        sampler = ClockSampler(local_rank) if rank == 0 else None
+        if sampler:
+            sampler.__enter__()
+        total_ms = timed(lambda: runtime.run(steps, drive, dendritic_drive=0.1, graph_ticks=chunk))
+        if sampler:
+            sampler.__exit__(None, None, None)
+        tick_ms = total_ms / steps
+        rows = runtime.shard.rows
+        host_drive = torch.full((batch, rows), 0.2).pin_memory()
+        host_state = torch.empty((batch, rows)).pin_memory()
+        dev_drive = torch.zeros((batch, neurons), device=device)
+        lo, hi = runtime.shard.lo, runtime.shard.hi
+        e2e_steps = min(steps, 256)
+
+        def e2e():
+            for _ in range(e2e_steps):
+                dev_drive[:, lo:hi].copy_(host_drive, non_blocking=True)
+                host_state.copy_(runtime.step(dev_drive, dendritic_drive=0.1), non_blocking=True)
+
+        e2e()
+        e2e_ms = timed(e2e) / e2e_steps
+    runtime.check_status()
+    result = {
+        "metric": "synapse-updates/s (M*B/tick)", "value": m * batch / (tick_ms * 1e-3),
+        "unit": "synapse-updates/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": tick_ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (reference random_topology stream, seed 0; drive 0.2 + 0.1 sin(0.11 t) "
+                "over a 64-tick cycle, dendritic 0.1)",
+        "config": {"workload": args.workload, "neurons": neurons, "edges": m, "batch": batch,
+                   "theta": PELS_THETA,
+                   "parallelism": f"row-sharded x{world}, " + (
+                       "deltas exchanged by peer stores inside the advance kernel (NVLink)"
+                       if runtime.exchange == "peer" else "NCCL all-gather of deltas"),
+                   "kernel_path": "pels-rows", "ticks_per_graph": chunk},
+        "roofline": {"bound": "hbm", "achieved": None, "peak": hbm_peak()[0], "unit": "GB/s",
+                     "frac": None, "traffic": None, "per_gpu": True,
+                     "kernel": "event_rows_kernel + event_scatter_rows_kernel"},
+        "e2e": {"value": m * batch / (e2e_ms * 1e-3), "unit": "synapse-updates/s",
+                "h2d_bytes_per_step": 4 * batch * neurons,
+                "d2h_bytes_per_step": 4 * batch * neurons, "ms_per_step": e2e_ms},
+        "gpu_launches": 2 * steps * world,
+        "clocks": sampler.summary() if sampler else None,
+    }
+    runtime.release_graphs()
+    runtime.close()
+    torch.cuda.synchronize()
+    dist.barrier()
+    dist.destroy_process_group()
+    return result if rank == 0 else None
+
+
 def run_sharded(args, explicit_workload: bool) -> dict:
     """Row-sharded ticks on every rank of the torchrun job; rank 0 reports."""
     import datetime
@@ -551,7 +645,10 @@ def main() -> None:
                                            max(world, args.gpus))))
         return
     if world > 1 or args.gpus > 1:
-        result = run_sharded(args, explicit_workload)
+        if args.workload.startswith("pels_"):
+            result = run_sharded_pels(args)
+        else:
+            result = run_sharded(args, explicit_workload)
         if rank == 0:
             print(json.dumps(result))
         return

@@ -45,7 +45,7 @@ extern "C" {
 #define NSB_API
 #endif
 
-#define NSB_ABI_VERSION 5
+#define NSB_ABI_VERSION 6
 
 enum nsb_status {
   NSB_OK = 0,
@@ -360,6 +360,68 @@ NSB_API int nsb_tiled_propagate(int64_t neurons, const nsb_tiled_layout* layout,
 
 /* Thread-local message of the last failing call ("" if none). */
 NSB_API const char* nsb_last_error(void);
+
+/* ---------------------------------------------------------------------------
+ * Row-sharded PELS ticks (no counterpart in the reference, which runs on one
+ * GPU; each call does what dendritic_event does for one rank's rows).  Rank r
+ * owns destination rows [row_offset, row_offset + rows): their s, d, a,
+ * emitted state, theta and persistent current.  A tick is two calls:
+ *
+ * 1. nsb_dendritic_event_rows: the update of the rank's rows with j = current,
+ *    the emit rule, and each row's delta (the residual where it emits, else 0)
+ *    written to the gathered delta buffer [cols, B] at (row_offset + r) * B + b.
+ *    - exchange == NULL: into `delta`; the caller all-gathers the ranks'
+ *      slices of it (e.g. ncclAllGather) before step 2.
+ *    - exchange != NULL: into every rank's buffer of this tick's parity (peer
+ *      stores over NVLink); the kernel's last CTA then adds one to every rank's
+ *      arrival counter.  `delta` is not used.
+ * 2. nsb_event_scatter_rows: for every nonzero delta of the gathered buffer
+ *    (all N sources), current[b, dst - row_offset] += delta * w over the
+ *    source's out-edges with a destination in the rank's rows: `csr` is the
+ *    source-major out-CSR restricted to them (rowptr [N+1], dst rebased to
+ *    [0, rows)).  With an exchange it first waits, bounded, until all ranks
+ *    have signalled this tick (timeout: code 6 in `status`, and it goes on).
+ *
+ * `workspace` (NSB_EVENT_ROWS_WORKSPACE bytes, 8-byte aligned) is zero-filled
+ * once and passed to both calls of every tick of one rank; it counts the
+ * rank's ticks, so peer-mode calls can be captured into a CUDA graph and
+ * replayed.  All ranks' counters start at zero and every rank runs the same
+ * ticks.  The float atomics make the summation order of the current
+ * nondeterministic (as on one GPU).
+ * ------------------------------------------------------------------------- */
+#define NSB_EVENT_ROWS_WORKSPACE 256
+
+typedef struct nsb_event_rows {
+  int64_t row_offset;      /* global index of the rank's first row            */
+  int64_t cols;            /* neuron rows of the gathered delta buffers (>= N) */
+  const float* current;    /* [B, rows] contiguous: the rank's rows            */
+  nsb_view emitted;        /* [B, rows]                                        */
+  const float* theta;      /* the rank's rows of theta                         */
+  int64_t theta_stride;
+} nsb_event_rows;
+
+typedef struct nsb_delta_exchange {
+  int32_t world;                               /* ranks, 1..NSB_MAX_PEERS       */
+  int32_t rank;
+  float* delta[NSB_MAX_PEERS][2];              /* each rank's two [cols, B] buffers */
+  unsigned long long* counters[NSB_MAX_PEERS]; /* each rank's arrival counter    */
+} nsb_delta_exchange;
+
+typedef struct nsb_scatter_rows {
+  int64_t n_edges;         /* edges with a destination in the rank's rows     */
+  const int32_t* rowptr;   /* [N+1] per source                                */
+  const int32_t* dst;      /* [n_edges] destination - row_offset              */
+  const float* weight;     /* [n_edges]                                       */
+} nsb_scatter_rows;
+
+NSB_API int nsb_dendritic_event_rows(const nsb_tick* tick, const nsb_event_rows* ev,
+                                     float* delta, const nsb_delta_exchange* exchange,
+                                     const nsb_tick_out* out, const nsb_out* out_emitted,
+                                     void* workspace, void* stream);
+NSB_API int nsb_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows,
+                                   const float* delta, const nsb_scatter_rows* csr,
+                                   float* current, const nsb_delta_exchange* exchange,
+                                   void* workspace, int* status, void* stream);
 
 /* NSB_ABI_VERSION of the loaded library. */
 NSB_API int nsb_abi_version(void);

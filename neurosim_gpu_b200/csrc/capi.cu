@@ -487,6 +487,94 @@ int nsb_dendritic_event(const nsb_tick* tick, float* current, const nsb_view* em
   return NSB_OK;
 }
 
+namespace {
+bool check_delta_exchange(const nsb_delta_exchange* x, nsb::DeltaPeers* px) {
+  if (x->world < 1 || x->world > NSB_MAX_PEERS || x->rank < 0 || x->rank >= x->world)
+    return fail(NSB_ERR_ARGUMENT, "delta exchange: world must be 1..8 and rank in [0, world)"),
+           false;
+  px->world = x->world;
+  px->rank = x->rank;
+  for (int p = 0; p < x->world; ++p) {
+    if (!x->delta[p][0] || !x->delta[p][1] || !x->counters[p])
+      return fail(NSB_ERR_ARGUMENT, "delta exchange: every rank needs two buffers and a counter"),
+             false;
+    px->delta[p][0] = x->delta[p][0];
+    px->delta[p][1] = x->delta[p][1];
+    px->counters[p] = x->counters[p];
+  }
+  return true;
+}
+
+bool check_rows_workspace(void* workspace) {
+  if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 8 != 0)
+    return fail(NSB_ERR_WORKSPACE, "row-event workspace must be 8-byte aligned"), false;
+  return true;
+}
+}  // namespace
+
+int nsb_dendritic_event_rows(const nsb_tick* tick, const nsb_event_rows* ev, float* delta,
+                             const nsb_delta_exchange* exchange, const nsb_tick_out* out,
+                             const nsb_out* out_emitted, void* workspace, void* stream) {
+  nsb::TickArgs t;
+  if (!check_tick(tick, &t)) return NSB_ERR_ARGUMENT;
+  if (!ev) return fail(NSB_ERR_ARGUMENT, "row-event arguments are required");
+  if (ev->row_offset < 0 || ev->cols < ev->row_offset + t.neurons ||
+      ev->cols * t.batch >= (int64_t(1) << 40))
+    return fail(NSB_ERR_ARGUMENT, "rows must lie in [0, cols) of the delta buffer");
+  if (t.batch > 0 && (!ev->current || !ev->emitted.data))
+    return fail(NSB_ERR_ARGUMENT, "persistent current and emitted state are required");
+  if (!ev->theta) return fail(NSB_ERR_ARGUMENT, "theta must have a value per row");
+  if (!exchange && !delta) return fail(NSB_ERR_ARGUMENT, "a delta buffer or an exchange is required");
+  nsb::DeltaPeers px{};
+  if (exchange && !check_delta_exchange(exchange, &px)) return NSB_ERR_ARGUMENT;
+  if (!out || !out_emitted) return fail(NSB_ERR_ARGUMENT, "outputs are required");
+  if (t.batch > 0 && (!check_out(out->state, "state") || !check_out(out->dendrite, "dendrite") ||
+                      !check_out(out->adaptation, "adaptation") ||
+                      !check_out(*out_emitted, "emitted")))
+    return NSB_ERR_ARGUMENT;
+  if (!check_rows_workspace(workspace)) return NSB_ERR_WORKSPACE;
+  g_error.clear();
+  if (t.batch == 0) return NSB_OK;
+  nsb::EventRowsArgs e;
+  e.row_offset = ev->row_offset;
+  e.current = ev->current;
+  e.emitted = to_view(ev->emitted);
+  e.theta = ev->theta;
+  e.theta_stride = ev->theta_stride;
+  e.delta = delta;
+  const nsb::TickOut o{to_out(out->state), to_out(out->dendrite), to_out(out->adaptation)};
+  const cudaError_t err = nsb::launch_event_rows(
+      t, e, o, to_out(*out_emitted), exchange ? &px : nullptr,
+      static_cast<nsb::EventRowsState*>(workspace), static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_event_rows launch");
+  return NSB_OK;
+}
+
+int nsb_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows, const float* delta,
+                           const nsb_scatter_rows* csr, float* current,
+                           const nsb_delta_exchange* exchange, void* workspace, int* status,
+                           void* stream) {
+  if (batch < 0 || neurons <= 0 || rows < 0 || rows > neurons || batch * neurons >= (int64_t(1) << 40))
+    return fail(NSB_ERR_ARGUMENT, "scatter geometry: B >= 0, N > 0, 0 <= rows <= N");
+  if (!csr || !csr->rowptr || csr->n_edges < 0 || csr->n_edges >= (int64_t(1) << 31) ||
+      (csr->n_edges > 0 && (!csr->dst || !csr->weight)))
+    return fail(NSB_ERR_ARGUMENT, "invalid row-scatter topology geometry");
+  if (batch > 0 && rows > 0 && !current) return fail(NSB_ERR_ARGUMENT, "current is required");
+  if (!exchange && !delta) return fail(NSB_ERR_ARGUMENT, "a delta buffer or an exchange is required");
+  nsb::DeltaPeers px{};
+  if (exchange && !check_delta_exchange(exchange, &px)) return NSB_ERR_ARGUMENT;
+  if (!check_rows_workspace(workspace)) return NSB_ERR_WORKSPACE;
+  g_error.clear();
+  if (batch == 0) return NSB_OK;
+  const nsb::ScatterRowsArgs c{csr->rowptr, csr->dst, csr->weight};
+  const cudaError_t err = nsb::launch_event_scatter_rows(
+      batch, neurons, rows, delta, c, current, exchange ? &px : nullptr,
+      static_cast<const nsb::EventRowsState*>(workspace), status,
+      static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_event_scatter_rows launch");
+  return NSB_OK;
+}
+
 int nsb_dendritic_event_noalloc(const nsb_tick* tick, float* current, const nsb_view* emitted,
                                 const float* theta, int64_t theta_stride,
                                 const nsb_out_csr* out_csr, const nsb_tick_out* out,

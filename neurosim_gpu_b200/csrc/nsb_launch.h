@@ -64,6 +64,46 @@ size_t cluster_smem_bytes(int64_t neurons, int64_t max_slots);
 cudaError_t launch_cluster(const TickArgs& t, const Csr& csr, int64_t max_slots, int ticks,
                            const TickOut& out, int* status, cudaStream_t stream);
 
+// Row-sharded PELS (pels_rows.cu).  One rank's rows of the event tick.
+struct EventRowsArgs {
+  int64_t row_offset;    // global index of the rank's first row
+  const float* current;  // [B, rows] contiguous
+  View emitted;          // [B, rows]
+  const float* theta;    // the rank's rows
+  int64_t theta_stride;
+  float* delta;          // local mode: the gathered delta buffer [cols, B]
+};
+
+// Every rank's two gathered delta buffers and arrival counters (peer mode).
+struct DeltaPeers {
+  int32_t world, rank;
+  float* delta[NSB_MAX_PEERS][2];
+  unsigned long long* counters[NSB_MAX_PEERS];
+};
+
+// Head of the caller's row-event workspace (zero-filled once).
+struct EventRowsState {
+  unsigned long long ticks;  // peer-mode ticks this rank has signalled
+  unsigned int done;         // CTAs of the current advance launch that finished
+  unsigned int reserved;
+};
+
+// The source-major out-CSR restricted to the rank's destination rows.
+struct ScatterRowsArgs {
+  const int32_t* rowptr;  // [N+1]
+  const int32_t* dst;     // [M_local], rebased to the rank's rows
+  const float* weight;    // [M_local]
+};
+
+cudaError_t launch_event_rows(const TickArgs& t, const EventRowsArgs& e, const TickOut& out,
+                              const Out& out_emitted, const DeltaPeers* px,
+                              EventRowsState* state, cudaStream_t stream);
+cudaError_t launch_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows,
+                                      const float* delta, const ScatterRowsArgs& c,
+                                      float* current, const DeltaPeers* px,
+                                      const EventRowsState* state, int* status,
+                                      cudaStream_t stream);
+
 cudaError_t launch_event(const TickArgs& t, const EventArgs& e, const TickOut& out,
                          const Out& out_emitted, void* workspace, cudaStream_t stream);
 

@@ -1,0 +1,200 @@
+// pels_rows.cu -- the PELS tick of one rank's rows (row-sharded event ticks).
+//
+// A rank owns destination rows [row_offset, row_offset + rows) and, for them,
+// the soma / dendrite / adaptation / emitted state, theta and the persistent
+// current.  One tick is two launches:
+//
+// 1. event_rows_kernel: thread per (b, r).  The pointwise update with
+//    j = current[b, r], the emit rule (|s' - emitted| >= theta; the rule of
+//    csrc/compartmental.cu:142-158) and the row's delta (the residual if it
+//    emits, else 0), written into the gathered delta buffer at
+//    [(row_offset + r) * B + b].  Every row is written every tick, so the
+//    gathered buffer needs no clearing.
+//    * Local mode: the caller all-gathers the buffers (NCCL) before step 2.
+//    * Peer mode (the exchange fused into the kernels): each delta is stored
+//      into every rank's buffer of this tick's parity over NVLink; each thread
+//      fences at system scope, each CTA counts itself done, and the last CTA
+//      adds one to every rank's arrival counter and advances this rank's tick
+//      count (device memory, so CUDA-graph replays need no host epoch).
+// 2. event_scatter_rows_kernel: in peer mode every CTA first waits (bounded)
+//    until its rank's counter shows all ranks' arrivals for this tick.  Then
+//    each warp takes 32 consecutive (source, batch) entries of the gathered
+//    delta, ballots the nonzero ones and scatters each one's out-edges with a
+//    destination in this rank's range (a source-major CSR filtered to the
+//    rank's rows, destinations rebased) into current[b, dst] with float
+//    atomics, 32 edges per step.
+//
+// The double-buffered delta buffers are safe to reuse: a rank writes parity p
+// again two ticks later, only after every rank has passed its wait of the tick
+// in between, which follows that rank's scatter of parity p.
+#include <algorithm>
+
+#include "nsb_launch.h"
+
+namespace nsb {
+namespace {
+
+constexpr int kRowThreads = 256;
+constexpr long long kDeltaWaitLimit = 1ll << 24;
+
+__device__ __forceinline__ unsigned long long load_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <bool X>
+__global__ void __launch_bounds__(kRowThreads)
+event_rows_kernel(TickArgs t, EventRowsArgs e, TickOut out, Out out_emitted, DeltaPeers px,
+                  EventRowsState* state) {
+  const int64_t rows = t.neurons;
+  const int64_t batch = t.batch;
+  const int64_t count = batch * rows;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int parity = 0;
+  if (X) parity = static_cast<int>(*reinterpret_cast<volatile unsigned long long*>(&state->ticks) & 1);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += stride) {
+    const int64_t b = i / rows;
+    const int64_t r = i - b * rows;
+    const Update q = advance_at(t, __ldg(e.current + b * rows + r), b, r);
+    out.s.put(b, r, q.s);
+    out.d.put(b, r, q.d);
+    out.a.put(b, r, q.a);
+    const float previous = e.emitted.at(b, r);
+    const float residual = __fsub_rn(q.s, previous);
+    const bool active = fabsf(residual) >= __ldg(e.theta + r * e.theta_stride);
+    out_emitted.put(b, r, active ? q.s : previous);
+    const float delta = active ? residual : 0.0f;
+    const int64_t at = (e.row_offset + r) * batch + b;
+    if (X) {
+      for (int p = 0; p < px.world; ++p) px.delta[p][parity][at] = delta;
+    } else {
+      e.delta[at] = delta;
+    }
+  }
+  if (X) {
+    __threadfence_system();  // this thread's peer stores, before the CTA counts itself done
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(&state->done, 1u) == gridDim.x - 1) {
+      // The last CTA of this tick: every CTA has counted itself, so the count
+      // can start over for the next tick.
+      state->done = 0;
+      __threadfence_system();
+      for (int p = 0; p < px.world; ++p) atomicAdd_system(px.counters[p], 1ull);
+      atomicAdd(&state->ticks, 1ull);
+    }
+  }
+}
+
+template <bool X>
+__global__ void __launch_bounds__(kRowThreads)
+event_scatter_rows_kernel(int64_t batch, int64_t neurons, int64_t rows, const float* delta,
+                          ScatterRowsArgs c, float* current, DeltaPeers px,
+                          const EventRowsState* state, int* status) {
+  if (X) {
+    // Tick k was counted by the advance launch just before this one, so this
+    // rank's tick count is k + 1: wait for world * (k + 1) arrivals.
+    const unsigned long long ticks = *reinterpret_cast<const volatile unsigned long long*>(&state->ticks);
+    delta = px.delta[px.rank][(ticks - 1) & 1];
+    if (threadIdx.x == 0) {
+      const unsigned long long target = static_cast<unsigned long long>(px.world) * ticks;
+      long long polls = 0;
+      while (load_acquire_sys(px.counters[px.rank]) < target) {
+        if (++polls > (1 << 12)) {
+          if (polls > kDeltaWaitLimit) {
+            if (status) atomicExch(status, 6);
+            break;
+          }
+          __nanosleep(128);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  const int lane = threadIdx.x & 31;
+  const int64_t entries = batch * neurons;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t base = warp * 32; base < entries; base += n_warps * 32) {
+    const int64_t mine = base + lane;
+    // Peer stores land in L2; read the deltas there (not through L1).
+    const float d = mine < entries ? __ldcg(delta + mine) : 0.0f;
+    unsigned int active = __ballot_sync(0xffffffffu, d != 0.0f);
+    while (active) {
+      const int k = __ffs(active) - 1;
+      active &= active - 1;
+      const int64_t entry = base + k;
+      const float value = __shfl_sync(0xffffffffu, d, k);
+      const int64_t n = entry / batch;
+      const int64_t b = entry - n * batch;
+      float* row = current + b * rows;
+      const int64_t e0 = __ldg(c.rowptr + n);
+      const int64_t e1 = __ldg(c.rowptr + n + 1);
+      for (int64_t edge = e0 + lane; edge < e1; edge += 32)
+        atomicAdd(row + __ldg(c.dst + edge), __fmul_rn(value, __ldg(c.weight + edge)));
+    }
+  }
+}
+
+template <typename K>
+int resident(K kernel) {
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kRowThreads, 0) != cudaSuccess)
+    blocks = 1;
+  return std::max(blocks, 1);
+}
+
+}  // namespace
+
+cudaError_t launch_event_rows(const TickArgs& t, const EventRowsArgs& e, const TickOut& out,
+                              const Out& out_emitted, const DeltaPeers* px,
+                              EventRowsState* state, cudaStream_t stream) {
+  DeviceInfo info;
+  cudaError_t err = device_info(&info);
+  if (err != cudaSuccess) return err;
+  const int64_t count = t.batch * t.neurons;
+  const int64_t needed = std::max<int64_t>(1, (count + kRowThreads - 1) / kRowThreads);
+  if (px) {
+    static int occupancy = 0;
+    if (occupancy == 0) occupancy = resident(event_rows_kernel<true>);
+    const int64_t blocks = std::min<int64_t>(needed, int64_t{info.sm_count} * occupancy);
+    event_rows_kernel<true><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(
+        t, e, out, out_emitted, *px, state);
+  } else {
+    static int occupancy = 0;
+    if (occupancy == 0) occupancy = resident(event_rows_kernel<false>);
+    const int64_t blocks = std::min<int64_t>(needed, int64_t{info.sm_count} * occupancy);
+    event_rows_kernel<false><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(
+        t, e, out, out_emitted, DeltaPeers{}, state);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows,
+                                      const float* delta, const ScatterRowsArgs& c,
+                                      float* current, const DeltaPeers* px,
+                                      const EventRowsState* state, int* status,
+                                      cudaStream_t stream) {
+  DeviceInfo info;
+  cudaError_t err = device_info(&info);
+  if (err != cudaSuccess) return err;
+  const int64_t warps = (batch * neurons + 31) / 32;
+  const int64_t needed = std::max<int64_t>(1, (warps * 32 + kRowThreads - 1) / kRowThreads);
+  if (px) {
+    static int occupancy = 0;
+    if (occupancy == 0) occupancy = resident(event_scatter_rows_kernel<true>);
+    const int64_t blocks = std::min<int64_t>(needed, int64_t{info.sm_count} * occupancy);
+    event_scatter_rows_kernel<true><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(
+        batch, neurons, rows, delta, c, current, *px, state, status);
+  } else {
+    static int occupancy = 0;
+    if (occupancy == 0) occupancy = resident(event_scatter_rows_kernel<false>);
+    const int64_t blocks = std::min<int64_t>(needed, int64_t{info.sm_count} * occupancy);
+    event_scatter_rows_kernel<false><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(
+        batch, neurons, rows, delta, c, current, DeltaPeers{}, state, status);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace nsb

@@ -99,6 +99,26 @@ class _PeerExchange(ctypes.Structure):
                 ("epoch", ctypes.c_uint64)]
 
 
+class _EventRows(ctypes.Structure):
+    _fields_ = [("row_offset", ctypes.c_int64), ("cols", ctypes.c_int64),
+                ("current", ctypes.c_void_p), ("emitted", _View), ("theta", ctypes.c_void_p),
+                ("theta_stride", ctypes.c_int64)]
+
+
+class _DeltaExchange(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("delta", (ctypes.c_void_p * 2) * MAX_PEERS),
+                ("counters", ctypes.c_void_p * MAX_PEERS)]
+
+
+class _ScatterRows(ctypes.Structure):
+    _fields_ = [("n_edges", ctypes.c_int64), ("rowptr", ctypes.c_void_p),
+                ("dst", ctypes.c_void_p), ("weight", ctypes.c_void_p)]
+
+
+EVENT_ROWS_WORKSPACE = 256
+
+
 class EventCounters(ctypes.Structure):
     """Head of the nsb_dendritic_event workspace (nsb_event_counters)."""
 
@@ -114,6 +134,7 @@ EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_ipc_export", "nsb_ipc_import", "nsb_ipc_release", "nsb_tiled_propagate",
                     "nsb_dendritic_event_noalloc", "nsb_dendritic_step_rows",
                     "nsb_cluster_slots", "nsb_cluster_smem_bytes", "nsb_dendritic_run_cluster",
+                    "nsb_dendritic_event_rows", "nsb_event_scatter_rows",
                     "nsb_last_error", "nsb_abi_version")
 
 
@@ -165,11 +186,18 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_cluster_smem_bytes.restype = ctypes.c_size_t
     lib.nsb_dendritic_run_cluster.argtypes = [p(_Tick), p(_Csr), ctypes.c_int64, ctypes.c_int64,
                                               p(_TickOut), ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_dendritic_event_rows.argtypes = [p(_Tick), p(_EventRows), ctypes.c_void_p,
+                                             p(_DeltaExchange), p(_TickOut), p(_Out),
+                                             ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_event_scatter_rows.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_void_p, p(_ScatterRows), ctypes.c_void_p,
+                                           p(_DeltaExchange), ctypes.c_void_p, ctypes.c_void_p,
+                                           ctypes.c_void_p]
     lib.nsb_last_error.restype = ctypes.c_char_p
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
         getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
-    if lib.nsb_abi_version() != 5:
+    if lib.nsb_abi_version() != 6:
         raise RuntimeError("libneurosim_b200.so ABI version mismatch")
     return lib
 
@@ -450,6 +478,88 @@ class DendriticExtension:
                 code = lib.nsb_dendritic_run_cluster(ctypes.byref(tick), ctypes.byref(csr), slots,
                                                      count, ctypes.byref(result), status_ptr,
                                                      _stream(device))
+            _raise_on_status(lib, code)
+
+        return launch
+
+    # -- row-sharded PELS --------------------------------------------------------
+    def prepare_event_rows(self, state, dendrite, adaptation, params, current, emitted, theta,
+                           input, input_scalar, dendritic_input, dendritic_scalar, *,
+                           row_offset, cols, delta, exchange, out, workspace):
+        """A launch callable for the advance + emit half of a row-sharded PELS tick.
+
+        ``state`` ... ``theta`` are this rank's rows ([B, rows] / [rows]);
+        ``delta`` is the gathered [cols, B] delta buffer (None with an
+        ``exchange``, a :class:`_DeltaExchange`); ``out`` is (s, d, a, emitted).
+        """
+        _check_state(state)
+        tick = _tick(state, dendrite, adaptation, params, input, input_scalar,
+                     dendritic_input, dendritic_scalar)
+        _view(current, state)
+        _check(current.is_contiguous(), "persistent current must be contiguous")
+        emitted_view = _view(emitted, state)
+        _float_on(theta, state)
+        _check(theta.dim() == 1 and theta.numel() == state.size(1), "theta must have a value per row")
+        _check((delta is None) != (exchange is None), "give a delta buffer or an exchange")
+        if delta is not None:
+            _float_on(delta, state)
+            _check(delta.is_contiguous() and delta.numel() == cols * state.size(0),
+                   "delta must be a contiguous [cols, B] buffer")
+        _check(len(out) == 4, "four output tensors are required")
+        for view in out:
+            _float_on(view, state)
+            _check(view.shape == state.shape, "output shape mismatch")
+        _check(workspace.device == state.device and workspace.numel() >= EVENT_ROWS_WORKSPACE,
+               "row-event workspace too small")
+        ev = _EventRows(int(row_offset), int(cols), current.data_ptr(), emitted_view,
+                        theta.data_ptr(), theta.stride(0))
+        result = _TickOut(_out(out[0]), _out(out[1]), _out(out[2]))
+        out_emitted = _out(out[3])
+        delta_ptr = delta.data_ptr() if delta is not None else None
+        x = ctypes.byref(exchange) if exchange is not None else None
+        lib, device = self.lib, state.device
+        keep = (state, dendrite, adaptation, params, current, emitted, theta, input,
+                dendritic_input, delta, exchange, out, workspace)
+
+        def launch() -> None:
+            assert keep is not None
+            with torch.cuda.device(device):
+                code = lib.nsb_dendritic_event_rows(ctypes.byref(tick), ctypes.byref(ev),
+                                                    delta_ptr, x, ctypes.byref(result),
+                                                    ctypes.byref(out_emitted),
+                                                    workspace.data_ptr(), _stream(device))
+            _raise_on_status(lib, code)
+
+        return launch
+
+    def prepare_scatter_rows(self, batch, neurons, rows, delta, rowptr, dst, weight, current, *,
+                             exchange, workspace, status=None):
+        """A launch callable for the scatter half of a row-sharded PELS tick."""
+        _check(current.is_cuda and current.dtype == torch.float32 and current.is_contiguous()
+               and tuple(current.shape) == (batch, rows), "current must be a contiguous [B, rows]")
+        for array in (rowptr, dst):
+            _check(array.device == current.device and array.dtype == torch.int32
+                   and array.is_contiguous(), "index arrays must be contiguous int32")
+        _check(weight.device == current.device and weight.dtype == torch.float32
+               and weight.is_contiguous() and weight.numel() == dst.numel()
+               and rowptr.numel() == neurons + 1, "invalid row-scatter topology geometry")
+        _check((delta is None) != (exchange is None), "give a delta buffer or an exchange")
+        edges = dst.numel()
+        csr = _ScatterRows(edges, rowptr.data_ptr(), dst.data_ptr() if edges else None,
+                           weight.data_ptr() if edges else None)
+        delta_ptr = delta.data_ptr() if delta is not None else None
+        x = ctypes.byref(exchange) if exchange is not None else None
+        status_ptr = status.data_ptr() if status is not None else None
+        lib, device = self.lib, current.device
+        keep = (delta, rowptr, dst, weight, current, exchange, workspace, status)
+
+        def launch() -> None:
+            assert keep is not None
+            with torch.cuda.device(device):
+                code = lib.nsb_event_scatter_rows(int(batch), int(neurons), int(rows), delta_ptr,
+                                                  ctypes.byref(csr), current.data_ptr(), x,
+                                                  workspace.data_ptr(), status_ptr,
+                                                  _stream(device))
             _raise_on_status(lib, code)
 
         return launch

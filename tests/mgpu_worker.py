@@ -8,6 +8,12 @@ Modes (argv[1]):
   checkpoint  a sharded run is captured into one payload and restored into a
            fresh sharded run and into a single-GPU runtime; both continue bit
            for bit like the original: prints "CHECKPOINT <case> <bool>".
+  pels     row-sharded PELS with the peer and the NCCL delta exchange: 4 ticks
+           against the single-GPU PELS runtime, then a CUDA-graph run; theta = 0
+           against the matrix tick and the current against W @ emitted: prints
+           "PELS <exchange>-<theta> <bool> ...".
+  pels_timeout  rank 1 stays alive but does not launch; rank 0's scatter must
+           end its bounded cross-GPU wait with status code 6: prints "STATUS <code>".
 """
 
 from __future__ import annotations
@@ -122,13 +128,80 @@ def checkpoint(device, rank):
     dist.barrier()
 
 
+def pels(device, rank):
+    from neurosim_gpu_b200 import NativeDendriticPELSRuntime
+    from neurosim_gpu_b200.native import load_native_extension
+    from neurosim_gpu_b200.sharded_pels import ShardedDendriticPELSRuntime
+    n, m, batch = 20011, 500000, 2
+    graph = broadcast_graph(n, m, seed=4, device=device)
+    dyn = model(n, device)
+    init = torch.rand(batch, n, generator=torch.Generator().manual_seed(3)).to(device)
+    ext = load_native_extension()
+    names = ("state", "dendritic_state", "adaptation_state", "emitted_state",
+             "persistent_current")
+    for exchange in ("peer", "nccl"):
+        for theta in (0.02, 0.0):
+            rt = ShardedDendriticPELSRuntime(graph, dyn, init, theta=theta, exchange=exchange)
+            with torch.inference_mode():
+                for _ in range(4):
+                    rt.step(0.2, dendritic_drive=0.1)
+                early = {name: rt.gather(name) for name in names}
+                rt.run(16, 0.2, dendritic_drive=0.1, graph_ticks=8)
+                rt.step(0.2, dendritic_drive=0.1)
+                late = {name: rt.gather(name) for name in names}
+            torch.cuda.synchronize()
+            status = int(rt.status.item())
+            path = rt.exchange
+            rt.release_graphs()
+            rt.close()
+            if rank == 0:
+                topo = random_topology(n, m, device="cpu", seed=4, build_device=device)
+                single = NativeDendriticPELSRuntime(topo, dyn, init.clone(), theta=theta)
+                with torch.inference_mode():
+                    for _ in range(4):
+                        single.step(0.2, dendritic_drive=0.1)
+                diff = max(float((early[k] - getattr(single, k)).abs().max()) for k in names)
+                product = ext.csr_propagate(topo.in_rowptr, topo.in_col, topo.in_weight,
+                                            late["emitted_state"].contiguous())
+                drift = float((late["persistent_current"] - product).abs().max())
+                ok = path == exchange and status == 0 and diff <= 2e-6 and drift <= 2e-5
+                extra = ""
+                if theta == 0.0:
+                    matrix = NativeDendriticMatrixRuntime(topo, dyn, init.clone(), kernel="csr")
+                    with torch.inference_mode():
+                        for _ in range(21):
+                            matrix.step(0.2, dendritic_drive=0.1)
+                    gap = float((late["state"] - matrix.state).abs().max())
+                    ok = ok and gap <= 8e-6
+                    extra = f" matrix_gap={gap:.3g}"
+                print(f"PELS {exchange}-{theta} {ok} diff={diff:.3g} drift={drift:.3g} "
+                      f"status={status}{extra}", flush=True)
+            dist.barrier()
+
+
+def pels_timeout(device, rank):
+    from neurosim_gpu_b200.sharded_pels import ShardedDendriticPELSRuntime
+    n, m = 20011, 500000
+    graph = broadcast_graph(n, m, seed=4, device=device)
+    rt = ShardedDendriticPELSRuntime(graph, model(n, device), torch.zeros(1, n, device=device),
+                                     theta=0.0, exchange="peer")
+    if rank == 0:
+        with torch.inference_mode():
+            rt.step(0.2, dendritic_drive=0.1)  # rank 1 never signals: bounded wait, code 6
+        torch.cuda.synchronize()
+        print(f"STATUS {int(rt.status.item())}", flush=True)
+    dist.barrier()  # rank 1 waits here, alive, with nothing in flight
+    rt.close()
+
+
 def main():
     local = int(os.environ["LOCAL_RANK"])
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     try:
-        {"parity": parity, "timeout": timeout, "checkpoint": checkpoint}[sys.argv[1]](
+        {"parity": parity, "timeout": timeout, "checkpoint": checkpoint, "pels": pels,
+         "pels_timeout": pels_timeout}[sys.argv[1]](
             device, dist.get_rank())
     finally:
         dist.destroy_process_group()

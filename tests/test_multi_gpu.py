@@ -67,3 +67,21 @@ def test_sharded_checkpoint_restores_sharded_and_single_gpu():
     assert [case for _, case, _ in lines] == ["sharded", "single"], out
     for _, case, ok in lines:
         assert ok == "True", case
+
+
+@pytest.mark.gpu
+@needs_two
+def test_sharded_pels_peer_and_nccl_exchanges_match_one_gpu():
+    out = _run("pels")
+    lines = [line.split() for line in out.splitlines() if line.startswith("PELS")]
+    assert len(lines) == 4, out
+    for _, case, ok, *diffs in lines:
+        assert ok == "True", (case, diffs)
+
+
+@pytest.mark.gpu
+@needs_two
+def test_missing_rank_ends_the_pels_delta_wait_with_a_status():
+    out = _run("pels_timeout")
+    codes = [int(line.split()[1]) for line in out.splitlines() if line.startswith("STATUS")]
+    assert codes == [6], out
