@@ -412,7 +412,7 @@ def run_sharded_pels(args) -> dict:
                                                  .manual_seed(0)) * 0.4 - 0.2).to(device))
     drive = [offset + 0.2 + 0.1 * math.sin(0.11 * t) for t in range(chunk)]
     runtime = ShardedDendriticPELSRuntime(graph, model, torch.zeros(batch, neurons, device=device),
-                                          theta=PELS_THETA)
+                                          theta=PELS_THETA, exchange=args.exchange)
     steps = max(args.steps - args.steps % chunk, chunk)
 
     def timed(fn) -> float:
@@ -508,7 +508,7 @@ def run_sharded(args, explicit_workload: bool) -> dict:
     m = int(graph[1].numel())
     model = bench_model(neurons, device)
     runtime = ShardedDendriticMatrixRuntime(graph, model, torch.zeros(batch, neurons, device=device),
-                                            precision=precision)
+                                            precision=precision, exchange=args.exchange)
     chunk = 32
     steps = max(args.steps - args.steps % chunk, chunk)
 
@@ -626,6 +626,8 @@ def main() -> None:
     parser.add_argument("--skip-cpu-baseline", action="store_true")
     parser.add_argument("--kernel", choices=("auto", "csr", "tiled", "cluster"), default="auto",
                         help="matrix tick path (auto: cluster for small graphs, tiled at B = 1)")
+    parser.add_argument("--exchange", choices=("auto", "nccl", "peer"), default="auto",
+                        help="row-sharded runs: soma / delta exchange (auto: peer stores)")
     parser.add_argument("--profile", action="store_true",
                         help="eager launches only, for ncu captures (prints no bench line)")
     parser.add_argument("--launch-ticks", type=int, default=1,
