@@ -45,7 +45,7 @@ extern "C" {
 #define NSB_API
 #endif
 
-#define NSB_ABI_VERSION 6
+#define NSB_ABI_VERSION 7
 
 enum nsb_status {
   NSB_OK = 0,
@@ -422,6 +422,21 @@ NSB_API int nsb_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows,
                                    const float* delta, const nsb_scatter_rows* csr,
                                    float* current, const nsb_delta_exchange* exchange,
                                    void* workspace, int* status, void* stream);
+
+/* Weight encoder (replaces encode_sparse_weights, src/neurosim_gpu/precision.py:76-90,
+ * for weights in device memory; bit-exact to it).  `format` is NSB_WEIGHT_E4M3
+ * (codes: n bytes) or NSB_WEIGHT_NVFP4 (codes: (n+1)/2 bytes, the even-indexed
+ * weight in the low nibble; block_scales: (n+15)/16 E4M3 bytes); `global_scale`
+ * receives the one float32 scale.  fp8: scale = max(amax/448, FLT_MIN),
+ * code = e4m3(clamp(w/scale, +-448)).  NVFP4: g = max(amax/2688, FLT_MIN), per
+ * 16 weights bs = e4m3(min(block_amax/(6g), 448)), code = E2M1 of |w|/(g*bs)
+ * (ties to the even code) with the sign of w in bit 3.  Weights must be finite.
+ * `workspace`: NSB_ENCODE_WORKSPACE bytes of device memory, 4-byte aligned
+ * (contents need not be initialised).  Two launches on `stream`. */
+#define NSB_ENCODE_WORKSPACE 256
+NSB_API int nsb_encode_weights(int32_t format, const float* weight, int64_t n, uint8_t* codes,
+                               uint8_t* block_scales, float* global_scale, void* workspace,
+                               void* stream);
 
 /* NSB_ABI_VERSION of the loaded library. */
 NSB_API int nsb_abi_version(void);

@@ -21,7 +21,7 @@ ROOT = PACKAGE.parent
 CSRC = PACKAGE / "csrc"
 INCLUDE = ROOT / "include"
 LIBRARY = PACKAGE / "libneurosim_b200.so"
-SOURCES = ("tick.cu", "tiled.cu", "pels.cu", "pels_rows.cu", "cluster.cu", "capi.cu")
+SOURCES = ("tick.cu", "tiled.cu", "pels.cu", "pels_rows.cu", "cluster.cu", "encode.cu", "capi.cu")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -575,6 +575,27 @@ int nsb_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows, const f
   return NSB_OK;
 }
 
+int nsb_encode_weights(int32_t format, const float* weight, int64_t n, uint8_t* codes,
+                       uint8_t* block_scales, float* global_scale, void* workspace,
+                       void* stream) {
+  if (format != NSB_WEIGHT_E4M3 && format != NSB_WEIGHT_NVFP4)
+    return fail(NSB_ERR_ARGUMENT, "the encoder takes NSB_WEIGHT_E4M3 or NSB_WEIGHT_NVFP4");
+  if (n < 0 || n >= (int64_t(1) << 31))
+    return fail(NSB_ERR_ARGUMENT, "weight count must be in [0, 2^31)");
+  if (n > 0 && (!weight || !codes))
+    return fail(NSB_ERR_ARGUMENT, "weights and a code buffer are required");
+  if (n > 0 && format == NSB_WEIGHT_NVFP4 && !block_scales)
+    return fail(NSB_ERR_ARGUMENT, "NVFP4 encoding needs a block-scale buffer");
+  if (!global_scale) return fail(NSB_ERR_ARGUMENT, "a global-scale output is required");
+  if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 4 != 0)
+    return fail(NSB_ERR_WORKSPACE, "encoder workspace must be 4-byte aligned");
+  g_error.clear();
+  const cudaError_t err = nsb::launch_encode(format, weight, n, codes, block_scales, global_scale,
+                                             workspace, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_encode_weights launch");
+  return NSB_OK;
+}
+
 int nsb_dendritic_event_noalloc(const nsb_tick* tick, float* current, const nsb_view* emitted,
                                 const float* theta, int64_t theta_stride,
                                 const nsb_out_csr* out_csr, const nsb_tick_out* out,

@@ -104,6 +104,11 @@ cudaError_t launch_event_scatter_rows(int64_t batch, int64_t neurons, int64_t ro
                                       const EventRowsState* state, int* status,
                                       cudaStream_t stream);
 
+// fp8 / NVFP4 weight encoders (encode.cu); workspace: 4 bytes (the amax word).
+cudaError_t launch_encode(int format, const float* weight, int64_t n, uint8_t* codes,
+                          uint8_t* block_scales, float* global_scale, void* workspace,
+                          cudaStream_t stream);
+
 cudaError_t launch_event(const TickArgs& t, const EventArgs& e, const TickOut& out,
                          const Out& out_emitted, void* workspace, cudaStream_t stream);
 

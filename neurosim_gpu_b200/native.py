@@ -134,7 +134,7 @@ EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_ipc_export", "nsb_ipc_import", "nsb_ipc_release", "nsb_tiled_propagate",
                     "nsb_dendritic_event_noalloc", "nsb_dendritic_step_rows",
                     "nsb_cluster_slots", "nsb_cluster_smem_bytes", "nsb_dendritic_run_cluster",
-                    "nsb_dendritic_event_rows", "nsb_event_scatter_rows",
+                    "nsb_dendritic_event_rows", "nsb_event_scatter_rows", "nsb_encode_weights",
                     "nsb_last_error", "nsb_abi_version")
 
 
@@ -193,11 +193,14 @@ def load_library() -> ctypes.CDLL:
                                            ctypes.c_void_p, p(_ScatterRows), ctypes.c_void_p,
                                            p(_DeltaExchange), ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_void_p]
+    lib.nsb_encode_weights.argtypes = [ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
+                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_last_error.restype = ctypes.c_char_p
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
         getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
-    if lib.nsb_abi_version() != 6:
+    if lib.nsb_abi_version() != 7:
         raise RuntimeError("libneurosim_b200.so ABI version mismatch")
     return lib
 
@@ -481,6 +484,29 @@ class DendriticExtension:
             _raise_on_status(lib, code)
 
         return launch
+
+    # -- weight encoder -----------------------------------------------------------
+    def encode_weights(self, weight: torch.Tensor, precision: str):
+        """``encode_sparse_weights`` on the device (``nsb_encode_weights``): returns
+        (codes uint8, block scales uint8 or None, global scale float32 [1])."""
+        _check(weight.is_cuda and weight.dtype == torch.float32 and weight.dim() == 1
+               and weight.is_contiguous(), "the encoder takes a contiguous CUDA float32 vector")
+        _check(precision in ("fp8", "nvfp4"), "compressed CSR encoding requires fp8 or nvfp4")
+        n = weight.numel()
+        device = weight.device
+        nvfp4 = precision == "nvfp4"
+        codes = torch.empty((n + 1) // 2 if nvfp4 else n, dtype=torch.uint8, device=device)
+        scales = torch.empty((n + 15) // 16, dtype=torch.uint8, device=device) if nvfp4 else None
+        scale = torch.empty(1, dtype=torch.float32, device=device)
+        workspace = torch.empty(64, dtype=torch.int32, device=device)
+        with torch.cuda.device(device):
+            status = self.lib.nsb_encode_weights(
+                NVFP4 if nvfp4 else E4M3, weight.data_ptr() if n else None, n,
+                codes.data_ptr() if codes.numel() else None,
+                scales.data_ptr() if scales is not None and scales.numel() else None,
+                scale.data_ptr(), workspace.data_ptr(), _stream(device))
+        _raise_on_status(self.lib, status)
+        return codes, scales, scale
 
     # -- row-sharded PELS --------------------------------------------------------
     def prepare_event_rows(self, state, dendrite, adaptation, params, current, emitted, theta,

@@ -11,8 +11,9 @@ The encoders produce exactly the bytes of the reference quantizer
          even-indexed weight in the low nibble.
 * decode: fp8 -> e4m3(code) * scale; nvfp4 -> level(code) * (e4m3(block) * g).
 
-They run with PyTorch ops on the weights' device, once per ``weight_version``
-(the runtime caches the packed arrays); the per-tick decode is in the kernel.
+Device weights are encoded by the library's CUDA encoder, host weights by
+PyTorch ops, once per ``weight_version`` (the runtime caches the packed
+arrays); the per-tick decode is in the kernel.
 """
 
 from __future__ import annotations
@@ -88,7 +89,26 @@ def _nvfp4(value: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tenso
 
 def encode_sparse_weights(value: torch.Tensor, precision: str
                           ) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor]:
-    """Packed CSR weight bytes, optional block-scale bytes and the FP32 global scale."""
+    """Packed CSR weight bytes, optional block-scale bytes and the FP32 global scale.
+
+    Weights in device memory are encoded by the library's CUDA encoder
+    (``nsb_encode_weights``, two launches); host weights by the same steps as
+    PyTorch ops.  Both give the reference quantizer's bytes.
+    """
+    if value.ndim != 1 or value.dtype != torch.float32:
+        raise ValueError("encoding requires a vector of FP32 CSR weights")
+    if precision not in ("fp8", "nvfp4"):
+        raise ValueError("compressed CSR encoding requires fp8 or nvfp4")
+    if value.is_cuda:
+        from .native import load_native_extension
+
+        return load_native_extension().encode_weights(value.detach().contiguous(), precision)
+    return encode_sparse_weights_torch(value, precision)
+
+
+def encode_sparse_weights_torch(value: torch.Tensor, precision: str
+                                ) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor]:
+    """The encoder as PyTorch ops on the weights' device (precision.py:76-90)."""
     if value.ndim != 1 or value.dtype != torch.float32:
         raise ValueError("encoding requires a vector of FP32 CSR weights")
     if precision == "fp8":
