@@ -615,6 +615,68 @@ def run_profile(args, workload: str) -> None:
                       "state_mean": float(runtime.state.mean())}))
 
 
+def run_profile_suite(args) -> None:
+    """Two launches of each kernel that is not the headline's, on small cases, in
+    a fixed order; the second launch of each runs inside an NVTX range named
+    ``measure`` (``ncu --nvtx --nvtx-include measure/`` captures just those):
+
+    1. cluster_tick_kernel: config 1 (4,096 / 65k), 64 ticks per launch;
+    2. event_advance_kernel + event_scatter_kernel: PELS at 50k / 1M, theta 0.02,
+       the reference's sinusoidal drive (a warmed-up, active state);
+    3. event_rows_kernel + event_scatter_rows_kernel: the row-sharded PELS tick
+       of one rank holding all rows (no exchange), same graph and drive;
+    4. amax_kernel + fp8_kernel, amax_kernel + nvfp4_kernel: the weight
+       encoders on 40M weights (160 MB, larger than L2).
+    """
+    from neurosim_gpu_b200 import NativeDendriticPELSRuntime, encode_sparse_weights
+    from neurosim_gpu_b200.sharded_pels import ShardedDendriticPELSRuntime
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    drive = [0.2 + 0.1 * math.sin(0.11 * t) for t in range(64)]
+    with torch.inference_mode():
+        small = build_graph(4096, 65_536, device)
+        cluster = NativeDendriticMatrixRuntime(small, bench_model(4096, device),
+                                               torch.zeros(1, 4096, device=device))
+        assert cluster.kernel_path == "cluster"
+        nvtx = torch.cuda.nvtx
+
+        def measured(fn):
+            torch.cuda.synchronize()
+            nvtx.range_push("measure")
+            fn()
+            torch.cuda.synchronize()
+            nvtx.range_pop()
+
+        cluster.run(64, 0.2, dendritic_drive=0.1)  # builds the plan (one launch)
+        cluster.run(64, 0.2, dendritic_drive=0.1)
+        measured(lambda: cluster.run(64, 0.2, dendritic_drive=0.1))
+        graph = build_graph(50_000, 1_000_000, device)
+        model = bench_model(50_000, device)
+        zero = torch.zeros(1, 50_000, device=device)
+        pels = NativeDendriticPELSRuntime(graph, model, zero.clone(), theta=PELS_THETA)
+        rows = ShardedDendriticPELSRuntime((graph.in_rowptr, graph.in_col, graph.in_weight), model,
+                                           zero.clone(), theta=PELS_THETA, rank=0, world=1)
+        for t in range(100):  # warm the dynamics up to the cycle's active phase, eagerly
+            pels.step(drive[t % 64], dendritic_drive=0.1)
+            rows.step(drive[t % 64], dendritic_drive=0.1)
+        torch.cuda.synchronize()
+        pels.step(drive[100 % 64], dendritic_drive=0.1)
+        measured(lambda: pels.step(drive[101 % 64], dendritic_drive=0.1))
+        rows.step(drive[100 % 64], dendritic_drive=0.1)
+        measured(lambda: rows.step(drive[101 % 64], dendritic_drive=0.1))
+        weights = torch.randn(40_000_000, device=device, generator=torch.Generator(device)
+                              .manual_seed(0)) * 0.02
+        for fmt in ("fp8", "nvfp4"):
+            encode_sparse_weights(weights, fmt)
+            measured(lambda: encode_sparse_weights(weights, fmt))
+        torch.cuda.synchronize()
+        marks = {"cluster_state_mean": float(cluster.state.mean()),
+                 "pels_state_mean": float(pels.state.mean()),
+                 "rows_state_mean": float(rows.state.mean())}
+    print(json.dumps({"profile": "suite", **marks}))
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -630,12 +692,17 @@ def main() -> None:
                         help="row-sharded runs: soma / delta exchange (auto: peer stores)")
     parser.add_argument("--profile", action="store_true",
                         help="eager launches only, for ncu captures (prints no bench line)")
+    parser.add_argument("--profile-suite", action="store_true",
+                        help="two launches of each non-headline kernel on small cases, for ncu")
     parser.add_argument("--launch-ticks", type=int, default=1,
                         help="with --profile: ticks per launch of the persistent tiled kernel")
     args = parser.parse_args()
     explicit_workload = args.workload is not None
     if args.workload is None:
         args.workload = DEFAULT_WORKLOAD
+    if args.profile_suite:
+        run_profile_suite(args)
+        return
     if args.profile:
         run_profile(args, args.workload)
         return

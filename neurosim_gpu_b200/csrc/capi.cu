@@ -566,7 +566,7 @@ int nsb_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows, const f
   if (!check_rows_workspace(workspace)) return NSB_ERR_WORKSPACE;
   g_error.clear();
   if (batch == 0) return NSB_OK;
-  const nsb::ScatterRowsArgs c{csr->rowptr, csr->dst, csr->weight};
+  const nsb::ScatterRowsArgs c{csr->rowptr, csr->dst, csr->weight, csr->n_edges};
   const cudaError_t err = nsb::launch_event_scatter_rows(
       batch, neurons, rows, delta, c, current, exchange ? &px : nullptr,
       static_cast<const nsb::EventRowsState*>(workspace), status,

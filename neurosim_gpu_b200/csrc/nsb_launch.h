@@ -93,6 +93,7 @@ struct ScatterRowsArgs {
   const int32_t* rowptr;  // [N+1]
   const int32_t* dst;     // [M_local], rebased to the rank's rows
   const float* weight;    // [M_local]
+  int64_t n_edges;        // M_local
 };
 
 cudaError_t launch_event_rows(const TickArgs& t, const EventRowsArgs& e, const TickOut& out,

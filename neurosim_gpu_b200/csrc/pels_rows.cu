@@ -22,7 +22,8 @@
 //    delta, ballots the nonzero ones and scatters each one's out-edges with a
 //    destination in this rank's range (a source-major CSR filtered to the
 //    rank's rows, destinations rebased) into current[b, dst] with float
-//    atomics, 32 edges per step.
+//    atomics, with G = 8 / 16 / 32 lanes per emitting source (from the mean
+//    degree into the rank's rows), 32 / G sources at a time.
 //
 // The double-buffered delta buffers are safe to reuse: a rank writes parity p
 // again two ticks later, only after every rank has passed its wait of the tick
@@ -87,7 +88,7 @@ event_rows_kernel(TickArgs t, EventRowsArgs e, TickOut out, Out out_emitted, Del
   }
 }
 
-template <bool X>
+template <bool X, int G>
 __global__ void __launch_bounds__(kRowThreads)
 event_scatter_rows_kernel(int64_t batch, int64_t neurons, int64_t rows, const float* delta,
                           ScatterRowsArgs c, float* current, DeltaPeers px,
@@ -112,7 +113,10 @@ event_scatter_rows_kernel(int64_t batch, int64_t neurons, int64_t rows, const fl
     }
     __syncthreads();
   }
+  constexpr int kGroups = 32 / G;  // active sources a warp scatters at once
   const int lane = threadIdx.x & 31;
+  const int group = lane / G;
+  const int lg = lane % G;
   const int64_t entries = batch * neurons;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -122,16 +126,20 @@ event_scatter_rows_kernel(int64_t batch, int64_t neurons, int64_t rows, const fl
     const float d = mine < entries ? __ldcg(delta + mine) : 0.0f;
     unsigned int active = __ballot_sync(0xffffffffu, d != 0.0f);
     while (active) {
-      const int k = __ffs(active) - 1;
-      active &= active - 1;
+      // Group g takes the g-th lowest emitting entry of this round.
+      unsigned int rest = active;
+      for (int i = 0; i < group && rest; ++i) rest &= rest - 1;
+      const int k = rest ? __ffs(rest) - 1 : -1;
+      for (int i = 0; i < kGroups && active; ++i) active &= active - 1;
+      const float value = __shfl_sync(0xffffffffu, d, k < 0 ? 0 : k);
+      if (k < 0) continue;
       const int64_t entry = base + k;
-      const float value = __shfl_sync(0xffffffffu, d, k);
       const int64_t n = entry / batch;
       const int64_t b = entry - n * batch;
       float* row = current + b * rows;
       const int64_t e0 = __ldg(c.rowptr + n);
       const int64_t e1 = __ldg(c.rowptr + n + 1);
-      for (int64_t edge = e0 + lane; edge < e1; edge += 32)
+      for (int64_t edge = e0 + lg; edge < e1; edge += G)
         atomicAdd(row + __ldg(c.dst + edge), __fmul_rn(value, __ldg(c.weight + edge)));
     }
   }
@@ -171,6 +179,40 @@ cudaError_t launch_event_rows(const TickArgs& t, const EventRowsArgs& e, const T
   return cudaGetLastError();
 }
 
+namespace {
+template <bool X, int G>
+cudaError_t scatter_rows_variant(int sm_count, int64_t batch, int64_t neurons, int64_t rows,
+                                 const float* delta, const ScatterRowsArgs& c, float* current,
+                                 const DeltaPeers& px, const EventRowsState* state, int* status,
+                                 cudaStream_t stream) {
+  static int occupancy = 0;
+  if (occupancy == 0) occupancy = resident(event_scatter_rows_kernel<X, G>);
+  const int64_t warps = (batch * neurons + 31) / 32;
+  const int64_t needed = std::max<int64_t>(1, (warps * 32 + kRowThreads - 1) / kRowThreads);
+  const int64_t blocks = std::min<int64_t>(needed, int64_t{sm_count} * occupancy);
+  event_scatter_rows_kernel<X, G><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(
+      batch, neurons, rows, delta, c, current, px, state, status);
+  return cudaGetLastError();
+}
+
+template <bool X>
+cudaError_t scatter_rows_width(int sm_count, int64_t n_edges, int64_t batch, int64_t neurons,
+                               int64_t rows, const float* delta, const ScatterRowsArgs& c,
+                               float* current, const DeltaPeers& px,
+                               const EventRowsState* state, int* status, cudaStream_t stream) {
+  // Lanes per emitting source from the mean out-degree into this rank's rows.
+  const double degree = static_cast<double>(n_edges) / static_cast<double>(std::max<int64_t>(neurons, 1));
+  if (degree <= 12)
+    return scatter_rows_variant<X, 8>(sm_count, batch, neurons, rows, delta, c, current, px, state,
+                                      status, stream);
+  if (degree <= 24)
+    return scatter_rows_variant<X, 16>(sm_count, batch, neurons, rows, delta, c, current, px,
+                                       state, status, stream);
+  return scatter_rows_variant<X, 32>(sm_count, batch, neurons, rows, delta, c, current, px, state,
+                                     status, stream);
+}
+}  // namespace
+
 cudaError_t launch_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows,
                                       const float* delta, const ScatterRowsArgs& c,
                                       float* current, const DeltaPeers* px,
@@ -179,22 +221,11 @@ cudaError_t launch_event_scatter_rows(int64_t batch, int64_t neurons, int64_t ro
   DeviceInfo info;
   cudaError_t err = device_info(&info);
   if (err != cudaSuccess) return err;
-  const int64_t warps = (batch * neurons + 31) / 32;
-  const int64_t needed = std::max<int64_t>(1, (warps * 32 + kRowThreads - 1) / kRowThreads);
-  if (px) {
-    static int occupancy = 0;
-    if (occupancy == 0) occupancy = resident(event_scatter_rows_kernel<true>);
-    const int64_t blocks = std::min<int64_t>(needed, int64_t{info.sm_count} * occupancy);
-    event_scatter_rows_kernel<true><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(
-        batch, neurons, rows, delta, c, current, *px, state, status);
-  } else {
-    static int occupancy = 0;
-    if (occupancy == 0) occupancy = resident(event_scatter_rows_kernel<false>);
-    const int64_t blocks = std::min<int64_t>(needed, int64_t{info.sm_count} * occupancy);
-    event_scatter_rows_kernel<false><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(
-        batch, neurons, rows, delta, c, current, DeltaPeers{}, state, status);
-  }
-  return cudaGetLastError();
+  if (px)
+    return scatter_rows_width<true>(info.sm_count, c.n_edges, batch, neurons, rows, delta, c,
+                                    current, *px, state, status, stream);
+  return scatter_rows_width<false>(info.sm_count, c.n_edges, batch, neurons, rows, delta, c,
+                                   current, DeltaPeers{}, state, status, stream);
 }
 
 }  // namespace nsb
