@@ -636,15 +636,18 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
     if (threadIdx.x == 0) *next_task = kConsumerWarps;
     grid_barrier(L.barrier, st);  // every row sum of this tick is in part
 
-    // Update of rows [update_lo, update_hi), two rows per thread per round:
-    // every operand of both rows is loaded before any store, so a round costs
+    // Update of rows [update_lo, update_hi), one row per thread per round:
+    // every operand of the row is loaded before any store, so a round costs
     // one memory round trip.  The row sums and the state written by earlier
-    // ticks of this launch are read through L2.
+    // ticks of this launch are read through L2.  (Two rows per round would
+    // save a round for the few threads with a second row, but its operands
+    // raise the kernel's register need, and the spills that follow slow the
+    // streaming loop: 41.0 against 37.6 us per tick at 166k / 25M fp32.)
     const int planes = static_cast<int>((L.cols + L.block_cols - 1) / L.block_cols) * L.splits;
-    for (int64_t n0 = update_lo + threadIdx.x; n0 < update_hi; n0 += 2 * blockDim.x) {
-      float j[2], s0[2], d0[2], a0[2], u[2], v[2], pr[2][6];
+    for (int64_t n0 = update_lo + threadIdx.x; n0 < update_hi; n0 += blockDim.x) {
+      float j[1], s0[1], d0[1], a0[1], u[1], v[1], pr[1][6];
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
+      for (int r = 0; r < 1; ++r) {
         const int64_t n = n0 + r * blockDim.x;
         const bool row = n < update_hi;
         s0[r] = d0[r] = a0[r] = u[r] = v[r] = 0.0f;
@@ -683,7 +686,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
         }
       }
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
+      for (int r = 0; r < 1; ++r) {
         const int64_t n = n0 + r * blockDim.x;
         if (n >= update_hi) continue;
         for (int k = 0; k < planes; ++k) L.part[n + k * L.rows] = 0.0f;
