@@ -265,12 +265,14 @@ def run_pels(args, workload: str) -> dict:
                    "theta": PELS_THETA, "active_neurons_per_tick": active_neurons,
                    "active_edges_per_tick": active_edges,
                    "active_edge_fraction": active_edges / max(m * batch, 1),
-                   "kernel_path": "pels", "ticks_per_graph": chunk},
+                   "kernel_path": "pels-" + runtime.propagation_path, "ticks_per_graph": chunk},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": None,
                      "algorithmic_bytes_per_launch": algo, "peak_source": peak_kind,
-                     "kernel": "event_advance_kernel + event_scatter_kernel", "per": "tick"},
-        "gpu_launches": 2 * steps,
+                     "kernel": "event_advance_kernel + event_scatter_kernel"
+                     + (" + tiled_tick_kernel (gated)" if runtime.propagation_path == "hybrid" else ""),
+                     "per": "tick"},
+        "gpu_launches": (3 if runtime.propagation_path == "hybrid" else 2) * steps,
     }
 
 

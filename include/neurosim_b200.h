@@ -45,7 +45,7 @@ extern "C" {
 #define NSB_API
 #endif
 
-#define NSB_ABI_VERSION 7
+#define NSB_ABI_VERSION 8
 
 enum nsb_status {
   NSB_OK = 0,
@@ -437,6 +437,26 @@ NSB_API int nsb_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows,
 NSB_API int nsb_encode_weights(int32_t format, const float* weight, int64_t n, uint8_t* codes,
                                uint8_t* block_scales, float* global_scale, void* workspace,
                                void* stream);
+
+/* Hybrid PELS tick (B = 1; no counterpart in the reference): the same tick as
+ * nsb_dendritic_event, with the propagation of the emitted deltas chosen on the
+ * device from this tick's activity.  The advance also writes every neuron's
+ * delta (0 where it does not emit) to `dense` ([N] floats, 16-byte aligned).
+ * Then, if the emitting sources have fewer than `gate_edges` (>= 1) out-edges
+ * in total, the active-edge scatter adds them into `current` (float atomics);
+ * otherwise the tiled kernel adds W @ dense into `current` (`layout`: the
+ * nsb_tiled_layout of the float32 destination CSR, N x N, with its workspace;
+ * deterministic sums).  Both launches are always enqueued and the unselected
+ * one returns at once, so the call can be captured into a CUDA graph.
+ * `status` receives the tiled kernel's timeout codes (may be NULL). */
+NSB_API int nsb_dendritic_event_hybrid(const nsb_tick* tick, float* current,
+                                       const nsb_view* emitted, const float* theta,
+                                       int64_t theta_stride, const nsb_out_csr* out_csr,
+                                       const nsb_tiled_layout* layout, void* tiled_workspace,
+                                       size_t tiled_workspace_bytes, float* dense,
+                                       uint64_t gate_edges, const nsb_tick_out* out,
+                                       const nsb_out* out_emitted, void* workspace,
+                                       size_t workspace_bytes, int* status, void* stream);
 
 /* NSB_ABI_VERSION of the loaded library. */
 NSB_API int nsb_abi_version(void);

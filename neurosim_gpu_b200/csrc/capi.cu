@@ -446,10 +446,22 @@ size_t nsb_dendritic_event_workspace_size(int64_t batch, int64_t neurons) {
   return nsb::event_workspace_bytes(batch, neurons);
 }
 
-int nsb_dendritic_event(const nsb_tick* tick, float* current, const nsb_view* emitted,
-                        const float* theta, int64_t theta_stride, const nsb_out_csr* out_csr,
-                        const nsb_tick_out* out, const nsb_out* out_emitted, void* workspace,
-                        size_t workspace_bytes, void* stream) {
+namespace {
+// The PELS tick, with or without the hybrid propagation (hybrid == nullptr:
+// the scatter handles every tick).
+struct HybridArgs {
+  const nsb_tiled_layout* layout;
+  void* tiled_workspace;
+  size_t tiled_workspace_bytes;
+  float* dense;
+  uint64_t gate_edges;
+  int* status;
+};
+
+int event_tick(const nsb_tick* tick, float* current, const nsb_view* emitted, const float* theta,
+               int64_t theta_stride, const nsb_out_csr* out_csr, const nsb_tick_out* out,
+               const nsb_out* out_emitted, void* workspace, size_t workspace_bytes,
+               const HybridArgs* hybrid, void* stream, const char* name) {
   nsb::TickArgs t;
   if (!check_tick(tick, &t)) return NSB_ERR_ARGUMENT;
   if (t.batch > 0 && (!current || !emitted || !emitted->data))
@@ -467,9 +479,22 @@ int nsb_dendritic_event(const nsb_tick* tick, float* current, const nsb_view* em
   if (!workspace || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
     return fail(NSB_ERR_WORKSPACE, "event workspace must be 256-byte aligned and at least " +
                                        std::to_string(need) + " bytes");
+  if (hybrid) {
+    if (t.batch != 1) return fail(NSB_ERR_ARGUMENT, "the hybrid PELS tick takes B = 1");
+    if (!check_tiled(hybrid->layout)) return tiled_status(NSB_ERR_ARGUMENT);
+    if (hybrid->layout->rows != t.neurons || hybrid->layout->cols != t.neurons ||
+        hybrid->layout->format != NSB_WEIGHT_F32)
+      return fail(NSB_ERR_ARGUMENT, "the hybrid layout must be the N x N float32 destination CSR");
+    if (!check_workspace(hybrid->layout, hybrid->tiled_workspace, hybrid->tiled_workspace_bytes))
+      return NSB_ERR_WORKSPACE;
+    if (!hybrid->dense || !aligned(hybrid->dense, 16))
+      return fail(NSB_ERR_ARGUMENT, "the hybrid tick needs a 16-byte aligned [N] delta buffer");
+    if (hybrid->gate_edges == 0)
+      return fail(NSB_ERR_ARGUMENT, "the hybrid gate must be at least one edge");
+  }
   g_error.clear();
   if (t.batch == 0) return NSB_OK;
-  nsb::EventArgs e;
+  nsb::EventArgs e{};
   e.current = current;
   e.current_out = current;
   e.emitted = to_view(*emitted);
@@ -480,11 +505,52 @@ int nsb_dendritic_event(const nsb_tick* tick, float* current, const nsb_view* em
   e.weight_index = out_csr->weight_index;
   e.weight = out_csr->weight;
   e.n_edges = out_csr->n_edges;
+  e.dense = hybrid ? hybrid->dense : nullptr;
+  e.gate_edges = hybrid ? hybrid->gate_edges : 0;
   const nsb::TickOut o{to_out(out->state), to_out(out->dendrite), to_out(out->adaptation)};
-  const cudaError_t err = nsb::launch_event(t, e, o, to_out(*out_emitted), workspace,
-                                            static_cast<cudaStream_t>(stream));
-  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_event launch");
+  cudaError_t err = nsb::launch_event(t, e, o, to_out(*out_emitted), workspace,
+                                      static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, name);
+  if (hybrid) {
+    // Ticks at or above the gate: current += W @ delta by the tiled kernel
+    // (the scatter has returned for them; below the gate this launch returns).
+    nsb::TiledGate gate;
+    gate.count = reinterpret_cast<const unsigned long long*>(
+        &static_cast<const nsb_event_counters*>(workspace)->active_edges);
+    gate.min = hybrid->gate_edges;
+    gate.accumulate = true;
+    nsb::TickArgs none{};
+    none.batch = 1;
+    none.neurons = t.neurons;
+    err = nsb::launch_tiled(*hybrid->layout, none, hybrid->dense, false, 1, nsb::TickOut{},
+                            nsb::Out{current, 0, 1}, hybrid->tiled_workspace, hybrid->status,
+                            static_cast<cudaStream_t>(stream), nullptr, gate);
+    if (err != cudaSuccess) return cuda_fail(err, name);
+  }
   return NSB_OK;
+}
+}  // namespace
+
+int nsb_dendritic_event(const nsb_tick* tick, float* current, const nsb_view* emitted,
+                        const float* theta, int64_t theta_stride, const nsb_out_csr* out_csr,
+                        const nsb_tick_out* out, const nsb_out* out_emitted, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  return event_tick(tick, current, emitted, theta, theta_stride, out_csr, out, out_emitted,
+                    workspace, workspace_bytes, nullptr, stream, "nsb_dendritic_event launch");
+}
+
+int nsb_dendritic_event_hybrid(const nsb_tick* tick, float* current, const nsb_view* emitted,
+                               const float* theta, int64_t theta_stride,
+                               const nsb_out_csr* out_csr, const nsb_tiled_layout* layout,
+                               void* tiled_workspace, size_t tiled_workspace_bytes, float* dense,
+                               uint64_t gate_edges, const nsb_tick_out* out,
+                               const nsb_out* out_emitted, void* workspace,
+                               size_t workspace_bytes, int* status, void* stream) {
+  const HybridArgs hybrid{layout, tiled_workspace, tiled_workspace_bytes, dense, gate_edges,
+                          status};
+  return event_tick(tick, current, emitted, theta, theta_stride, out_csr, out, out_emitted,
+                    workspace, workspace_bytes, &hybrid, stream,
+                    "nsb_dendritic_event_hybrid launch");
 }
 
 namespace {

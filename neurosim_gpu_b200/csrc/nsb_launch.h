@@ -45,6 +45,8 @@ struct EventArgs {
   const int32_t* weight_index;  // nullptr: weight is source-major
   const float* weight;
   int64_t n_edges;
+  float* dense;                  // hybrid: [B,N] contiguous delta of every pair (0: none), or null
+  unsigned long long gate_edges;  // hybrid: the scatter runs only below this many active edges (0: always)
 };
 
 // Tiled B = 1 tick with the gathered state staged in shared memory (tiled.cu):
@@ -52,10 +54,19 @@ struct EventArgs {
 // in place on `out`).
 size_t tiled_smem_bytes(int block_cols, int buffers);
 size_t tiled_workspace_bytes(const nsb_tiled_layout& layout);
+// Gate of a propagate-only launch (the hybrid PELS tick): the kernel returns at
+// once unless *count >= min, and with `accumulate` adds W @ x into `product`.
+struct TiledGate {
+  const unsigned long long* count = nullptr;
+  unsigned long long min = 0;
+  bool accumulate = false;
+};
+
 cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, const float* x,
                          bool update, int ticks, const TickOut& out, const Out& product,
                          void* workspace, int* status, cudaStream_t stream,
-                         const nsb_peer_exchange* exchange = nullptr);
+                         const nsb_peer_exchange* exchange = nullptr,
+                         const TiledGate& gate = TiledGate{});
 
 // Small-graph tick on one thread-block cluster (cluster.cu): `ticks` ticks of
 // B = 1 with the state and the edges in the cluster's shared memory.

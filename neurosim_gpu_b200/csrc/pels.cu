@@ -58,6 +58,7 @@ event_advance_kernel(TickArgs t, EventArgs e, TickOut out, Out out_emitted, uint
       const float residual = __fsub_rn(r.s, previous);
       active = fabsf(residual) >= __ldg(e.theta + n * e.theta_stride);
       out_emitted.put(b, n, active ? r.s : previous);
+      if (e.dense) e.dense[i] = active ? residual : 0.0f;
       if (active) {
         degree = static_cast<unsigned int>(__ldg(e.out_rowptr + n + 1) - __ldg(e.out_rowptr + n));
         delta = residual;
@@ -97,6 +98,11 @@ event_scatter_kernel(EventArgs e, int64_t neurons, const uint2* __restrict__ que
   const int lg = threadIdx.x % G;
   const int64_t group = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / G;
   const int64_t n_groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) / G;
+  // Hybrid tick: at or above the gate the tiled kernel propagates this tick's
+  // deltas instead (all threads read the same count, written by the advance).
+  if (e.gate_edges &&
+      *reinterpret_cast<const volatile unsigned long long*>(&counters->active_edges) >= e.gate_edges)
+    return;
   const int64_t queued = *reinterpret_cast<const volatile unsigned int*>(&counters->queued);
   const uint64_t pol = evict_first_policy();
   for (int64_t q = group; q < queued; q += n_groups) {

@@ -383,10 +383,12 @@ __device__ void peer_barrier(const Peers& px, unsigned long long* local, int tic
 
 // X: the row-sharded variant with the peer exchange (nsb_dendritic_run_tiled_peers);
 // the single-GPU instantiation carries none of its code.
-template <typename W, int D, bool X>
+// G: the gated, accumulating propagate-only launch of the hybrid PELS tick.
+template <typename W, int D, bool X, bool G>
 __global__ void __launch_bounds__(kTiledThreads, 1)
 tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ x0, TickOut out,
-                  Out product, bool update, int ticks, int* status, Peers px) {
+                  Out product, bool update, int ticks, int* status, Peers px,
+                  const unsigned long long* gate_count, unsigned long long gate_min) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int nbuf = L.buffers;
   const int cb_pad = L.block_cols + 4;
@@ -395,6 +397,11 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
   int* next_task = reinterpret_cast<int*>(empty + 2);
   float* sbuf = reinterpret_cast<float*>(smem_raw + kTiledHeader);    // [nbuf][cb_pad]
   int* st = status ? status : &g_tiled_status;
+  // A gated launch whose count is below its minimum leaves at once: every CTA
+  // reads the same count (written by an earlier launch), so all leave together,
+  // before any barrier.
+  if (G && *reinterpret_cast<const volatile unsigned long long*>(gate_count) < gate_min)
+    return;
 
   const int c = blockIdx.x;
   const int warp = threadIdx.x >> 5;
@@ -701,7 +708,10 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
           out.d.put(0, n, q.d);
           out.a.put(0, n, q.a);
         } else {
-          product.put(0, n, j[r]);
+          if (G)
+            product.data[n * product.sn] += j[r];
+          else
+            product.put(0, n, j[r]);
         }
       }
     }
@@ -715,13 +725,14 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
   }
 }
 
-template <typename W, int D, bool X>
+template <typename W, int D, bool X, bool G>
 cudaError_t launch_tiled_kernel(const TiledArgs& L, const W& w, const TickArgs& t,
                                 const float* x, const TickOut& out, const Out& product,
                                 bool update, int ticks, int* status, int ctas,
-                                cudaStream_t stream, const Peers& px) {
+                                cudaStream_t stream, const Peers& px,
+                                const TiledGate& gate = TiledGate{}) {
   const size_t smem = tiled_smem_bytes(L.block_cols, L.buffers);
-  auto kernel = tiled_tick_kernel<W, D, X>;
+  auto kernel = tiled_tick_kernel<W, D, X, G>;
   static int configured[64] = {0};
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
@@ -743,7 +754,8 @@ cudaError_t launch_tiled_kernel(const TiledArgs& L, const W& w, const TickArgs& 
   attribute[0].val.cooperative = 1;
   config.attrs = attribute;
   config.numAttrs = 1;
-  return cudaLaunchKernelEx(&config, kernel, L, w, t, x, out, product, update, ticks, status, px);
+  return cudaLaunchKernelEx(&config, kernel, L, w, t, x, out, product, update, ticks, status, px,
+                            gate.count, gate.min);
 }
 
 template <typename W, int D>
@@ -752,10 +764,10 @@ cudaError_t launch_tiled_variant(const TiledArgs& L, const W& w, const TickArgs&
                                  bool update, int ticks, int* status, int ctas,
                                  cudaStream_t stream, const Peers& px) {
   if (px.world > 0)
-    return launch_tiled_kernel<W, D, true>(L, w, t, x, out, product, update, ticks, status, ctas,
-                                           stream, px);
-  return launch_tiled_kernel<W, D, false>(L, w, t, x, out, product, update, ticks, status, ctas,
-                                          stream, px);
+    return launch_tiled_kernel<W, D, true, false>(L, w, t, x, out, product, update, ticks, status,
+                                                  ctas, stream, px);
+  return launch_tiled_kernel<W, D, false, false>(L, w, t, x, out, product, update, ticks, status,
+                                                 ctas, stream, px);
 }
 
 }  // namespace
@@ -772,7 +784,7 @@ size_t tiled_workspace_bytes(const nsb_tiled_layout& layout) {
 cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, const float* x,
                          bool update, int ticks, const TickOut& out, const Out& product,
                          void* workspace, int* status, cudaStream_t stream,
-                         const nsb_peer_exchange* exchange) {
+                         const nsb_peer_exchange* exchange, const TiledGate& gate) {
   Peers px{};
   if (exchange) {
     px.world = exchange->world;
@@ -812,6 +824,11 @@ cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, cons
                               : 0;
   L.prefetch_first = prefetch ? kConsumerWarps : 0;
   const int ctas = layout.ctas;
+  if (gate.count) {  // the hybrid PELS propagate: float32 weights only (checked by the caller)
+    return launch_tiled_kernel<ChunkF32, 4, false, true>(
+        L, ChunkF32{static_cast<const float*>(layout.weight)}, t, x, out, product, update, ticks,
+        status, ctas, stream, Peers{}, gate);
+  }
   switch (layout.format) {
     case NSB_WEIGHT_F16:
       return launch_tiled_variant<ChunkF16, 4>(L, ChunkF16{static_cast<const __half*>(layout.weight)},

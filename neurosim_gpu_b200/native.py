@@ -135,6 +135,7 @@ EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_dendritic_event_noalloc", "nsb_dendritic_step_rows",
                     "nsb_cluster_slots", "nsb_cluster_smem_bytes", "nsb_dendritic_run_cluster",
                     "nsb_dendritic_event_rows", "nsb_event_scatter_rows", "nsb_encode_weights",
+                    "nsb_dendritic_event_hybrid",
                     "nsb_last_error", "nsb_abi_version")
 
 
@@ -196,11 +197,15 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_encode_weights.argtypes = [ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_dendritic_event_hybrid.argtypes = [
+        p(_Tick), ctypes.c_void_p, p(_View), ctypes.c_void_p, ctypes.c_int64, p(_OutCsr),
+        p(_TiledLayout), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_uint64,
+        p(_TickOut), p(_Out), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_last_error.restype = ctypes.c_char_p
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
         getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
-    if lib.nsb_abi_version() != 7:
+    if lib.nsb_abi_version() != 8:
         raise RuntimeError("libneurosim_b200.so ABI version mismatch")
     return lib
 
@@ -720,7 +725,10 @@ class DendriticExtension:
 
     def dendritic_event(self, state, dendrite, adaptation, params, current, emitted, theta,
                         out_rowptr, dst, out_weight_index, weight, input, input_scalar,
-                        dendritic_input, dendritic_scalar, *, workspace=None):
+                        dendritic_input, dendritic_scalar, *, workspace=None, hybrid=None):
+        """The PELS tick (``dendritic_event``).  ``hybrid`` = (tiled layout of the
+        float32 destination CSR, dense [N] delta buffer, gate in active edges,
+        status word) selects ``nsb_dendritic_event_hybrid`` (B = 1)."""
         _check_state(state)
         tick = _tick(state, dendrite, adaptation, params, input, input_scalar,
                      dendritic_input, dendritic_scalar)
@@ -749,11 +757,26 @@ class DendriticExtension:
         if workspace is None:
             workspace = self.event_workspace(state)
         with torch.cuda.device(state.device):
-            status = self.lib.nsb_dendritic_event(
-                ctypes.byref(tick), current.data_ptr(), ctypes.byref(emitted_view),
-                theta.data_ptr(), theta.stride(0), ctypes.byref(out_csr), ctypes.byref(out),
-                ctypes.byref(out_emitted), workspace.data_ptr(), workspace.numel(),
-                _stream(state.device))
+            if hybrid is None:
+                status = self.lib.nsb_dendritic_event(
+                    ctypes.byref(tick), current.data_ptr(), ctypes.byref(emitted_view),
+                    theta.data_ptr(), theta.stride(0), ctypes.byref(out_csr), ctypes.byref(out),
+                    ctypes.byref(out_emitted), workspace.data_ptr(), workspace.numel(),
+                    _stream(state.device))
+            else:
+                layout, dense, gate, word = hybrid
+                _float_on(dense, state)
+                _check(dense.is_contiguous() and dense.numel() == state.size(1),
+                       "the hybrid delta buffer must be a contiguous [N]")
+                c_layout = layout.c_struct()
+                tiled_ws = layout.workspace()
+                status = self.lib.nsb_dendritic_event_hybrid(
+                    ctypes.byref(tick), current.data_ptr(), ctypes.byref(emitted_view),
+                    theta.data_ptr(), theta.stride(0), ctypes.byref(out_csr),
+                    ctypes.byref(c_layout), tiled_ws.data_ptr(), tiled_ws.numel(),
+                    dense.data_ptr(), int(gate), ctypes.byref(out), ctypes.byref(out_emitted),
+                    workspace.data_ptr(), workspace.numel(),
+                    word.data_ptr() if word is not None else None, _stream(state.device))
         _raise_on_status(self.lib, status)
         return views
 

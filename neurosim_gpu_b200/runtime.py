@@ -440,6 +440,7 @@ class _EventGraph:
         workspace = runtime._workspace_for(state)
         params = runtime._parameters()
         current = runtime.persistent_current
+        hybrid = runtime._hybrid()  # built outside the capture
 
         # u / us: one drive per graph tick, or one for all of them.
         drive_at = (lambda k: (u[k % len(u)], us[k % len(us)]))
@@ -451,7 +452,7 @@ class _EventGraph:
                 s, d, a, e = ext.dendritic_event(
                     s, d, a, params, current, e, runtime.theta, topology.out_rowptr,
                     topology.dst, None, topology.weight.detach(), uk, usk, v, vs,
-                    workspace=workspace)
+                    workspace=workspace, hybrid=hybrid)
             return s, d, a, e
 
         # Warm-up outside capture must not advance the simulation: run it on
@@ -467,7 +468,7 @@ class _EventGraph:
             ext.dendritic_event(*self.inputs[:3], params, current, self.inputs[3],
                                 runtime.theta, topology.out_rowptr, topology.dst, None,
                                 topology.weight.detach(), *drive_at(0), v, vs,
-                                workspace=workspace)
+                                workspace=workspace, hybrid=hybrid)
             current.copy_(saved)
         torch.cuda.current_stream(device).wait_stream(stream)
         self.graph = torch.cuda.CUDAGraph()
@@ -499,9 +500,14 @@ class NativeDendriticPELSRuntime(_NativeCompartments):
 
     def __init__(self, topology: SparseTopology, dynamics: DendriticDynamics,
                  initial_state: torch.Tensor, *, theta: float | torch.Tensor,
-                 extension=None, precision: str | None = None) -> None:
+                 extension=None, precision: str | None = None, propagation: str = "auto",
+                 hybrid_gate: float = 0.15) -> None:
         if precision not in (None, "fp32"):
             raise ValueError("native PELS supports FP32 only")
+        if propagation not in ("auto", "event", "hybrid"):
+            raise ValueError("propagation must be 'auto', 'event' or 'hybrid'")
+        if not 0.0 < hybrid_gate <= 1.0:
+            raise ValueError("hybrid_gate must be in (0, 1]")
         if initial_state.device.type != "cuda" or initial_state.dtype != torch.float32:
             raise ValueError("native compartment runtime requires CUDA float32")
         self._init_compartments(topology, dynamics, initial_state, extension)
@@ -514,6 +520,11 @@ class NativeDendriticPELSRuntime(_NativeCompartments):
         self._tick = 0
         self._weight_version = topology.weight_version
         self._workspace = None
+        self.propagation_mode = propagation
+        self.hybrid_gate = hybrid_gate
+        self._hybrid_key = None
+        self._hybrid_args = None
+        self._status = _tiled.status_word(initial_state.device)
 
     def _invalidate_precision_cache(self) -> None:
         pass
@@ -538,6 +549,47 @@ class NativeDendriticPELSRuntime(_NativeCompartments):
         if self._weight_version != self.topology.weight_version:
             self.persistent_current = self._propagate(self.emitted_state).contiguous()
             self._weight_version = self.topology.weight_version
+
+    @property
+    def propagation_path(self) -> str:
+        """'hybrid' (per tick on the device: active-edge scatter below the gate,
+        tiled W @ delta at or above it) or 'event' (the scatter every tick)."""
+        return "hybrid" if self._hybrid() is not None else "event"
+
+    def check_status(self) -> None:
+        """Raise if a hybrid tick's tiled launch reported a pipeline timeout."""
+        code = int(self._status.item())
+        if code:
+            raise RuntimeError(f"tiled propagation pipeline timeout (code {code})")
+
+    def _hybrid(self):
+        """(layout, dense delta buffer, gate in edges, status) or None.
+
+        ``propagation='auto'`` uses the hybrid tick at B = 1 for graphs of at
+        least 2^20 edges: a tick whose emitting sources have at least
+        ``hybrid_gate`` x M out-edges propagates its deltas with the tiled
+        kernel (W @ delta, no atomics) instead of the scatter.
+        """
+        state = self.state
+        topology = self.topology
+        wanted = self.propagation_mode == "hybrid" or (
+            self.propagation_mode == "auto" and topology.n_edges >= (1 << 20))
+        if not wanted or state.shape[0] != 1 or topology.n_edges == 0:
+            if self.propagation_mode == "hybrid" and state.shape[0] != 1:
+                raise ValueError("the hybrid PELS tick takes B = 1")
+            return None
+        key = (topology.weight_version, state.device)
+        if self._hybrid_key != key:
+            device = state.device
+            layout = _tiled.build_tiled_layout(
+                topology.in_rowptr, topology.in_col, topology.in_weight.detach().float(),
+                neurons=topology.n_neurons, ctas=_tiled.sm_count(device),
+                smem_limit=_tiled.smem_limit(device))
+            dense = torch.zeros(topology.n_neurons, device=device)
+            gate = max(1, int(self.hybrid_gate * topology.n_edges))
+            self._hybrid_args = (layout, dense, gate, self._status)
+            self._hybrid_key = key
+        return self._hybrid_args
 
     def _workspace_for(self, state: torch.Tensor) -> torch.Tensor:
         need = int(self.extension.lib.nsb_dendritic_event_workspace_size(*state.shape))
@@ -564,7 +616,7 @@ class NativeDendriticPELSRuntime(_NativeCompartments):
                 self.state, self.dendritic_state, self.adaptation_state, self._parameters(),
                 self.persistent_current, self.emitted_state, self.theta, topology.out_rowptr,
                 topology.dst, None, topology.weight.detach(), u, us, v, vs,
-                workspace=workspace))
+                workspace=workspace, hybrid=self._hybrid()))
         self._tick += 1
         if not collect_stats:
             self.last_backend = "native"

@@ -235,3 +235,70 @@ def test_run_with_a_drive_cycle_equals_steps(ext):
     torch.testing.assert_close(replayed.state, stepped.state, atol=1e-5, rtol=0)
     with pytest.raises(ValueError, match="cycle"):
         replayed.run(20, cycle, dendritic_drive=0.1, graph_ticks=16)
+
+
+# --- hybrid propagation (B = 1): scatter below the gate, tiled W @ delta above it ---
+
+def test_hybrid_theta_zero_through_the_tiled_propagation_equals_the_matrix_tick(ext):
+    """theta = 0: every neuron emits, so every tick is above any gate below M and
+    the deltas are propagated by the tiled kernel; the tick equals the matrix tick."""
+    n = 20000
+    graph = random_topology(n, 400000, device="cpu", seed=8).to("cuda")
+    model = bench_model(n)
+    initial = torch.rand(1, n, generator=torch.Generator().manual_seed(2)).cuda()
+    pels = NativeDendriticPELSRuntime(graph, model, initial.clone(), theta=0.0,
+                                      propagation="hybrid", hybrid_gate=0.5)
+    assert pels.propagation_path == "hybrid"
+    reference = OracleMatrix(graph, model, initial)
+    with torch.inference_mode():
+        for _ in range(40):
+            pels.step(0.2, dendritic_drive=0.1)
+            reference.step(0.2, 0.1)
+        pels.run(64, 0.2, dendritic_drive=0.1, graph_ticks=32)
+    for _ in range(64):
+        reference.step(0.2, 0.1)
+    assert_same_as(pels, reference, atol=8e-6, rtol=0)
+    pels.check_status()
+
+
+@pytest.mark.parametrize("gate", [1e-6, 0.05, 1.0])
+def test_hybrid_theta_nonzero_matches_the_event_path(ext, gate):
+    """theta = 0.02 under the reference's sinusoidal drive: light ticks take the
+    scatter and heavy ones the tiled kernel (gate 0.05); all tiled (1e-6) or all
+    scatter (1.0).  Equal to the event path for the first ticks; afterwards the
+    persistent current stays W @ emitted."""
+    import math
+    n = 20000
+    graph = random_topology(n, 400000, device="cpu", seed=8).to("cuda")
+    model = bench_model(n)
+    initial = torch.rand(1, n, generator=torch.Generator().manual_seed(4)).cuda()
+    hybrid = NativeDendriticPELSRuntime(graph, model, initial.clone(), theta=0.02,
+                                        propagation="hybrid", hybrid_gate=gate)
+    event = NativeDendriticPELSRuntime(graph, model, initial.clone(), theta=0.02,
+                                       propagation="event")
+    assert event.propagation_path == "event"
+    drive = [0.2 + 0.1 * math.sin(0.11 * t) for t in range(32)]
+    with torch.inference_mode():
+        for t in range(4):
+            hybrid.step(drive[t], dendritic_drive=0.1)
+            event.step(drive[t], dendritic_drive=0.1)
+    for name in ("state", "dendritic_state", "adaptation_state", "emitted_state",
+                 "persistent_current"):
+        torch.testing.assert_close(getattr(hybrid, name), getattr(event, name), atol=2e-6,
+                                   rtol=0, msg=name)
+    with torch.inference_mode():
+        hybrid.run(64, drive, dendritic_drive=0.1, graph_ticks=32)
+    want = oracle.spmv(csr_of(graph), npy(hybrid.emitted_state))
+    np.testing.assert_allclose(npy(hybrid.persistent_current), want, atol=2e-5, rtol=0)
+    hybrid.check_status()
+
+
+def test_hybrid_is_for_single_batches(ext):
+    graph, model, state = make(500, 2, 5000)
+    with pytest.raises(ValueError, match="B = 1"):
+        NativeDendriticPELSRuntime(graph, model, state, theta=0.02,
+                                   propagation="hybrid").step(0.2)
+    with pytest.raises(ValueError, match="propagation"):
+        NativeDendriticPELSRuntime(graph, model, state, theta=0.02, propagation="matrix")
+    auto = NativeDendriticPELSRuntime(graph, model, state[:1].clone(), theta=0.02)
+    assert auto.propagation_path == "event"  # below 2^20 edges the scatter does every tick
