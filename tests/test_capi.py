@@ -129,3 +129,13 @@ def test_empty_batch_needs_no_output_arrays(lib):
     out = native._TickOut()
     status, message = _step(lib, _tick(batch=0), _csr(), out=out)
     assert status == 0 and message == ""
+
+
+def test_hybrid_event_rejects_bad_arguments(lib):
+    """nsb_dendritic_event_hybrid validates like nsb_dendritic_event, then its own
+    arguments (B = 1, an N x N float32 layout, a delta buffer, a gate >= 1)."""
+    tick = _tick(batch=2, neurons=4)
+    status = lib.nsb_dendritic_event_hybrid(ctypes.byref(tick), None, None, None, 0, None, None,
+                                            None, 0, None, 1, None, None, None, 0, None, None)
+    assert status != 0
+    assert b"current" in lib.nsb_last_error() or b"required" in lib.nsb_last_error()
