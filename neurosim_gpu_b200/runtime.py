@@ -392,6 +392,77 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         return self.state
 
 
+    # -- streamed rollout: host drives in, host states out ----------------------
+    def stream(self, drives: torch.Tensor, out: torch.Tensor | None = None, *,
+               dendritic_drive: torch.Tensor | float = 0.0) -> torch.Tensor:
+        """Advance ``len(drives)`` ticks; tick t is driven by ``drives[t]`` ([B, N]
+        or broadcastable) and its new soma state is copied into ``out[t]``.
+
+        ``drives`` and ``out`` ([T, B, N] float32) may live on the host: pinned
+        host memory lets the copies overlap the ticks.  The drive of tick t + 1
+        is uploaded on one CUDA stream and the state of tick t - 1 downloaded on
+        another while tick t runs; every tick's two copies still happen, and
+        ``out`` holds every tick's state when the call returns.  Equal to
+        ``len(drives)`` calls of :meth:`step` with those drives.  Returns
+        ``out`` (allocated pinned if not given).
+        """
+        if self._needs_autograd(0.0, dendritic_drive) or drives.requires_grad:
+            raise RuntimeError("stream() is inference-only; use step() for autograd")
+        ticks = drives.shape[0]
+        state = self.state
+        device = state.device
+        batch, neurons = state.shape
+        if out is None:
+            out = torch.empty((ticks, batch, neurons), dtype=state.dtype,
+                              pin_memory=drives.device.type == "cpu",
+                              device=drives.device if drives.device.type == "cuda" else "cpu")
+        if out.shape[:1] != (ticks,) or out.shape[1:] != state.shape or out.dtype != state.dtype:
+            raise ValueError("out must be [T, B, N] float32")
+        if ticks == 0:
+            return out
+        v, vs = self._drive(dendritic_drive, "dendritic_drive")
+        drive_buf = [torch.empty_like(state) for _ in range(2)]
+        buffers = [(torch.empty_like(state), torch.empty_like(state), torch.empty_like(state))
+                   for _ in range(2)]
+        for target, value in zip(buffers[0], (state, self.dendritic_state,
+                                              self.adaptation_state)):
+            target.copy_(value)
+        # One launch callable per parity: tick t reads buffers[t % 2] and
+        # drive_buf[t % 2] and writes buffers[(t + 1) % 2].
+        calls = [self._prepare(*buffers[k], drive_buf[k], 0.0, v, vs, buffers[1 - k])
+                 for k in range(2)]
+        compute = torch.cuda.current_stream(device)
+        upload = torch.cuda.Stream(device=device)
+        download = torch.cuda.Stream(device=device)
+        uploaded = [torch.cuda.Event() for _ in range(2)]
+        consumed = [torch.cuda.Event() for _ in range(2)]   # tick t done with drive_buf / buffers[t % 2]
+        saved = [torch.cuda.Event() for _ in range(2)]      # download of buffers[k] finished
+        upload.wait_stream(compute)
+        download.wait_stream(compute)
+        with torch.inference_mode():
+            for t in range(ticks):
+                k = t % 2
+                with torch.cuda.stream(upload):
+                    if t >= 2:
+                        upload.wait_event(consumed[k])
+                    drive_buf[k].copy_(drives[t].expand(batch, neurons), non_blocking=True)
+                    uploaded[k].record(upload)
+                compute.wait_event(uploaded[k])
+                if t >= 1:
+                    compute.wait_event(saved[1 - k])  # buffers[1 - k] is downloaded, rewrite it
+                calls[k]()
+                consumed[k].record(compute)
+                with torch.cuda.stream(download):
+                    download.wait_event(consumed[k])
+                    out[t].copy_(buffers[1 - k][0], non_blocking=True)
+                    saved[1 - k].record(download)
+            compute.wait_stream(download)
+        final = buffers[ticks % 2]
+        self.state, self.dendritic_state, self.adaptation_state = (x.clone() for x in final)
+        self.last_backend = self._weights()[3]
+        return out
+
+
 class _TickGraph:
     """A CUDA graph of ``ticks`` native ticks ping-ponging between two buffers."""
 
