@@ -12,8 +12,10 @@ stream), B=1, fp32 weights, constant drives 0.2 / 0.1.  A step is one tick.
                 ``NativeDendriticMatrixRuntime.stream`` over 512 ticks, which
                 for every tick copies its drive [B,N] from pinned host memory to
                 the device, runs the tick and copies the new state back to
-                pinned host memory (one single-tick launch per tick; the copies
-                of neighbouring ticks overlap the tick on two copy streams).
+                pinned host memory.  At B = 1 the ticks run in rollout launches
+                of up to 32 ticks (each tick reads its own drive row and writes
+                its own state row); the copies of neighbouring chunks overlap
+                the running chunk on two copy streams.
 * ``roofline``  HBM roofline of the tick kernel: algorithmic bytes
                 M*(w+4) + 4*(N+1) + 24*B*N per tick over the measured tick
                 time, against MEASURED_PEAKS.json's hbm_gbs.  The tiled layout

@@ -45,7 +45,7 @@ extern "C" {
 #define NSB_API
 #endif
 
-#define NSB_ABI_VERSION 8
+#define NSB_ABI_VERSION 9
 
 enum nsb_status {
   NSB_OK = 0,
@@ -276,6 +276,22 @@ NSB_API int nsb_dendritic_step_tiled(const nsb_tick* tick, const nsb_tiled_layou
 NSB_API int nsb_dendritic_run_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
                                     int64_t ticks, const nsb_tick_out* out, void* workspace,
                                     size_t workspace_bytes, int* status, void* stream);
+
+/* A rollout: `ticks` (>= 1) matrix ticks at B = 1 in ONE cooperative launch,
+ * each tick with its own soma drive and its soma state kept (no counterpart in
+ * the reference, whose rollouts call the tick once per step: simulate.py:105-107
+ * over native_compartmental.py:102-129).  Tick k reads
+ * the drive view tick->drive moved on by k * drive_tick_stride floats (0: the
+ * same drive every tick; a scalar drive ignores it) and, if `history` is not
+ * NULL, writes its new soma state to history[k * history_tick_stride + n]
+ * (history_tick_stride >= N).  Otherwise as nsb_dendritic_run_tiled: `out`
+ * holds the state after the last tick, which equals `ticks` calls of
+ * nsb_dendritic_step_tiled with those drives, bit for bit. */
+NSB_API int nsb_dendritic_rollout_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
+                                        int64_t ticks, int64_t drive_tick_stride,
+                                        float* history, int64_t history_tick_stride,
+                                        const nsb_tick_out* out, void* workspace,
+                                        size_t workspace_bytes, int* status, void* stream);
 
 /* Small graphs: `ticks` (>= 1) matrix ticks at B = 1 on ONE thread-block
  * cluster of 8 CTAs (no counterpart in the reference).  Every CTA keeps the

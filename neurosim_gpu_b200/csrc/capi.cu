@@ -240,6 +240,7 @@ int check_tiled_tick(const nsb_tick* tick, const nsb_tiled_layout* layout, const
                      nsb::TickArgs* t, nsb::TickOut* o) {
   if (!check_tick(tick, t)) return NSB_ERR_ARGUMENT;
   if (t->batch != 1) return fail(NSB_ERR_ARGUMENT, "the tiled tick takes B = 1");
+  t->u.sb = 0;  // the kernel reads the drive of tick k at batch index k
   if (!*source) {
     if (t->s.sn != 1)
       return fail(NSB_ERR_ARGUMENT, "the tiled tick needs a contiguous, 16-byte aligned state");
@@ -301,6 +302,35 @@ int nsb_dendritic_run_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout
                                             nsb::Out{nullptr, 0, 0}, workspace, status,
                                             static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_run_tiled launch");
+  return NSB_OK;
+}
+
+int nsb_dendritic_rollout_tiled(const nsb_tick* tick, const nsb_tiled_layout* layout,
+                                int64_t ticks, int64_t drive_tick_stride, float* history,
+                                int64_t history_tick_stride, const nsb_tick_out* out,
+                                void* workspace, size_t workspace_bytes, int* status,
+                                void* stream) {
+  if (ticks < 1 || ticks > (int64_t{1} << 24))
+    return fail(NSB_ERR_ARGUMENT, "ticks must be in [1, 2^24]");
+  if (drive_tick_stride < 0 || drive_tick_stride > (int64_t{1} << 40))
+    return fail(NSB_ERR_ARGUMENT, "drive_tick_stride must be in [0, 2^40]");
+  nsb::TickArgs t;
+  nsb::TickOut o;
+  const float* source = nullptr;
+  const int code = check_tiled_tick(tick, layout, &source, out, workspace, workspace_bytes, &t, &o);
+  if (code != NSB_OK) return code;
+  if (layout->cols != t.neurons)
+    return fail(NSB_ERR_ARGUMENT, "layout and state sizes differ");
+  if (ticks > 1 && (out->state.neuron_stride != 1 || !aligned(out->state.data, 16)))
+    return fail(NSB_ERR_ARGUMENT, "multi-tick runs need a contiguous, 16-byte aligned state output");
+  if (history && (history_tick_stride < t.neurons || history_tick_stride > (int64_t{1} << 40)))
+    return fail(NSB_ERR_ARGUMENT, "history_tick_stride must be in [neurons, 2^40]");
+  if (t.u.data) t.u.sb = drive_tick_stride;
+  g_error.clear();
+  const cudaError_t err = nsb::launch_tiled(*layout, t, source, true, static_cast<int>(ticks), o,
+                                            nsb::Out{history, history ? history_tick_stride : 0, 1},
+                                            workspace, status, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_rollout_tiled launch");
   return NSB_OK;
 }
 

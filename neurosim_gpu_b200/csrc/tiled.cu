@@ -38,7 +38,8 @@
 //      (sequential, CSR order) is stored to part[block][split][row].
 //   3. grid barrier; every CTA takes rows [c*R/C, (c+1)*R/C), adds their sums
 //      in (block, split) order (clearing part for the next tick), applies the
-//      pointwise update and writes s', d', a'.
+//      pointwise update and writes s', d', a' (and, for a rollout, s' into the
+//      history row of the tick; tick k's drive is read k drive strides on).
 //   4. for the next tick (in place on the outputs): back to 1; the producer
 //      waits at a grid barrier (every CTA's update done) before it stages the
 //      new state, while the consumers already load the next tick's edges.
@@ -674,7 +675,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
             d0[r] = __ldcg(out.d.data + n * out.d.sn);
             a0[r] = __ldcg(out.a.data + n * out.a.sn);
           }
-          u[r] = t.u.at(0, n);
+          u[r] = t.u.at(tick, n);  // batch stride = the drive's tick stride (B = 1)
           v[r] = t.v.at(0, n);
 #pragma unroll
           for (int i = 0; i < 6; ++i) pr[r][i] = t.p.at(i, n);
@@ -707,6 +708,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
           }
           out.d.put(0, n, q.d);
           out.a.put(0, n, q.a);
+          if (product.data) product.put(tick, n, q.s);  // a rollout's soma history
         } else {
           if (G)
             product.data[n * product.sn] += j[r];

@@ -135,7 +135,7 @@ EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_dendritic_event_noalloc", "nsb_dendritic_step_rows",
                     "nsb_cluster_slots", "nsb_cluster_smem_bytes", "nsb_dendritic_run_cluster",
                     "nsb_dendritic_event_rows", "nsb_event_scatter_rows", "nsb_encode_weights",
-                    "nsb_dendritic_event_hybrid",
+                    "nsb_dendritic_event_hybrid", "nsb_dendritic_rollout_tiled",
                     "nsb_last_error", "nsb_abi_version")
 
 
@@ -167,6 +167,10 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_dendritic_run_tiled.argtypes = [p(_Tick), p(_TiledLayout), ctypes.c_int64,
                                             p(_TickOut), ctypes.c_void_p, ctypes.c_size_t,
                                             ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_dendritic_rollout_tiled.argtypes = [p(_Tick), p(_TiledLayout), ctypes.c_int64,
+                                                ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+                                                p(_TickOut), ctypes.c_void_p, ctypes.c_size_t,
+                                                ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_dendritic_run_tiled_peers.argtypes = [p(_Tick), p(_TiledLayout), ctypes.c_int64,
                                                   p(_PeerExchange), p(_TickOut), ctypes.c_void_p,
                                                   ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p]
@@ -205,7 +209,7 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
         getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
-    if lib.nsb_abi_version() != 8:
+    if lib.nsb_abi_version() != 9:
         raise RuntimeError("libneurosim_b200.so ABI version mismatch")
     return lib
 
@@ -396,7 +400,7 @@ class DendriticExtension:
 
     def prepare_step_tiled(self, state, dendrite, adaptation, params, layout, input,
                            input_scalar, dendritic_input, dendritic_scalar, *, out, status=None,
-                           source=None, ticks=None):
+                           source=None, ticks=None, rollout=None):
         """Like :meth:`prepare_step` for B = 1 over a :class:`~neurosim_gpu_b200.tiled.TiledLayout`.
 
         ``source`` (optional) is the full gathered state of ``layout.cols``
@@ -405,6 +409,10 @@ class DendriticExtension:
         (``nsb_dendritic_run_tiled``): the first reads ``state`` / ``dendrite``
         / ``adaptation``, the later ones update ``out`` in place.  The launch
         uses the layout's own workspace (:meth:`TiledLayout.workspace`).
+        ``rollout`` = ``(drive_tick_stride, history)`` gives each of the T ticks
+        its own drive (tick k reads ``input`` moved on by k * drive_tick_stride
+        floats) and, with ``history`` a contiguous [T, 1, N] tensor, keeps every
+        tick's soma state there (``nsb_dendritic_rollout_tiled``).
         """
         _check_state(state)
         _check(state.size(0) == 1, "the tiled tick takes B = 1")
@@ -414,6 +422,15 @@ class DendriticExtension:
                "the tiled tick needs a contiguous, 16-byte aligned state")
         _check(layout.neurons == state.size(1), "layout and state neuron counts differ")
         _check(ticks is None or source is None, "multi-tick runs gather from their own state")
+        drive_stride, history = (0, None) if rollout is None else rollout
+        _check(rollout is None or ticks is not None, "a rollout needs ticks")
+        if history is not None:
+            _float_on(history, state)
+            _check(history.is_contiguous() and history.numel() == ticks * layout.neurons,
+                   "history must be a contiguous [T, 1, N] tensor")
+        if drive_stride and input is not None:
+            _check(input.numel() + (ticks - 1) * drive_stride <= input.untyped_storage().nbytes()
+                   // 4 - input.storage_offset(), "the rollout's drives exceed their storage")
         tick = _tick(state, dendrite, adaptation, params, input, input_scalar,
                      dendritic_input, dendritic_scalar)
         for view in out:
@@ -426,12 +443,18 @@ class DendriticExtension:
         source_ptr = source.data_ptr() if source is not None else None
         lib, device = self.lib, state.device
         keep = (state, dendrite, adaptation, params, layout, input, dendritic_input, out, status,
-                source, workspace)
+                source, workspace, history)
+        history_ptr = history.data_ptr() if history is not None else None
 
         def launch() -> None:
             assert keep is not None
             with torch.cuda.device(device):
-                if ticks is None:
+                if rollout is not None:
+                    code = lib.nsb_dendritic_rollout_tiled(
+                        ctypes.byref(tick), ctypes.byref(c_layout), int(ticks), int(drive_stride),
+                        history_ptr, layout.neurons, ctypes.byref(result), workspace.data_ptr(),
+                        workspace.numel(), status_ptr, _stream(device))
+                elif ticks is None:
                     code = lib.nsb_dendritic_step_tiled(
                         ctypes.byref(tick), ctypes.byref(c_layout), source_ptr,
                         ctypes.byref(result), workspace.data_ptr(), workspace.numel(), status_ptr,

@@ -399,12 +399,17 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         or broadcastable) and its new soma state is copied into ``out[t]``.
 
         ``drives`` and ``out`` ([T, B, N] float32) may live on the host: pinned
-        host memory lets the copies overlap the ticks.  The drive of tick t + 1
-        is uploaded on one CUDA stream and the state of tick t - 1 downloaded on
-        another while tick t runs; every tick's two copies still happen, and
-        ``out`` holds every tick's state when the call returns.  Equal to
-        ``len(drives)`` calls of :meth:`step` with those drives.  Returns
-        ``out`` (allocated pinned if not given).
+        host memory lets the copies overlap the ticks.  On the tiled path (B = 1)
+        the ticks run in rollout launches of up to 32 ticks
+        (``nsb_dendritic_rollout_tiled``: one cooperative launch per chunk, each
+        tick reading its own drive row and writing its own history row); chunk
+        c + 1's drives are uploaded on one CUDA stream and chunk c - 1's states
+        downloaded on another while chunk c runs.  The other paths launch one
+        tick at a time with the same two-stream overlap.  Every tick's drive is
+        copied in and its state copied out; ``out`` holds every tick's state
+        when the call returns.  Equal to ``len(drives)`` calls of :meth:`step`
+        with those drives, bit for bit.  Returns ``out`` (allocated pinned if
+        not given).
         """
         if self._needs_autograd(0.0, dendritic_drive) or drives.requires_grad:
             raise RuntimeError("stream() is inference-only; use step() for autograd")
@@ -420,7 +425,84 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
             raise ValueError("out must be [T, B, N] float32")
         if ticks == 0:
             return out
+        if drives.dim() == 2:
+            drives = drives.unsqueeze(1)  # [T, N]: one drive row per tick
         v, vs = self._drive(dendritic_drive, "dendritic_drive")
+        with torch.inference_mode():
+            if self.kernel_path == "tiled":
+                final = self._stream_rollouts(drives, out, v, vs)
+            else:
+                final = self._stream_ticks(drives, out, v, vs)
+        self.state, self.dendritic_state, self.adaptation_state = final
+        self.last_backend = self._weights()[3]
+        return out
+
+    @staticmethod
+    def _rollout_chunks(ticks: int, cap: int = 32, first: int = 4) -> list[int]:
+        """Chunk lengths of a streamed rollout: 4, 8, 16, then ``cap``-tick chunks,
+        then 16, 8, 4, so that the first upload and the last download are short."""
+        head, size = [], first
+        while size < cap and 2 * (sum(head) + size) <= ticks:
+            head.append(size)
+            size *= 2
+        middle = ticks - 2 * sum(head)
+        body = [cap] * (middle // cap) + ([middle % cap] if middle % cap else [])
+        return head + body + head[::-1]
+
+    def _stream_rollouts(self, drives, out, v, vs):
+        state = self.state
+        device = state.device
+        neurons = state.shape[1]
+        chunks = self._rollout_chunks(drives.shape[0])
+        widest = max(chunks)
+        running = tuple(x.clone() for x in (state, self.dendritic_state, self.adaptation_state))
+        drive_ring = [torch.empty((widest, 1, neurons), device=device) for _ in range(2)]
+        history = [torch.empty((widest, 1, neurons), device=device) for _ in range(2)]
+        calls: dict[tuple[int, int], object] = {}
+
+        def call(k: int, length: int):
+            if (k, length) not in calls:
+                calls[k, length] = self.extension.prepare_step_tiled(
+                    *running, self._parameters(), self._tiled_layout(), drive_ring[k][0], 0.0,
+                    v, vs, out=running, status=self._status, ticks=length,
+                    rollout=(neurons, history[k][:length]))
+            return calls[k, length]
+
+        compute = torch.cuda.current_stream(device)
+        upload = torch.cuda.Stream(device=device)
+        download = torch.cuda.Stream(device=device)
+        uploaded = [torch.cuda.Event() for _ in range(2)]
+        consumed = [torch.cuda.Event() for _ in range(2)]  # rollout done with ring slot k
+        saved = [torch.cuda.Event() for _ in range(2)]     # history[k] downloaded
+        upload.wait_stream(compute)
+        download.wait_stream(compute)
+        lo = 0
+        for c, length in enumerate(chunks):
+            k, hi = c % 2, lo + length
+            with torch.cuda.stream(upload):
+                if c >= 2:
+                    upload.wait_event(consumed[k])
+                drive_ring[k][:length].copy_(drives[lo:hi], non_blocking=True)
+                uploaded[k].record(upload)
+            compute.wait_event(uploaded[k])
+            if c >= 2:
+                compute.wait_event(saved[k])
+            call(k, length)()
+            consumed[k].record(compute)
+            with torch.cuda.stream(download):
+                download.wait_event(consumed[k])
+                out[lo:hi].copy_(history[k][:length], non_blocking=True)
+                saved[k].record(download)
+            lo = hi
+        compute.wait_stream(download)
+        compute.wait_stream(upload)
+        return running
+
+    def _stream_ticks(self, drives, out, v, vs):
+        state = self.state
+        device = state.device
+        batch, neurons = state.shape
+        ticks = drives.shape[0]
         drive_buf = [torch.empty_like(state) for _ in range(2)]
         buffers = [(torch.empty_like(state), torch.empty_like(state), torch.empty_like(state))
                    for _ in range(2)]
@@ -439,28 +521,25 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         saved = [torch.cuda.Event() for _ in range(2)]      # download of buffers[k] finished
         upload.wait_stream(compute)
         download.wait_stream(compute)
-        with torch.inference_mode():
-            for t in range(ticks):
-                k = t % 2
-                with torch.cuda.stream(upload):
-                    if t >= 2:
-                        upload.wait_event(consumed[k])
-                    drive_buf[k].copy_(drives[t].expand(batch, neurons), non_blocking=True)
-                    uploaded[k].record(upload)
-                compute.wait_event(uploaded[k])
-                if t >= 1:
-                    compute.wait_event(saved[1 - k])  # buffers[1 - k] is downloaded, rewrite it
-                calls[k]()
-                consumed[k].record(compute)
-                with torch.cuda.stream(download):
-                    download.wait_event(consumed[k])
-                    out[t].copy_(buffers[1 - k][0], non_blocking=True)
-                    saved[1 - k].record(download)
-            compute.wait_stream(download)
-        final = buffers[ticks % 2]
-        self.state, self.dendritic_state, self.adaptation_state = (x.clone() for x in final)
-        self.last_backend = self._weights()[3]
-        return out
+        for t in range(ticks):
+            k = t % 2
+            with torch.cuda.stream(upload):
+                if t >= 2:
+                    upload.wait_event(consumed[k])
+                drive_buf[k].copy_(drives[t].expand(batch, neurons), non_blocking=True)
+                uploaded[k].record(upload)
+            compute.wait_event(uploaded[k])
+            if t >= 1:
+                compute.wait_event(saved[1 - k])  # buffers[1 - k] is downloaded, rewrite it
+            calls[k]()
+            consumed[k].record(compute)
+            with torch.cuda.stream(download):
+                download.wait_event(consumed[k])
+                out[t].copy_(buffers[1 - k][0], non_blocking=True)
+                saved[1 - k].record(download)
+        compute.wait_stream(download)
+        compute.wait_stream(upload)
+        return tuple(x.clone() for x in buffers[ticks % 2])
 
 
 class _TickGraph:

@@ -139,3 +139,16 @@ def test_hybrid_event_rejects_bad_arguments(lib):
                                             None, 0, None, 1, None, None, None, 0, None, None)
     assert status != 0
     assert b"current" in lib.nsb_last_error() or b"required" in lib.nsb_last_error()
+
+
+def test_rollout_rejects_bad_ticks_and_strides(lib):
+    tick = _tick(batch=1)
+    status = lib.nsb_dendritic_rollout_tiled(ctypes.byref(tick), None, 0, 0, None, 0, None,
+                                             None, 0, None, None)
+    assert status == -1 and b"ticks" in lib.nsb_last_error()
+    status = lib.nsb_dendritic_rollout_tiled(ctypes.byref(tick), None, 4, -1, None, 0, None,
+                                             None, 0, None, None)
+    assert status == -1 and b"drive_tick_stride" in lib.nsb_last_error()
+    status = lib.nsb_dendritic_rollout_tiled(ctypes.byref(tick), None, 4, 8, None, 0, None,
+                                             None, 0, None, None)
+    assert status != 0  # no layout

@@ -331,26 +331,32 @@ def test_config4_1000_ticks_against_oracle(ext):
     assert_same_as(native, reference, atol=1e-5, rtol=0)
 
 
-@pytest.mark.parametrize("kernel,batch,n,m", [("tiled", 1, 6000, 150000), ("cluster", 1, 1000, 20000),
-                                              ("csr", 2, 3000, 60000)])
-def test_stream_equals_steps_with_the_same_drives(ext, kernel, batch, n, m):
+@pytest.mark.parametrize("kernel,batch,n,m,ticks", [
+    ("tiled", 1, 6000, 150000, 9), ("tiled", 1, 6000, 150000, 70), ("cluster", 1, 1000, 20000, 9),
+    ("csr", 2, 3000, 60000, 9)])
+def test_stream_equals_steps_with_the_same_drives(ext, kernel, batch, n, m, ticks):
     """stream(): host drives in, every tick's state out, copies overlapping the
-    ticks; equal bit for bit to step() with the same drives."""
+    ticks (tiled: rollout launches of 4, 8, 16, ... ticks); equal bit for bit
+    to step() with the same drives."""
     graph = random_topology(n, m, device="cpu", seed=5).to("cuda")
     model = bench_model(n)
     initial = torch.rand(batch, n, generator=torch.Generator().manual_seed(1)).cuda()
-    drives = (torch.rand(9, batch, n, generator=torch.Generator().manual_seed(2)) * 0.4).pin_memory()
+    drives = torch.rand(ticks, batch, n, generator=torch.Generator().manual_seed(2)) * 0.4
+    if ticks > 9:
+        drives = drives[:, 0]  # [T, N] drives, one row per tick
+    drives = drives.pin_memory()
     stepped = NativeDendriticMatrixRuntime(graph, model, initial.clone(), kernel=kernel)
     streamed = NativeDendriticMatrixRuntime(graph, model, initial.clone(), kernel=kernel)
     assert streamed.kernel_path == kernel
     states = []
     with torch.inference_mode():
-        for t in range(9):
+        for t in range(ticks):
             states.append(stepped.step(drives[t].cuda(), dendritic_drive=0.1).clone())
         out = streamed.stream(drives, dendritic_drive=0.1)
     torch.cuda.synchronize()
     assert out.device.type == "cpu" and out.is_pinned()
-    for t in range(9):
+    for t in range(ticks):
         assert torch.equal(out[t], states[t].cpu()), t
+    streamed.check_status()
     for name in ("state", "dendritic_state", "adaptation_state"):
         assert torch.equal(getattr(streamed, name), getattr(stepped, name)), name

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 import oracle
-from _util import OracleMatrix, assert_same_as, bench_model, csr_of, make, npy
+from _util import OracleMatrix, assert_same_as, bench_model, csr_of, make, npy, params_of
 from neurosim_gpu_b200 import (NativeDendriticMatrixRuntime, encode_sparse_weights,
                                load_native_extension, quantize_dequantize, random_topology)
 from neurosim_gpu_b200 import native
@@ -143,6 +143,62 @@ def test_multi_tick_run_equals_single_ticks_bitwise(fmt):
         assert torch.equal(got, want)
     assert int(status.item()) == 0
     assert int(layout.workspace()[256:].count_nonzero().item()) == 0  # row sums left cleared
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["fp32", "fp8"])
+def test_rollout_per_tick_drives_and_history_match_single_ticks_and_oracle(fmt):
+    """nsb_dendritic_rollout_tiled: tick k reads drive row k and writes history
+    row k; bit-equal to single ticks with those drives, and to the oracle."""
+    ext = load_native_extension()
+    n, ticks = 6000, 13
+    graph = random_topology(n, 150000, device="cpu", seed=12).to("cuda")
+    weight, scales, scale, decoded = _packed(graph, fmt)
+    layout = build_tiled_layout(graph.in_rowptr, graph.in_col, weight, neurons=n, ctas=24,
+                                smem_limit=12000, block_scales=scales, global_scale=scale)
+    model = bench_model(n)
+    gen = torch.Generator().manual_seed(4)
+    s0 = torch.rand(1, n, generator=gen).cuda()
+    d0 = (torch.rand(1, n, generator=gen) - 0.5).cuda()
+    a0 = torch.rand(1, n, generator=gen).cuda()
+    # Drive rows 5 floats apart in a wider buffer: the tick stride is not N.
+    stride = n + 5
+    drives = (torch.rand(ticks * stride, generator=gen) * 0.4).cuda()
+    drive_row = [drives[k * stride: k * stride + n].view(1, n) for k in range(ticks)]
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s, d, a = s0, d0, a0
+    singles = []
+    for k in range(ticks):
+        s, d, a = ext.dendritic_step_tiled(s, d, a, model.parameters(), layout, drive_row[k], 0.0,
+                                           None, 0.1, status=status)
+        singles.append(s)
+    out = [torch.empty_like(s0) for _ in range(3)]
+    history = torch.full((ticks, 1, n), float("nan"), device="cuda")
+    ext.prepare_step_tiled(s0, d0, a0, model.parameters(), layout, drive_row[0], 0.0, None, 0.1,
+                           out=out, status=status, ticks=ticks, rollout=(stride, history))()
+    torch.cuda.synchronize()
+    for got, want in zip(out, (s, d, a)):
+        assert torch.equal(got, want)
+    for k in range(ticks):
+        assert torch.equal(history[k], singles[k]), k
+    assert int(status.item()) == 0
+    # Against the oracle on the decoded weights.
+    csr, params = csr_of(graph, decoded), params_of(model)
+    os_, od, oa = npy(s0), npy(d0), npy(a0)
+    for k in range(ticks):
+        os_, od, oa = oracle.matrix_tick(csr, os_, od, oa, params, npy(drive_row[k]),
+                                         np.full_like(os_, 0.1))
+        np.testing.assert_allclose(npy(history[k]), os_, atol=1e-5, rtol=0)
+    # Without a history and with a zero drive stride it is the plain multi-tick run.
+    plain = [torch.empty_like(s0) for _ in range(3)]
+    ext.prepare_step_tiled(s0, d0, a0, model.parameters(), layout, drive_row[0], 0.0, None, 0.1,
+                           out=plain, status=status, ticks=5)()
+    rolled = [torch.empty_like(s0) for _ in range(3)]
+    ext.prepare_step_tiled(s0, d0, a0, model.parameters(), layout, drive_row[0], 0.0, None, 0.1,
+                           out=rolled, status=status, ticks=5, rollout=(0, None))()
+    torch.cuda.synchronize()
+    for got, want in zip(rolled, plain):
+        assert torch.equal(got, want)
 
 
 @pytest.mark.gpu
