@@ -29,7 +29,10 @@ is Python/PyTorch-CPU and cannot run on the GPU box; its arithmetic is the
 oracle's).
 
 ``--gpus N`` (under torchrun, one rank per GPU) row-shards the graph over the
-ranks and all-gathers the soma vector every tick (NCCL).  With the default
+ranks; the soma vector is exchanged every tick by peer stores inside the tick
+kernel over NVLink (B = 1, the tiled path), else by an NCCL all-gather.  Its
+``e2e`` goes through ``ShardedDendriticMatrixRuntime.stream`` (every rank
+uploads its rows' drive and downloads its rows' state every tick).  With the default
 workload the graph grows with N -- N*166,000 neurons and N*25M candidate
 edges, i.e. a fixed 166k-row, ~25M-edge share per GPU ("scaling": "weak"; at
 N = 8 this is the 1.33M / 200M graph).  An explicit ``--workload`` is split
@@ -538,23 +541,17 @@ def run_sharded(args, explicit_workload: bool) -> dict:
         if sampler:
             sampler.__exit__(None, None, None)
         tick_ms = total_ms / steps
-        # End to end through the public step(): per step every rank copies its rows'
-        # drive in from pinned host memory and its rows' new state back out.
+        # End to end through the public stream(): every step, every rank copies its
+        # rows' drive in from pinned host memory and its rows' new state back out
+        # (peer exchange: rollout launches of up to 32 ticks, the copies overlapping
+        # them; NCCL exchange: one step() per tick).
         rows = runtime.shard.rows
-        host_drive = torch.full((batch, rows), 0.2).pin_memory()
-        host_state = torch.empty((batch, rows)).pin_memory()
-        dev_drive = torch.zeros((batch, neurons), device=device)
-        lo, hi = runtime.shard.lo, runtime.shard.hi
         e2e_steps = min(steps, 512)
-
-        def e2e():
-            for _ in range(e2e_steps):
-                dev_drive[:, lo:hi].copy_(host_drive, non_blocking=True)
-                runtime.step(dev_drive, dendritic_drive=0.1)
-                host_state.copy_(runtime.shard.own(runtime.shard.current), non_blocking=True)
-
-        e2e()
-        e2e_ms = timed(e2e) / e2e_steps
+        host_drives = torch.full((e2e_steps, batch, rows), 0.2).pin_memory()
+        host_states = torch.empty((e2e_steps, batch, rows)).pin_memory()
+        runtime.stream(host_drives[:8], host_states[:8], dendritic_drive=0.1)
+        e2e_ms = timed(lambda: runtime.stream(host_drives, host_states,
+                                              dendritic_drive=0.1)) / e2e_steps
     runtime.check_status()
     layout = runtime.layout
     local_algo = algorithmic_bytes(rows, runtime.local_edges, batch, precision)
@@ -580,7 +577,8 @@ def run_sharded(args, explicit_workload: bool) -> dict:
                      "kernel": "tiled_tick_kernel" if layout is not None else "csr_tick_kernel"},
         "e2e": {"value": m * batch / (e2e_ms * 1e-3), "unit": "synapse-updates/s",
                 "h2d_bytes_per_step": 4 * batch * neurons, "d2h_bytes_per_step": 4 * batch * neurons,
-                "ms_per_step": e2e_ms},
+                "ms_per_step": e2e_ms, "api": "ShardedDendriticMatrixRuntime.stream",
+                "steps": e2e_steps},
         "gpu_launches": world if runtime.exchange == "peer" else steps * world,
         "clocks": sampler.summary() if sampler else None,
     }

@@ -45,7 +45,7 @@ extern "C" {
 #define NSB_API
 #endif
 
-#define NSB_ABI_VERSION 9
+#define NSB_ABI_VERSION 10
 
 enum nsb_status {
   NSB_OK = 0,
@@ -352,6 +352,20 @@ NSB_API int nsb_dendritic_run_tiled_peers(const nsb_tick* tick, const nsb_tiled_
                                           int64_t ticks, const nsb_peer_exchange* exchange,
                                           const nsb_tick_out* out, void* workspace,
                                           size_t workspace_bytes, int* status, void* stream);
+
+/* nsb_dendritic_run_tiled_peers as a rollout (see nsb_dendritic_rollout_tiled):
+ * tick k reads this rank's rows' drive tick->drive moved on by
+ * k * drive_tick_stride floats and, if `history` is not NULL, writes the new
+ * soma state of this rank's rows to history[k * history_tick_stride + row]
+ * (history_tick_stride >= layout->rows).  Same exchange, barrier and epoch
+ * rules; no counterpart in the reference. */
+NSB_API int nsb_dendritic_rollout_tiled_peers(const nsb_tick* tick,
+                                              const nsb_tiled_layout* layout, int64_t ticks,
+                                              int64_t drive_tick_stride, float* history,
+                                              int64_t history_tick_stride,
+                                              const nsb_peer_exchange* exchange,
+                                              const nsb_tick_out* out, void* workspace,
+                                              size_t workspace_bytes, int* status, void* stream);
 
 /* CUDA IPC for the peer exchange: export a device pointer of this process as a
  * 64-byte handle plus the pointer's offset in its allocation, and import such

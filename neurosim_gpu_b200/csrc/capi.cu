@@ -334,12 +334,17 @@ int nsb_dendritic_rollout_tiled(const nsb_tick* tick, const nsb_tiled_layout* la
   return NSB_OK;
 }
 
-int nsb_dendritic_run_tiled_peers(const nsb_tick* tick, const nsb_tiled_layout* layout,
-                                  int64_t ticks, const nsb_peer_exchange* x,
-                                  const nsb_tick_out* out, void* workspace,
-                                  size_t workspace_bytes, int* status, void* stream) {
+namespace {
+
+// The checks and the launch shared by the two peer-exchange entry points.
+int run_tiled_peers(const nsb_tick* tick, const nsb_tiled_layout* layout, int64_t ticks,
+                    int64_t drive_tick_stride, float* history, int64_t history_tick_stride,
+                    const nsb_peer_exchange* x, const nsb_tick_out* out, void* workspace,
+                    size_t workspace_bytes, int* status, void* stream, const char* name) {
   if (ticks < 1 || ticks > (int64_t{1} << 24))
     return fail(NSB_ERR_ARGUMENT, "ticks must be in [1, 2^24]");
+  if (drive_tick_stride < 0 || drive_tick_stride > (int64_t{1} << 40))
+    return fail(NSB_ERR_ARGUMENT, "drive_tick_stride must be in [0, 2^40]");
   if (!x || x->world < 1 || x->world > NSB_MAX_PEERS || x->rank < 0 || x->rank >= x->world)
     return fail(NSB_ERR_ARGUMENT, "invalid peer exchange: world / rank");
   for (int p = 0; p < x->world; ++p)
@@ -354,12 +359,35 @@ int nsb_dendritic_run_tiled_peers(const nsb_tick* tick, const nsb_tiled_layout* 
   if (code != NSB_OK) return code;
   if (x->row_offset < 0 || x->row_offset + layout->rows > layout->cols)
     return fail(NSB_ERR_ARGUMENT, "invalid peer exchange: rows outside the gathered state");
+  if (history && (history_tick_stride < t.neurons || history_tick_stride > (int64_t{1} << 40)))
+    return fail(NSB_ERR_ARGUMENT, "history_tick_stride must be in [rows, 2^40]");
+  if (t.u.data) t.u.sb = drive_tick_stride;
   g_error.clear();
   const cudaError_t err = nsb::launch_tiled(*layout, t, source, true, static_cast<int>(ticks), o,
-                                            nsb::Out{nullptr, 0, 0}, workspace, status,
-                                            static_cast<cudaStream_t>(stream), x);
-  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_run_tiled_peers launch");
+                                            nsb::Out{history, history ? history_tick_stride : 0, 1},
+                                            workspace, status, static_cast<cudaStream_t>(stream), x);
+  if (err != cudaSuccess) return cuda_fail(err, name);
   return NSB_OK;
+}
+
+}  // namespace
+
+int nsb_dendritic_run_tiled_peers(const nsb_tick* tick, const nsb_tiled_layout* layout,
+                                  int64_t ticks, const nsb_peer_exchange* x,
+                                  const nsb_tick_out* out, void* workspace,
+                                  size_t workspace_bytes, int* status, void* stream) {
+  return run_tiled_peers(tick, layout, ticks, 0, nullptr, 0, x, out, workspace, workspace_bytes,
+                         status, stream, "nsb_dendritic_run_tiled_peers launch");
+}
+
+int nsb_dendritic_rollout_tiled_peers(const nsb_tick* tick, const nsb_tiled_layout* layout,
+                                      int64_t ticks, int64_t drive_tick_stride, float* history,
+                                      int64_t history_tick_stride, const nsb_peer_exchange* x,
+                                      const nsb_tick_out* out, void* workspace,
+                                      size_t workspace_bytes, int* status, void* stream) {
+  return run_tiled_peers(tick, layout, ticks, drive_tick_stride, history, history_tick_stride, x,
+                         out, workspace, workspace_bytes, status, stream,
+                         "nsb_dendritic_rollout_tiled_peers launch");
 }
 
 int64_t nsb_cluster_slots(int64_t neurons, const int32_t* host_rowptr) {

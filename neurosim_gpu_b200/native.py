@@ -136,6 +136,7 @@ EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_cluster_slots", "nsb_cluster_smem_bytes", "nsb_dendritic_run_cluster",
                     "nsb_dendritic_event_rows", "nsb_event_scatter_rows", "nsb_encode_weights",
                     "nsb_dendritic_event_hybrid", "nsb_dendritic_rollout_tiled",
+                    "nsb_dendritic_rollout_tiled_peers",
                     "nsb_last_error", "nsb_abi_version")
 
 
@@ -171,6 +172,10 @@ def load_library() -> ctypes.CDLL:
                                                 ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
                                                 p(_TickOut), ctypes.c_void_p, ctypes.c_size_t,
                                                 ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_dendritic_rollout_tiled_peers.argtypes = [
+        p(_Tick), p(_TiledLayout), ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+        ctypes.c_int64, p(_PeerExchange), p(_TickOut), ctypes.c_void_p, ctypes.c_size_t,
+        ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_dendritic_run_tiled_peers.argtypes = [p(_Tick), p(_TiledLayout), ctypes.c_int64,
                                                   p(_PeerExchange), p(_TickOut), ctypes.c_void_p,
                                                   ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p]
@@ -209,7 +214,7 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
         getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
-    if lib.nsb_abi_version() != 9:
+    if lib.nsb_abi_version() != 10:
         raise RuntimeError("libneurosim_b200.so ABI version mismatch")
     return lib
 
@@ -620,12 +625,16 @@ class DendriticExtension:
 
     def prepare_run_tiled_peers(self, state, dendrite, adaptation, params, layout, input,
                                 input_scalar, dendritic_input, dendritic_scalar, *, out, ticks,
-                                exchange, status=None):
+                                exchange, status=None, rollout=None):
         """A launch callable for ``ticks`` row-sharded ticks with the exchange in the kernel.
 
         ``exchange`` is a :class:`_PeerExchange` (see ``nsb_dendritic_run_tiled_peers``);
         ``state`` is this rank's rows of the current gathered buffer, ``out`` the
         rows' dendrite / adaptation outputs (``out[0]`` is not written).
+        ``rollout`` = ``(drive_tick_stride, history)``: tick k reads ``input``
+        moved on by k * drive_tick_stride floats and writes the rows' new soma
+        state into ``history[k]`` (a contiguous [T, 1, rows] tensor, or None)
+        (``nsb_dendritic_rollout_tiled_peers``).
         """
         _check_state(state)
         _check(state.size(0) == 1, "the tiled tick takes B = 1")
@@ -640,16 +649,32 @@ class DendriticExtension:
         workspace = layout.workspace()
         status_ptr = status.data_ptr() if status is not None else None
         lib, device = self.lib, state.device
+        drive_stride, history = (0, None) if rollout is None else rollout
+        if history is not None:
+            _float_on(history, state)
+            _check(history.is_contiguous() and history.numel() == ticks * layout.neurons,
+                   "history must be a contiguous [T, 1, rows] tensor")
+        if drive_stride and input is not None:
+            _check(input.numel() + (ticks - 1) * drive_stride <= input.untyped_storage().nbytes()
+                   // 4 - input.storage_offset(), "the rollout's drives exceed their storage")
+        history_ptr = history.data_ptr() if history is not None else None
         keep = (state, dendrite, adaptation, params, layout, input, dendritic_input, out, status,
-                workspace, exchange)
+                workspace, exchange, history)
 
         def launch() -> None:
             assert keep is not None
             with torch.cuda.device(device):
-                code = lib.nsb_dendritic_run_tiled_peers(
-                    ctypes.byref(tick), ctypes.byref(c_layout), int(ticks), ctypes.byref(exchange),
-                    ctypes.byref(result), workspace.data_ptr(), workspace.numel(), status_ptr,
-                    _stream(device))
+                if rollout is None:
+                    code = lib.nsb_dendritic_run_tiled_peers(
+                        ctypes.byref(tick), ctypes.byref(c_layout), int(ticks),
+                        ctypes.byref(exchange), ctypes.byref(result), workspace.data_ptr(),
+                        workspace.numel(), status_ptr, _stream(device))
+                else:
+                    code = lib.nsb_dendritic_rollout_tiled_peers(
+                        ctypes.byref(tick), ctypes.byref(c_layout), int(ticks), int(drive_stride),
+                        history_ptr, layout.neurons, ctypes.byref(exchange),
+                        ctypes.byref(result), workspace.data_ptr(), workspace.numel(),
+                        status_ptr, _stream(device))
             _raise_on_status(lib, code)
 
         return launch

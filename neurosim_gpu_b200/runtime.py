@@ -437,23 +437,11 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         self.last_backend = self._weights()[3]
         return out
 
-    @staticmethod
-    def _rollout_chunks(ticks: int, cap: int = 32, first: int = 4) -> list[int]:
-        """Chunk lengths of a streamed rollout: 4, 8, 16, then ``cap``-tick chunks,
-        then 16, 8, 4, so that the first upload and the last download are short."""
-        head, size = [], first
-        while size < cap and 2 * (sum(head) + size) <= ticks:
-            head.append(size)
-            size *= 2
-        middle = ticks - 2 * sum(head)
-        body = [cap] * (middle // cap) + ([middle % cap] if middle % cap else [])
-        return head + body + head[::-1]
-
     def _stream_rollouts(self, drives, out, v, vs):
         state = self.state
         device = state.device
         neurons = state.shape[1]
-        chunks = self._rollout_chunks(drives.shape[0])
+        chunks = _tiled.rollout_chunks(drives.shape[0])
         widest = max(chunks)
         running = tuple(x.clone() for x in (state, self.dendritic_state, self.adaptation_state))
         drive_ring = [torch.empty((widest, 1, neurons), device=device) for _ in range(2)]

@@ -330,6 +330,100 @@ class ShardedDendriticMatrixRuntime:
         self._tick += ticks
         return self.state
 
+    def stream(self, drives: torch.Tensor, out: torch.Tensor | None = None, *,
+               dendritic_drive=0.0) -> torch.Tensor:
+        """Advance ``len(drives)`` ticks (every rank calls it with the same count);
+        tick t drives THIS rank's rows with ``drives[t]`` and copies the rows' new
+        soma state into ``out[t]``.
+
+        ``drives`` is [T, rows] or [T, B, rows] (the rank's rows only) and ``out``
+        [T, B, rows], on the host (pinned, so the copies overlap the ticks) or on
+        the device.  With the peer exchange (B = 1) the ticks run in rollout
+        launches of up to 32 ticks per rank (``nsb_dendritic_rollout_tiled_peers``:
+        tick k reads drive row k and writes history row k); the next launch's
+        drives are uploaded and the previous launch's states downloaded on two
+        copy streams while a launch runs.  Otherwise every tick is a
+        :meth:`step` with its drive copied in and the rows' state copied out.
+        Equal to ``len(drives)`` calls of :meth:`step` with those drives on the
+        rows.  Returns ``out`` (allocated pinned if not given and ``drives`` is on
+        the host).
+        """
+        ticks = drives.shape[0]
+        rows, batch = self.shard.rows, self.batch
+        if drives.dim() == 2:
+            drives = drives.unsqueeze(1)
+        if drives.dim() != 3 or drives.shape[-1] != rows or drives.shape[1] not in (1, batch):
+            raise ValueError("drives must be [T, rows] or [T, B, rows] (this rank's rows)")
+        if out is None:
+            on_host = drives.device.type == "cpu"
+            out = torch.empty((ticks, batch, rows), pin_memory=on_host,
+                              device="cpu" if on_host else drives.device)
+        if tuple(out.shape) != (ticks, batch, rows) or out.dtype != torch.float32:
+            raise ValueError("out must be [T, B, rows] float32")
+        if ticks == 0:
+            return out
+        with torch.inference_mode():
+            if self._peer is not None:
+                self._stream_peer(drives, out, dendritic_drive)
+            else:
+                device = self.shard.device
+                drive = torch.zeros((batch, self.neurons), device=device)
+                lo, hi = self.shard.lo, self.shard.hi
+                for t in range(ticks):
+                    drive[:, lo:hi].copy_(drives[t], non_blocking=True)
+                    self.step(drive, dendritic_drive=dendritic_drive)
+                    out[t].copy_(self.shard.own(self.shard.current), non_blocking=True)
+        return out
+
+    def _stream_peer(self, drives, out, dendritic_drive) -> None:
+        device = self.shard.device
+        rows = self.shard.rows
+        _, _, v, vs = self._drives(0.0, dendritic_drive)
+        # As in _run_peer: earlier NCCL exchanges end on every rank first.
+        torch.cuda.current_stream(device).synchronize()
+        dist.barrier(group=self.group)
+        chunks = _tiled.rollout_chunks(drives.shape[0])
+        widest = max(chunks)
+        d, a = self.dendritic_state.clone(), self.adaptation_state.clone()
+        drive_ring = [torch.empty((widest, 1, rows), device=device) for _ in range(2)]
+        history = [torch.empty((widest, 1, rows), device=device) for _ in range(2)]
+        compute = torch.cuda.current_stream(device)
+        upload = torch.cuda.Stream(device=device)
+        download = torch.cuda.Stream(device=device)
+        uploaded = [torch.cuda.Event() for _ in range(2)]
+        consumed = [torch.cuda.Event() for _ in range(2)]  # launch done with ring slot k
+        saved = [torch.cuda.Event() for _ in range(2)]     # history[k] downloaded
+        upload.wait_stream(compute)
+        download.wait_stream(compute)
+        lo = 0
+        for c, length in enumerate(chunks):
+            k, hi = c % 2, lo + length
+            with torch.cuda.stream(upload):
+                if c >= 2:
+                    upload.wait_event(consumed[k])
+                drive_ring[k][:length].copy_(drives[lo:hi], non_blocking=True)
+                uploaded[k].record(upload)
+            compute.wait_event(uploaded[k])
+            if c >= 2:
+                compute.wait_event(saved[k])
+            s_rows = self.shard.own(self.shard.current)
+            self.extension.prepare_run_tiled_peers(
+                s_rows, d, a, self.params, self.layout, drive_ring[k][0], 0.0, v, vs,
+                out=(s_rows, d, a), ticks=length, exchange=self._exchange(), status=self.status,
+                rollout=(rows, history[k][:length]))()
+            self.shard.current = (self.shard.current + length) % 2
+            self._peer_epoch += length
+            self._tick += length
+            consumed[k].record(compute)
+            with torch.cuda.stream(download):
+                download.wait_event(consumed[k])
+                out[lo:hi].copy_(history[k][:length], non_blocking=True)
+                saved[k].record(download)
+            lo = hi
+        compute.wait_stream(download)
+        compute.wait_stream(upload)
+        self.dendritic_state, self.adaptation_state = d, a
+
     def _run_graph(self, ticks: int, drive, dendritic_drive, graph_ticks: int) -> torch.Tensor:
         """``ticks`` ticks with fixed drives, replaying a CUDA graph of ticks + all-gathers."""
         graph_ticks = max(2, min(graph_ticks, ticks) // 2 * 2)

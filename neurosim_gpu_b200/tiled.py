@@ -438,3 +438,16 @@ def status_word(device: torch.device) -> torch.Tensor:
 
 __all__ = ["TiledLayout", "build_tiled_layout", "emulate", "plan_blocks", "cta_row_ranges",
            "smem_limit", "sm_count", "status_word", "ctypes"]
+
+
+def rollout_chunks(ticks: int, cap: int = 32, first: int = 4) -> list[int]:
+    """Launch lengths of a streamed rollout of ``ticks`` ticks: 4, 8, 16, then
+    ``cap``-tick launches, then 16, 8, 4, so that the upload before the first
+    launch and the download after the last one are short."""
+    head, size = [], first
+    while size < cap and 2 * (sum(head) + size) <= ticks:
+        head.append(size)
+        size *= 2
+    middle = ticks - 2 * sum(head)
+    body = [cap] * (middle // cap) + ([middle % cap] if middle % cap else [])
+    return head + body + head[::-1]

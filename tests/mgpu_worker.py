@@ -14,6 +14,10 @@ Modes (argv[1]):
            "PELS <exchange>-<theta> <bool> ...".
   pels_timeout  rank 1 stays alive but does not launch; rank 0's scatter must
            end its bounded cross-GPU wait with status code 6: prints "STATUS <code>".
+  stream   sharded stream() (per-tick drives of the rank's rows, every tick's
+           rows copied out) with the peer exchange (rollout launches) and with
+           NCCL, interleaved with run(), against single-GPU steps with the same
+           drives: prints "STREAM <exchange> <bool>".
 """
 
 from __future__ import annotations
@@ -194,6 +198,45 @@ def pels_timeout(device, rank):
     rt.close()
 
 
+def stream(device, rank):
+    n, m = 20011, 500000
+    graph = broadcast_graph(n, m, seed=4, device=device)
+    dyn = model(n, device)
+    init = torch.rand(1, n, generator=torch.Generator().manual_seed(3)).to(device)
+    drives = torch.rand(48, 1, n, generator=torch.Generator().manual_seed(8)) * 0.4
+    topo = random_topology(n, m, device="cpu", seed=4, build_device=device)
+    single = NativeDendriticMatrixRuntime(topo, dyn, init.clone(), kernel="tiled")
+    want = []
+    with torch.inference_mode():
+        for t in range(45):
+            want.append(single.step(drives[t].to(device), dendritic_drive=0.1).clone())
+        for _ in range(5):
+            single.step(0.2, dendritic_drive=0.1)
+        for t in range(45, 48):
+            want.append(single.step(drives[t].to(device), dendritic_drive=0.1).clone())
+    torch.cuda.synchronize()
+    for exchange in ("peer", "nccl"):
+        rt = ShardedDendriticMatrixRuntime(graph, dyn, init, exchange=exchange)
+        lo, hi = rt.shard.lo, rt.shard.hi
+        mine = drives[:, :, lo:hi].contiguous().pin_memory()
+        with torch.inference_mode():
+            first = rt.stream(mine[:45], dendritic_drive=0.1)  # launches of 4, 8, 21, 8, 4 ticks
+            rt.run(5, 0.2, dendritic_drive=0.1, graph_ticks=4)
+            second = rt.stream(mine[45:, 0], dendritic_drive=0.1)  # [T, rows] drives
+        torch.cuda.synchronize()
+        got = torch.cat([first, second])
+        ok = rt.exchange == exchange and all(
+            torch.equal(got[t].to(device), want[t][:, lo:hi]) for t in range(48))
+        ok = ok and torch.equal(rt.state, single.state) and int(rt.status.item()) == 0
+        flag = torch.tensor([int(ok)], device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        rt.release_graphs()
+        rt.close()
+        if rank == 0:
+            print(f"STREAM {exchange} {bool(flag.item())}", flush=True)
+        dist.barrier()
+
+
 def main():
     local = int(os.environ["LOCAL_RANK"])
     device = torch.device("cuda", local)
@@ -201,7 +244,7 @@ def main():
     dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     try:
         {"parity": parity, "timeout": timeout, "checkpoint": checkpoint, "pels": pels,
-         "pels_timeout": pels_timeout}[sys.argv[1]](
+         "pels_timeout": pels_timeout, "stream": stream}[sys.argv[1]](
             device, dist.get_rank())
     finally:
         dist.destroy_process_group()

@@ -152,3 +152,17 @@ def test_rollout_rejects_bad_ticks_and_strides(lib):
     status = lib.nsb_dendritic_rollout_tiled(ctypes.byref(tick), None, 4, 8, None, 0, None,
                                              None, 0, None, None)
     assert status != 0  # no layout
+
+
+def test_peer_rollout_rejects_bad_ticks_strides_and_exchanges(lib):
+    tick = _tick(batch=1)
+    args = (None, None, None, 0, None, None)  # exchange, out, workspace, bytes, status, stream
+    assert lib.nsb_dendritic_rollout_tiled_peers(ctypes.byref(tick), None, 0, 0, None, 0,
+                                                 *args) == -1
+    assert b"ticks" in lib.nsb_last_error()
+    assert lib.nsb_dendritic_rollout_tiled_peers(ctypes.byref(tick), None, 3, -2, None, 0,
+                                                 *args) == -1
+    assert b"drive_tick_stride" in lib.nsb_last_error()
+    assert lib.nsb_dendritic_rollout_tiled_peers(ctypes.byref(tick), None, 3, 4, None, 0,
+                                                 *args) == -1
+    assert b"peer exchange" in lib.nsb_last_error()

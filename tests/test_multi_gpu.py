@@ -85,3 +85,15 @@ def test_missing_rank_ends_the_pels_delta_wait_with_a_status():
     out = _run("pels_timeout")
     codes = [int(line.split()[1]) for line in out.splitlines() if line.startswith("STATUS")]
     assert codes == [6], out
+
+
+@pytest.mark.gpu
+@needs_two
+def test_sharded_stream_rollouts_equal_one_gpu_steps():
+    """ShardedDendriticMatrixRuntime.stream(): rollout launches with the peer
+    exchange, step() per tick with NCCL; every tick's rows equal one GPU's."""
+    out = _run("stream")
+    lines = [line.split() for line in out.splitlines() if line.startswith("STREAM")]
+    assert [case for _, case, _ in lines] == ["peer", "nccl"], out
+    for _, case, ok in lines:
+        assert ok == "True", case
