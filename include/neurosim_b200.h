@@ -45,7 +45,7 @@ extern "C" {
 #define NSB_API
 #endif
 
-#define NSB_ABI_VERSION 10
+#define NSB_ABI_VERSION 11
 
 enum nsb_status {
   NSB_OK = 0,
@@ -313,6 +313,17 @@ NSB_API size_t nsb_cluster_smem_bytes(int64_t neurons, int64_t max_slots);
 NSB_API int nsb_dendritic_run_cluster(const nsb_tick* tick, const nsb_csr* csr, int64_t max_slots,
                                       int64_t ticks, const nsb_tick_out* out, int* status,
                                       void* stream);
+
+/* nsb_dendritic_run_cluster as a rollout (see nsb_dendritic_rollout_tiled; no
+ * counterpart in the reference): tick k reads tick->drive moved on by
+ * k * drive_tick_stride floats (0: the same drive every tick) and, if
+ * `history` is not NULL, writes its new soma state to
+ * history[k * history_tick_stride + n] (history_tick_stride >= N). */
+NSB_API int nsb_dendritic_rollout_cluster(const nsb_tick* tick, const nsb_csr* csr,
+                                          int64_t max_slots, int64_t ticks,
+                                          int64_t drive_tick_stride, float* history,
+                                          int64_t history_tick_stride, const nsb_tick_out* out,
+                                          int* status, void* stream);
 
 /* Up to this many GPUs take part in a peer exchange. */
 #define NSB_MAX_PEERS 8

@@ -402,11 +402,15 @@ size_t nsb_cluster_smem_bytes(int64_t neurons, int64_t max_slots) {
   return nsb::cluster_smem_bytes(neurons, max_slots);
 }
 
-int nsb_dendritic_run_cluster(const nsb_tick* tick, const nsb_csr* csr, int64_t max_slots,
-                              int64_t ticks, const nsb_tick_out* out, int* status,
-                              void* stream) {
+namespace {
+
+int run_cluster(const nsb_tick* tick, const nsb_csr* csr, int64_t max_slots, int64_t ticks,
+                int64_t drive_tick_stride, float* history, int64_t history_tick_stride,
+                const nsb_tick_out* out, int* status, void* stream, const char* name) {
   if (ticks < 1 || ticks > (int64_t{1} << 30))
     return fail(NSB_ERR_ARGUMENT, "ticks must be in [1, 2^30]");
+  if (drive_tick_stride < 0 || drive_tick_stride > (int64_t{1} << 40))
+    return fail(NSB_ERR_ARGUMENT, "drive_tick_stride must be in [0, 2^40]");
   nsb::TickArgs t;
   if (!check_tick(tick, &t)) return NSB_ERR_ARGUMENT;
   if (t.batch != 1) return fail(NSB_ERR_ARGUMENT, "the cluster tick takes B = 1");
@@ -417,6 +421,8 @@ int nsb_dendritic_run_cluster(const nsb_tick* tick, const nsb_csr* csr, int64_t 
     return NSB_ERR_ARGUMENT;
   if (max_slots < 0 || max_slots >= (int64_t{1} << 31))
     return fail(NSB_ERR_ARGUMENT, "max_slots must be in [0, 2^31)");
+  if (history && (history_tick_stride < t.neurons || history_tick_stride > (int64_t{1} << 40)))
+    return fail(NSB_ERR_ARGUMENT, "history_tick_stride must be in [neurons, 2^40]");
   int device = 0, optin = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err == cudaSuccess)
@@ -427,9 +433,28 @@ int nsb_dendritic_run_cluster(const nsb_tick* tick, const nsb_csr* csr, int64_t 
   g_error.clear();
   const nsb::TickOut o{to_out(out->state), to_out(out->dendrite), to_out(out->adaptation)};
   err = nsb::launch_cluster(t, c, max_slots, static_cast<int>(ticks), o, status,
-                            static_cast<cudaStream_t>(stream));
-  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_run_cluster launch");
+                            static_cast<cudaStream_t>(stream), drive_tick_stride,
+                            nsb::Out{history, history ? history_tick_stride : 0, 1});
+  if (err != cudaSuccess) return cuda_fail(err, name);
   return NSB_OK;
+}
+
+}  // namespace
+
+int nsb_dendritic_run_cluster(const nsb_tick* tick, const nsb_csr* csr, int64_t max_slots,
+                              int64_t ticks, const nsb_tick_out* out, int* status,
+                              void* stream) {
+  return run_cluster(tick, csr, max_slots, ticks, 0, nullptr, 0, out, status, stream,
+                     "nsb_dendritic_run_cluster launch");
+}
+
+int nsb_dendritic_rollout_cluster(const nsb_tick* tick, const nsb_csr* csr, int64_t max_slots,
+                                  int64_t ticks, int64_t drive_tick_stride, float* history,
+                                  int64_t history_tick_stride, const nsb_tick_out* out,
+                                  int* status, void* stream) {
+  return run_cluster(tick, csr, max_slots, ticks, drive_tick_stride, history,
+                     history_tick_stride, out, status, stream,
+                     "nsb_dendritic_rollout_cluster launch");
 }
 
 namespace {

@@ -17,7 +17,9 @@
 //   * one cluster barrier per tick (arrive.release / wait.acquire) orders those
 //     stores before the next tick's reads, and all reads of the current buffer
 //     before it is overwritten one tick later.
-// After T ticks each CTA writes its rows' s, d, a to the outputs.
+// After T ticks each CTA writes its rows' s, d, a to the outputs.  A rollout
+// (drive tick stride > 0 or a history) reads tick k's drive from global memory
+// k strides on and writes every tick's new s of its rows to history row k.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -51,7 +53,8 @@ __device__ __forceinline__ int degree(const int32_t* rowptr, int64_t row, int64_
 
 template <typename W>
 __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kClusterThreads, 1)
-cluster_tick_kernel(ClusterArgs A, W weights, TickArgs t, TickOut out, int ticks, int* status) {
+cluster_tick_kernel(ClusterArgs A, W weights, TickArgs t, TickOut out, int ticks, int* status,
+                    Out history) {
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
   const int lane = threadIdx.x & 31;
@@ -156,10 +159,12 @@ cluster_tick_kernel(ClusterArgs A, W weights, TickArgs t, TickOut out, int ticks
           if (k + q < mine) j = fmaf(w[q], x[q], j);
       }
       for (; k < mine; ++k) j = fmaf(ww[base + 32 * k], sc[cc[base + 32 * k]], j);
-      const Update q = advance(j, sc[row0 + r], d[r], a[r], uu[r], vv[r], prm[r], prm[R + r],
+      const float u = t.u.sb ? t.u.at(tick, row0 + r) : uu[r];  // batch stride = tick stride
+      const Update q = advance(j, sc[row0 + r], d[r], a[r], u, vv[r], prm[r], prm[R + r],
                                prm[2 * R + r], prm[3 * R + r], prm[4 * R + r], prm[5 * R + r]);
       d[r] = q.d;
       a[r] = q.a;
+      if (history.data) history.put(tick, row0 + r, q.s);
 #pragma unroll
       for (int peer = 0; peer < kClusterCtas; ++peer)
         cluster.map_shared_rank(next, peer)[row0 + r] = q.s;
@@ -179,12 +184,12 @@ cluster_tick_kernel(ClusterArgs A, W weights, TickArgs t, TickOut out, int ticks
 template <typename W>
 cudaError_t launch_cluster_variant(const ClusterArgs& A, const W& w, const TickArgs& t,
                                    const TickOut& out, int ticks, size_t smem, int* status,
-                                   cudaStream_t stream) {
+                                   const Out& history, cudaStream_t stream) {
   auto kernel = cluster_tick_kernel<W>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return err;
-  kernel<<<kClusterCtas, kClusterThreads, smem, stream>>>(A, w, t, out, ticks, status);
+  kernel<<<kClusterCtas, kClusterThreads, smem, stream>>>(A, w, t, out, ticks, status, history);
   return cudaGetLastError();
 }
 
@@ -218,8 +223,11 @@ size_t cluster_smem_bytes(int64_t neurons, int64_t max_slots) {
   return static_cast<size_t>(head + 2 * n_pad * 4 + R * 11 * 4 + max_slots * 8);
 }
 
-cudaError_t launch_cluster(const TickArgs& t, const Csr& csr, int64_t max_slots, int ticks,
-                           const TickOut& out, int* status, cudaStream_t stream) {
+cudaError_t launch_cluster(const TickArgs& tick, const Csr& csr, int64_t max_slots, int ticks,
+                           const TickOut& out, int* status, cudaStream_t stream,
+                           int64_t drive_tick_stride, const Out& history) {
+  TickArgs t = tick;
+  t.u.sb = t.u.data ? drive_tick_stride : 0;  // B = 1: the batch stride is the tick stride
   const size_t smem = cluster_smem_bytes(t.neurons, max_slots);
   ClusterArgs A;
   A.rowptr = csr.rowptr;
@@ -230,19 +238,19 @@ cudaError_t launch_cluster(const TickArgs& t, const Csr& csr, int64_t max_slots,
   switch (csr.format) {
     case NSB_WEIGHT_F16:
       return launch_cluster_variant(A, WeightsF16{static_cast<const __half*>(csr.weight)}, t, out,
-                                    ticks, smem, status, stream);
+                                    ticks, smem, status, history, stream);
     case NSB_WEIGHT_E4M3:
       return launch_cluster_variant(
           A, WeightsE4M3{static_cast<const uint8_t*>(csr.weight), csr.global_scale}, t, out, ticks,
-          smem, status, stream);
+          smem, status, history, stream);
     case NSB_WEIGHT_NVFP4:
       return launch_cluster_variant(
           A, WeightsNVFP4{static_cast<const uint8_t*>(csr.weight), csr.block_scales,
                           csr.global_scale},
-          t, out, ticks, smem, status, stream);
+          t, out, ticks, smem, status, history, stream);
     default:
       return launch_cluster_variant(A, WeightsF32{static_cast<const float*>(csr.weight)}, t, out,
-                                    ticks, smem, status, stream);
+                                    ticks, smem, status, history, stream);
   }
 }
 

@@ -69,11 +69,14 @@ cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, cons
                          const TiledGate& gate = TiledGate{});
 
 // Small-graph tick on one thread-block cluster (cluster.cu): `ticks` ticks of
-// B = 1 with the state and the edges in the cluster's shared memory.
+// B = 1 with the state and the edges in the cluster's shared memory.  With a
+// nonzero drive_tick_stride tick k reads the drive that many floats on per
+// tick; with a history, tick k's new s goes to history.put(k, n).
 int64_t cluster_slots(int64_t neurons, const int32_t* host_rowptr);
 size_t cluster_smem_bytes(int64_t neurons, int64_t max_slots);
 cudaError_t launch_cluster(const TickArgs& t, const Csr& csr, int64_t max_slots, int ticks,
-                           const TickOut& out, int* status, cudaStream_t stream);
+                           const TickOut& out, int* status, cudaStream_t stream,
+                           int64_t drive_tick_stride = 0, const Out& history = Out{nullptr, 0, 0});
 
 // Row-sharded PELS (pels_rows.cu).  One rank's rows of the event tick.
 struct EventRowsArgs {

@@ -136,7 +136,7 @@ EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_cluster_slots", "nsb_cluster_smem_bytes", "nsb_dendritic_run_cluster",
                     "nsb_dendritic_event_rows", "nsb_event_scatter_rows", "nsb_encode_weights",
                     "nsb_dendritic_event_hybrid", "nsb_dendritic_rollout_tiled",
-                    "nsb_dendritic_rollout_tiled_peers",
+                    "nsb_dendritic_rollout_tiled_peers", "nsb_dendritic_rollout_cluster",
                     "nsb_last_error", "nsb_abi_version")
 
 
@@ -194,6 +194,9 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_cluster_slots.restype = ctypes.c_int64
     lib.nsb_cluster_smem_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
     lib.nsb_cluster_smem_bytes.restype = ctypes.c_size_t
+    lib.nsb_dendritic_rollout_cluster.argtypes = [
+        p(_Tick), p(_Csr), ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+        ctypes.c_int64, p(_TickOut), ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_dendritic_run_cluster.argtypes = [p(_Tick), p(_Csr), ctypes.c_int64, ctypes.c_int64,
                                               p(_TickOut), ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_dendritic_event_rows.argtypes = [p(_Tick), p(_EventRows), ctypes.c_void_p,
@@ -214,7 +217,7 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
         getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
-    if lib.nsb_abi_version() != 10:
+    if lib.nsb_abi_version() != 11:
         raise RuntimeError("libneurosim_b200.so ABI version mismatch")
     return lib
 
@@ -485,12 +488,16 @@ class DendriticExtension:
     def prepare_run_cluster(self, state, dendrite, adaptation, params, rowptr, source, weight,
                             input, input_scalar, dendritic_input, dendritic_scalar,
                             block_scales=None, global_scale=None, *, out, ticks, max_slots,
-                            status=None):
+                            status=None, rollout=None):
         """A launch callable for ``ticks`` B = 1 ticks on one thread-block cluster.
 
         ``max_slots`` comes from :meth:`cluster_plan` of the same ``rowptr``.
         The first tick reads ``state`` / ``dendrite`` / ``adaptation``, the last
-        writes ``out``; nothing else touches global memory in between.
+        writes ``out``; nothing else touches global memory in between, except
+        for a ``rollout`` = ``(drive_tick_stride, history)``: tick k reads
+        ``input`` moved on by k * drive_tick_stride floats and writes its soma
+        state to ``history[k]`` (a contiguous [T, 1, N] tensor, or None)
+        (``nsb_dendritic_rollout_cluster``).
         """
         _check_state(state)
         _check(state.size(0) == 1, "the cluster tick takes B = 1")
@@ -505,15 +512,30 @@ class DendriticExtension:
         result = _TickOut(_out(out[0]), _out(out[1]), _out(out[2]))
         status_ptr = status.data_ptr() if status is not None else None
         lib, device, slots, count = self.lib, state.device, int(max_slots), int(ticks)
+        drive_stride, history = (0, None) if rollout is None else rollout
+        if history is not None:
+            _float_on(history, state)
+            _check(history.is_contiguous() and history.numel() == count * state.size(1),
+                   "history must be a contiguous [T, 1, N] tensor")
+        if drive_stride and input is not None:
+            _check(input.numel() + (count - 1) * drive_stride <= input.untyped_storage().nbytes()
+                   // 4 - input.storage_offset(), "the rollout's drives exceed their storage")
+        history_ptr = history.data_ptr() if history is not None else None
         keep = (state, dendrite, adaptation, params, rowptr, source, weight, input,
-                dendritic_input, block_scales, global_scale, out, status)
+                dendritic_input, block_scales, global_scale, out, status, history)
 
         def launch() -> None:
             assert keep is not None
             with torch.cuda.device(device):
-                code = lib.nsb_dendritic_run_cluster(ctypes.byref(tick), ctypes.byref(csr), slots,
-                                                     count, ctypes.byref(result), status_ptr,
-                                                     _stream(device))
+                if rollout is None:
+                    code = lib.nsb_dendritic_run_cluster(
+                        ctypes.byref(tick), ctypes.byref(csr), slots, count,
+                        ctypes.byref(result), status_ptr, _stream(device))
+                else:
+                    code = lib.nsb_dendritic_rollout_cluster(
+                        ctypes.byref(tick), ctypes.byref(csr), slots, count, int(drive_stride),
+                        history_ptr, state.size(1), ctypes.byref(result), status_ptr,
+                        _stream(device))
             _raise_on_status(lib, code)
 
         return launch

@@ -399,10 +399,11 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         or broadcastable) and its new soma state is copied into ``out[t]``.
 
         ``drives`` and ``out`` ([T, B, N] float32) may live on the host: pinned
-        host memory lets the copies overlap the ticks.  On the tiled path (B = 1)
-        the ticks run in rollout launches of up to 32 ticks
-        (``nsb_dendritic_rollout_tiled``: one cooperative launch per chunk, each
-        tick reading its own drive row and writing its own history row); chunk
+        host memory lets the copies overlap the ticks.  On the tiled and cluster
+        paths (B = 1) the ticks run in rollout launches of up to 32 (tiled) or
+        128 (cluster) ticks (``nsb_dendritic_rollout_tiled`` /
+        ``nsb_dendritic_rollout_cluster``: one launch per chunk, each tick
+        reading its own drive row and writing its own history row); chunk
         c + 1's drives are uploaded on one CUDA stream and chunk c - 1's states
         downloaded on another while chunk c runs.  The other paths launch one
         tick at a time with the same two-stream overlap.  Every tick's drive is
@@ -429,7 +430,7 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
             drives = drives.unsqueeze(1)  # [T, N]: one drive row per tick
         v, vs = self._drive(dendritic_drive, "dendritic_drive")
         with torch.inference_mode():
-            if self.kernel_path == "tiled":
+            if self.kernel_path in ("tiled", "cluster"):
                 final = self._stream_rollouts(drives, out, v, vs)
             else:
                 final = self._stream_ticks(drives, out, v, vs)
@@ -441,7 +442,15 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         state = self.state
         device = state.device
         neurons = state.shape[1]
-        chunks = _tiled.rollout_chunks(drives.shape[0])
+        slots = self._cluster_slots()
+        # A cluster tick takes ~2 us and moves a few KB of copies: uniform
+        # launches of 128 ticks (two prepared launch callables; preparing one
+        # costs more host time than a short launch runs).  The tiled path ramps
+        # 4, 8, 16, 32 so that its first upload (0.7 MB per tick at 166k) is short.
+        if slots is not None:
+            chunks = _tiled.rollout_chunks(drives.shape[0], cap=128, first=128)
+        else:
+            chunks = _tiled.rollout_chunks(drives.shape[0])
         widest = max(chunks)
         running = tuple(x.clone() for x in (state, self.dendritic_state, self.adaptation_state))
         drive_ring = [torch.empty((widest, 1, neurons), device=device) for _ in range(2)]
@@ -449,12 +458,22 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         calls: dict[tuple[int, int], object] = {}
 
         def call(k: int, length: int):
-            if (k, length) not in calls:
-                calls[k, length] = self.extension.prepare_step_tiled(
+            if (k, length) in calls:
+                return calls[k, length]
+            rollout = (neurons, history[k][:length])
+            if slots is not None:
+                weight, scales, scale, _ = self._weights()
+                topology = self.topology
+                launch = self.extension.prepare_run_cluster(
+                    *running, self._parameters(), topology.in_rowptr, topology.in_col, weight,
+                    drive_ring[k][0], 0.0, v, vs, scales, scale, out=running, ticks=length,
+                    max_slots=slots, status=self._status, rollout=rollout)
+            else:
+                launch = self.extension.prepare_step_tiled(
                     *running, self._parameters(), self._tiled_layout(), drive_ring[k][0], 0.0,
-                    v, vs, out=running, status=self._status, ticks=length,
-                    rollout=(neurons, history[k][:length]))
-            return calls[k, length]
+                    v, vs, out=running, status=self._status, ticks=length, rollout=rollout)
+            calls[k, length] = launch
+            return launch
 
         compute = torch.cuda.current_stream(device)
         upload = torch.cuda.Stream(device=device)

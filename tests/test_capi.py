@@ -166,3 +166,13 @@ def test_peer_rollout_rejects_bad_ticks_strides_and_exchanges(lib):
     assert lib.nsb_dendritic_rollout_tiled_peers(ctypes.byref(tick), None, 3, 4, None, 0,
                                                  *args) == -1
     assert b"peer exchange" in lib.nsb_last_error()
+
+
+def test_cluster_rollout_rejects_bad_ticks_and_strides(lib):
+    tick = _tick(batch=1)
+    assert lib.nsb_dendritic_rollout_cluster(ctypes.byref(tick), None, 0, 0, 0, None, 0, None,
+                                             None, None) == -1
+    assert b"ticks" in lib.nsb_last_error()
+    assert lib.nsb_dendritic_rollout_cluster(ctypes.byref(tick), None, 0, 5, -1, None, 0, None,
+                                             None, None) == -1
+    assert b"drive_tick_stride" in lib.nsb_last_error()

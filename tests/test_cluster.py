@@ -198,3 +198,50 @@ def test_runtime_picks_cluster_for_small_graphs(fmt):
         tiled.run(30, 0.2, dendritic_drive=0.1)
     assert tiled.kernel_path == "tiled"
     assert_same_as(ran, tiled, atol=1e-5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["fp32", "nvfp4"])
+def test_cluster_rollout_per_tick_drives_and_history(fmt):
+    """nsb_dendritic_rollout_cluster: tick k reads drive row k (rows 3 floats
+    apart beyond N) and writes history row k; equal to single-tick launches
+    with those drives, and to the oracle."""
+    ext = load_native_extension()
+    n, ticks = 1000, 11
+    graph = random_topology(n, 20000, device="cpu", seed=3).to("cuda")
+    weight, scales, scale, decoded = _packed(graph, fmt)
+    model = bench_model(n)
+    gen = torch.Generator().manual_seed(5)
+    s0 = torch.rand(1, n, generator=gen).cuda()
+    d0 = (torch.rand(1, n, generator=gen) - 0.5).cuda()
+    a0 = torch.rand(1, n, generator=gen).cuda()
+    stride = n + 3
+    drives = (torch.rand(ticks * stride, generator=gen) * 0.4).cuda()
+    row = [drives[k * stride: k * stride + n].view(1, n) for k in range(ticks)]
+    slots, _ = ext.cluster_plan(graph.in_rowptr)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    state = (s0, d0, a0)
+    singles = []
+    for k in range(ticks):
+        nxt = [torch.empty_like(s0) for _ in range(3)]
+        ext.prepare_run_cluster(*state, model.parameters(), graph.in_rowptr, graph.in_col, weight,
+                                row[k], 0.0, None, 0.1, scales, scale, out=nxt, ticks=1,
+                                max_slots=slots, status=status)()
+        state = nxt
+        singles.append(nxt[0])
+    out = [torch.empty_like(s0) for _ in range(3)]
+    history = torch.full((ticks, 1, n), float("nan"), device="cuda")
+    ext.prepare_run_cluster(s0, d0, a0, model.parameters(), graph.in_rowptr, graph.in_col, weight,
+                            row[0], 0.0, None, 0.1, scales, scale, out=out, ticks=ticks,
+                            max_slots=slots, status=status, rollout=(stride, history))()
+    torch.cuda.synchronize()
+    for got, want in zip(out, state):
+        assert torch.equal(got, want)
+    for k in range(ticks):
+        assert torch.equal(history[k], singles[k]), k
+    assert int(status.item()) == 0
+    csr, params = csr_of(graph, decoded), params_of(model)
+    s, d, a = npy(s0), npy(d0), npy(a0)
+    for k in range(ticks):
+        s, d, a = oracle.matrix_tick(csr, s, d, a, params, npy(row[k]), np.full_like(s, 0.1))
+        np.testing.assert_allclose(npy(history[k]), s, atol=1e-5, rtol=0)

@@ -333,11 +333,11 @@ def test_config4_1000_ticks_against_oracle(ext):
 
 @pytest.mark.parametrize("kernel,batch,n,m,ticks", [
     ("tiled", 1, 6000, 150000, 9), ("tiled", 1, 6000, 150000, 70), ("cluster", 1, 1000, 20000, 9),
-    ("csr", 2, 3000, 60000, 9)])
+    ("cluster", 1, 1000, 20000, 300), ("csr", 2, 3000, 60000, 9)])
 def test_stream_equals_steps_with_the_same_drives(ext, kernel, batch, n, m, ticks):
     """stream(): host drives in, every tick's state out, copies overlapping the
-    ticks (tiled: rollout launches of 4, 8, 16, ... ticks); equal bit for bit
-    to step() with the same drives."""
+    ticks (tiled and cluster: rollout launches of 4, 8, 16, ... ticks); equal
+    bit for bit to step() with the same drives."""
     graph = random_topology(n, m, device="cpu", seed=5).to("cuda")
     model = bench_model(n)
     initial = torch.rand(batch, n, generator=torch.Generator().manual_seed(1)).cuda()
