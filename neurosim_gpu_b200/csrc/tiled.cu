@@ -357,8 +357,8 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
 }
 
 // End-of-tick barrier across ranks, for one thread per CTA after a
-// __syncthreads that follows the CTA's peer stores (each storing thread has
-// fenced them at system scope): all CTAs of this rank meet at the local grid
+// __syncthreads that follows the CTA's peer stores and a system-scope fence by
+// that thread: all CTAs of this rank meet at the local grid
 // barrier, CTA 0 then adds one to every rank's counter, and every CTA waits
 // until its rank's counter shows all ranks' arrivals for this tick.  Bounded:
 // on timeout it records code 6.
@@ -718,9 +718,14 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
       }
     }
     if (exchange) {
-      __threadfence_system();  // this thread's peer stores, before the ranks' barrier
+      // Every thread's peer stores of this tick precede the CTA barrier; one
+      // system-scope fence after it (cumulative over the barrier) orders them
+      // all before this CTA's arrival at the ranks' barrier.
       __syncthreads();
-      if (warp == kProducerWarp && lane == 0) peer_barrier(px, L.barrier, tick, st);
+      if (warp == kProducerWarp && lane == 0) {
+        __threadfence_system();
+        peer_barrier(px, L.barrier, tick, st);
+      }
     } else {
       __syncthreads();  // this CTA's update is done (the producer's barrier orders it)
     }
