@@ -21,12 +21,14 @@ stream), B=1, fp32 weights, constant drives 0.2 / 0.1.  A step is one tick.
                 time, against MEASURED_PEAKS.json's hbm_gbs.  The tiled layout
                 stores 2-byte column indices, so it streams fewer bytes than
                 the algorithmic count (``streamed_bytes_per_tick``).
-* ``cpu_baseline``  the CPU oracle (a C restatement of the reference tick,
-                OpenMP over all host cores) on a bounded sample of the same ticks.
+* ``cpu_baseline``  the reference's own CPU ``DendriticMatrixRuntime`` (fp32,
+                ``torch.sparse.mm``) from its offline install under baseline/_ref,
+                on all host cores and on one thread, with the CPU model and
+                torch version; beside it the C port of the tick (oracle/, OpenMP
+                over all host cores).  Each on a bounded sample of the same ticks.
 
-``--impl reference`` times that CPU implementation alone (the reference path
-is Python/PyTorch-CPU and cannot run on the GPU box; its arithmetic is the
-oracle's).
+``--impl reference`` times the reference's own CPU runtime alone on all host
+cores (the C port when the install is absent).
 
 ``--gpus N`` (under torchrun, one rank per GPU) row-shards the graph over the
 ranks; the soma vector is exchanged every tick by peer stores inside the tick
@@ -59,6 +61,7 @@ sys.path.insert(0, str(ROOT))
 
 from neurosim_gpu_b200 import (DendriticDynamics, Dynamics,  # noqa: E402
                                NativeDendriticMatrixRuntime, random_topology)
+from neurosim_gpu_b200.native import _outputs  # noqa: E402
 
 WORKLOADS = {
     # name: (neurons, candidate edges, batch, precision)
@@ -83,6 +86,7 @@ PELS_THETA = 0.02
 DEFAULT_WORKLOAD = "matrix_n166k_m25M_b1_fp32"
 WEIGHT_BYTES = {"fp32": 4.0, "fp16": 2.0, "fp8": 1.0, "nvfp4": 0.5 + 1.0 / 16.0}
 FALLBACK_HBM_GBS = 6650.0
+L2_FLUSH_BYTES = 256 << 20  # twice the B200's 126 MB L2
 
 
 def algorithmic_bytes(neurons: int, edges: int, batch: int, precision: str) -> float:
@@ -191,21 +195,109 @@ def cpu_oracle_rate(graph, batch: int, seconds: float, max_ticks: int | None = N
     return graph.n_edges * batch / per_tick, per_tick, ticks, oracle.max_threads()
 
 
+REFERENCE_INSTALL = ROOT / "baseline" / "_ref"
+TOPOLOGY_FIELDS = ("src", "dst", "weight", "out_rowptr", "in_rowptr", "in_col",
+                   "out_weight_index", "in_weight")
+
+
+def host_identity() -> dict:
+    """CPU model, usable cores and torch version of the host that runs the CPU leg."""
+    model = None
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return {"cpu_model": model, "host_cores": cores, "torch": torch.__version__}
+
+
+def reference_runtime_rate(graph, batch: int, seconds: float, max_ticks: int | None = None
+                           ) -> dict | None:
+    """The reference's own CPU ``DendriticMatrixRuntime`` (fp32, ``torch.sparse.mm``;
+    compartmental.py:274-293), from its offline install under baseline/_ref, on the
+    same graph: all host cores, then one thread, under ``inference_mode`` with 5
+    warm-up ticks, the median of timed blocks of ticks.  None when the install is
+    absent.  The graph is handed over as the reference's own ``SparseTopology``
+    dataclass holding this run's arrays (equal, array for array, to the
+    reference generator's: tests/test_topology_golden.py).
+    """
+    if not (REFERENCE_INSTALL / "neurosim_gpu" / "__init__.py").exists():
+        return None
+    if str(REFERENCE_INSTALL) not in sys.path:
+        sys.path.insert(0, str(REFERENCE_INSTALL))
+    import neurosim_gpu as ref
+
+    n = graph.n_neurons
+    topology = ref.SparseTopology(n_neurons=n, **{f: getattr(graph, f).detach().cpu()
+                                                  for f in TOPOLOGY_FIELDS})
+    soma = ref.Dynamics(torch.full((n,), 0.72), torch.full((n,), 0.8))
+    model = ref.DendriticDynamics.from_time_constants(soma, dt=1.0, tau_dendrite=4.0,
+                                                      tau_adaptation=25.0, coupling=0.5,
+                                                      adaptation_strength=0.2)
+    identity = host_identity()
+    threads_before = torch.get_num_threads()
+    result = {"kind": "reference", "runtime": "neurosim_gpu.DendriticMatrixRuntime (fp32)",
+              "reference_version": getattr(ref, "__version__", None), **identity, "runs": []}
+    try:
+        for threads in (identity["host_cores"], 1):
+            torch.set_num_threads(threads)
+            runtime = ref.DendriticMatrixRuntime(topology, model, torch.zeros(batch, n))
+            with torch.inference_mode():
+                for _ in range(5):
+                    runtime.step(0.2, dendritic_drive=0.1)
+                blocks, ticks, start = [], 0, time.perf_counter()
+                while True:
+                    t0 = time.perf_counter()
+                    for _ in range(4):
+                        runtime.step(0.2, dendritic_drive=0.1)
+                    blocks.append((time.perf_counter() - t0) / 4)
+                    ticks += 4
+                    if time.perf_counter() - start >= seconds or (
+                            max_ticks is not None and ticks >= max_ticks):
+                        break
+            per_tick = statistics.median(blocks)
+            result["runs"].append({"threads": threads, "ms_per_tick": per_tick * 1e3,
+                                   "value": graph.n_edges * batch / per_tick, "ticks": ticks})
+    finally:
+        torch.set_num_threads(threads_before)
+    return result
+
+
 def build_graph(neurons: int, edges: int, device):
     # CPU draws (the reference's random stream), canonicalised on the GPU.
     return random_topology(neurons, edges, device="cpu", seed=0, build_device=device)
 
 
 def run_reference(args, workload: str, explicit_workload: bool, world: int) -> dict:
+    """The reference arm: the reference's own CPU DendriticMatrixRuntime on all host
+    cores (the baseline/_ref install), each step one full tick of the same graph; the
+    C port of the tick (oracle/) when the install is absent."""
     neurons, edges, batch, precision = WORKLOADS[workload]
     name = workload
     if world > 1 and not explicit_workload:
         neurons, edges = neurons * world, edges * world
         name = f"matrix_weak_n{neurons}_m{edges}_b{batch}_{precision}"
     graph = random_topology(neurons, edges, device="cpu", seed=0)
-    # Each step is one full tick; the run is capped at about a minute of CPU time.
-    rate, per_tick, ticks, cores = cpu_oracle_rate(graph, batch, seconds=60.0,
-                                                   max_ticks=max(args.steps, 1))
+    steps = max(args.steps, 1)
+    reference = reference_runtime_rate(graph, batch, seconds=30.0, max_ticks=steps)
+    # The C port (oracle/, OpenMP over all host cores), reported beside it.
+    port_rate, port_tick, port_ticks, port_cores = cpu_oracle_rate(graph, batch, seconds=10.0,
+                                                                   max_ticks=steps)
+    port = {"value": port_rate, "unit": "synapse-updates/s", "cores": port_cores, "kind": "port",
+            "ms_per_tick": port_tick * 1e3, "sample": f"{port_ticks} ticks of the full graph"}
+    if reference is not None:
+        full = reference["runs"][0]
+        rate, per_tick = full["value"], full["ms_per_tick"] * 1e-3
+        baseline = {"value": rate, "unit": "synapse-updates/s", "cores": full["threads"],
+                    "kind": "reference",
+                    "sample": f"{full['ticks']} ticks of the full graph (median of 4-tick blocks)",
+                    **{k: v for k, v in reference.items() if k != "kind"}, "port": port}
+    else:
+        rate, per_tick = port_rate, port_tick
+        baseline = {**port, "reason": "the reference install (baseline/_ref) is absent"}
     return {
         "metric": "synapse-updates/s (M*B/tick)", "value": rate, "unit": "synapse-updates/s",
         "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -213,8 +305,7 @@ def run_reference(args, workload: str, explicit_workload: bool, world: int) -> d
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference random_topology stream, seed 0)",
         "config": {"workload": name, "neurons": neurons, "edges": graph.n_edges,
                    "batch": batch, "weights": "fp32"},
-        "cpu_baseline": {"value": rate, "unit": "synapse-updates/s", "cores": cores,
-                         "kind": "port", "sample": f"{ticks} ticks of the full graph"},
+        "cpu_baseline": baseline,
         "e2e": {"value": rate, "unit": "synapse-updates/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -304,6 +395,17 @@ def run_native(args, workload: str) -> dict:
         steps = max(args.steps, 1) if tiled else max(args.steps - args.steps % chunk, chunk)
         runtime.run(chunk, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
         torch.cuda.synchronize()
+        timed_launch = None
+        if tiled:
+            # The timed launch is prepared (validated, its arguments packed)
+            # before the timed region, so the region holds device work only.
+            u, us = runtime._drive(0.2)
+            v, vs = runtime._drive(0.1, "dendritic_drive")
+            _, views = _outputs(3, runtime.state)
+            timed_launch = runtime._prepare(runtime.state, runtime.dendritic_state,
+                                            runtime.adaptation_state, u, us, v, vs, views,
+                                            ticks=steps)
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
         sampler = ClockSampler(torch.cuda.current_device())
         with sampler:
             # Busy pre-roll so the first samples already see the loaded clock.
@@ -313,10 +415,19 @@ def run_native(args, workload: str) -> dict:
                 torch.cuda.synchronize()
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
+            # An L2 flush (a write of twice the L2) before the start event: no
+            # edge bytes of earlier launches stay in L2, and the device is busy
+            # while the host enqueues the timed work.
+            flush.zero_()
             start.record()
-            runtime.run(steps, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
+            if timed_launch is not None:
+                timed_launch()
+            else:
+                runtime.run(steps, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
             end.record()
             end.synchronize()
+            if timed_launch is not None:
+                runtime.state, runtime.dendritic_state, runtime.adaptation_state = views
             post = time.perf_counter()
             while time.perf_counter() - post < 0.3:
                 runtime.run(chunk * 4, 0.2, dendritic_drive=0.1, graph_ticks=chunk)
@@ -340,7 +451,9 @@ def run_native(args, workload: str) -> dict:
         e2e_steps = min(steps, 512)
         host_drives = torch.full((e2e_steps, batch, neurons), 0.2).pin_memory()
         host_states = torch.empty((e2e_steps, batch, neurons)).pin_memory()
-        runtime.stream(host_drives[:8], host_states[:8], dendritic_drive=0.1)
+        # Warm-up call of the same length (builds the rollout plan: rings,
+        # streams and the prepared launches it reuses).
+        runtime.stream(host_drives, host_states, dendritic_drive=0.1)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         wall = time.perf_counter()
@@ -364,7 +477,8 @@ def run_native(args, workload: str) -> dict:
         "data": "synthetic (reference random_topology stream, seed 0; drives 0.2/0.1)",
         "config": {"workload": workload, "neurons": neurons, "edges": m, "batch": batch,
                    "weights": precision, "parallelism": "single GPU",
-                   "l2": "inputs larger than L2 (edge stream %.0f MB vs 126 MB)" % (algo / 1e6),
+                   "l2": "inputs larger than L2 (edge stream %.0f MB vs 126 MB); L2 flushed "
+                         "(256 MB write) before the timed launch" % (algo / 1e6),
                    **({"ticks_per_launch": steps} if tiled else {"ticks_per_graph": chunk}),
                    "kernel_path": runtime.kernel_path,
                    "column_blocks": layout.blocks if layout is not None else None,
@@ -389,10 +503,20 @@ def run_native(args, workload: str) -> dict:
     }
     if not args.skip_cpu_baseline:
         rate_cpu, per_tick, ticks, cores = cpu_oracle_rate(graph, batch, seconds=args.cpu_seconds)
-        result["cpu_baseline"] = {"value": rate_cpu, "unit": "synapse-updates/s", "cores": cores,
-                                  "kind": "port",
-                                  "sample": f"{ticks} ticks of the full graph "
-                                            f"({per_tick * 1e3:.2f} ms/tick)"}
+        port = {"value": rate_cpu, "unit": "synapse-updates/s", "cores": cores, "kind": "port",
+                "sample": f"{ticks} ticks of the full graph ({per_tick * 1e3:.2f} ms/tick)"}
+        reference = reference_runtime_rate(graph, batch, seconds=args.cpu_seconds)
+        if reference is not None:
+            full = reference["runs"][0]
+            result["cpu_baseline"] = {
+                "value": full["value"], "unit": "synapse-updates/s", "cores": full["threads"],
+                "kind": "reference",
+                "sample": f"{full['ticks']} ticks of the full graph ({full['ms_per_tick']:.2f} "
+                          "ms/tick, median of 4-tick blocks)",
+                **{k: v for k, v in reference.items() if k != "kind"}, "port": port}
+        else:
+            result["cpu_baseline"] = {**port, **host_identity(),
+                                      "reason": "the reference install (baseline/_ref) is absent"}
     return result
 
 

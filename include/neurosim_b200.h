@@ -184,9 +184,12 @@ NSB_API int nsb_dendritic_event(const nsb_tick* tick, float* current, const nsb_
  * holds plain device pointers and has no CUDA allocator of its own.
  *
  * - B * N above NSB_EVENT_NOALLOC_MAX_PAIRS is rejected with NSB_ERR_ARGUMENT.
- * - The first call on a device looks up the array's device address with that
- *   device current (cudaGetSymbolAddress) and keeps it; make that first call
- *   before any stream capture.
+ * - The first call in each CUDA context (normally once per device, in its
+ *   primary context) looks up the array's device address with that device
+ *   current (cudaGetSymbolAddress) and keeps it for that context; a call in a
+ *   new context (after cudaDeviceReset, or with another driver context
+ *   current) looks it up again.  Make the first call before any stream
+ *   capture.
  * - All calls on a device share the one array, and each call only clears the
  *   counter head it needs zeroed; calls whose work overlaps on the GPU (other
  *   streams, other threads) race on the array and must be serialised by the

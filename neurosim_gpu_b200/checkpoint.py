@@ -27,7 +27,7 @@ from __future__ import annotations
 import hashlib
 import json
 from pathlib import Path
-from typing import Any, BinaryIO, Mapping
+from typing import Any, BinaryIO, Mapping, Sequence
 
 import torch
 
@@ -190,8 +190,38 @@ def capture_sharded_runtime(runtime: Any, topology: SparseTopology | None) -> di
     adaptation = runtime.gather("adaptation_state").detach().to("cpu").clone()
     if runtime.rank != 0:
         return None
+    return _sharded_payload(runtime, topology, state, dendrite, adaptation)
+
+
+def capture_sharded_ranks(ranks: Sequence[Any], topology: SparseTopology) -> dict:
+    """One payload of a row-sharded run whose ranks all live in this process.
+
+    ``ranks`` are the per-rank runtimes built with explicit ``rank`` / ``world``
+    and no process group (the caller exchanges the soma vector between them);
+    their rows are concatenated in rank order, which is what the collective
+    :func:`capture_sharded_runtime` gathers to rank 0.  The payload is the same.
+    """
+    if not ranks:
+        raise ValueError("no ranks given")
+    world = ranks[0].world
+    if sorted(r.rank for r in ranks) != list(range(world)) or any(r.world != world for r in ranks):
+        raise ValueError("ranks must be every rank 0..world-1 of one run")
+    ordered = sorted(ranks, key=lambda r: r.rank)
+    if len({(r._tick, r.shard.current) for r in ordered}) != 1:
+        raise ValueError("the ranks are not at the same tick")
+    state = ordered[0].state.detach().to("cpu").clone()
+    dendrite = torch.cat([r.dendritic_state.detach().to("cpu") for r in ordered], dim=1)
+    adaptation = torch.cat([r.adaptation_state.detach().to("cpu") for r in ordered], dim=1)
+    return _sharded_payload(ordered[0], topology, state, dendrite, adaptation)
+
+
+def _sharded_payload(runtime: Any, topology: SparseTopology | None, state: torch.Tensor,
+                     dendrite: torch.Tensor, adaptation: torch.Tensor) -> dict:
     if not isinstance(topology, SparseTopology) or topology.n_neurons != runtime.neurons:
         raise ValueError("rank 0 must pass the run's full SparseTopology")
+    shape = (runtime.batch, runtime.neurons)
+    if any(tuple(t.shape) != shape for t in (state, dendrite, adaptation)):
+        raise ValueError("the gathered states do not cover every neuron of the run")
     payload = _header("NativeDendriticMatrixRuntime", runtime.precision,
                       runtime_signature(_SignatureView(runtime)), topology)
     payload["tensors"].update(state=state, dendritic_state=dendrite, adaptation_state=adaptation)
@@ -240,5 +270,5 @@ def load_runtime_checkpoint(source: str | Path | BinaryIO, runtime: Any) -> None
 
 
 __all__ = ["FORMAT", "VERSION", "runtime_signature", "capture_runtime", "restore_runtime",
-           "capture_sharded_runtime", "restore_sharded_runtime", "save_runtime_checkpoint",
-           "load_runtime_checkpoint"]
+           "capture_sharded_runtime", "capture_sharded_ranks", "restore_sharded_runtime",
+           "save_runtime_checkpoint", "load_runtime_checkpoint"]

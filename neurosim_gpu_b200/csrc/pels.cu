@@ -185,25 +185,74 @@ static __device__ __align__(256) unsigned char g_event_scratch[256 + NSB_EVENT_N
 
 namespace {
 std::mutex g_scratch_mutex;
-void* g_scratch_address[64] = {nullptr};
+
+// The scratch address belongs to one CUDA context: after cudaDeviceReset, or
+// with a different (non-primary) driver context current, the array has another
+// address.  Cached addresses are therefore keyed by the context's unique id
+// (cuCtxGetId: never reused within a process), reached through the runtime's
+// driver entry point so the library does not link libcuda.
+using CtxGetCurrent = int (*)(void**);
+using CtxGetId = int (*)(void*, unsigned long long*);
+struct ScratchEntry {
+  unsigned long long context_id;
+  void* address;
+};
+ScratchEntry g_scratch_address[64] = {};
+
+cudaError_t current_context_id(unsigned long long* id) {
+  static CtxGetCurrent get_current = nullptr;
+  static CtxGetId get_id = nullptr;
+  if (!get_current || !get_id) {
+    void* fn_current = nullptr;
+    void* fn_id = nullptr;
+    cudaDriverEntryPointQueryResult found_current, found_id;
+    cudaError_t err = cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn_current, cudaEnableDefault,
+                                              &found_current);
+    if (err != cudaSuccess) return err;
+    err = cudaGetDriverEntryPoint("cuCtxGetId", &fn_id, cudaEnableDefault, &found_id);
+    if (err != cudaSuccess) return err;
+    if (found_current != cudaDriverEntryPointSuccess || found_id != cudaDriverEntryPointSuccess ||
+        !fn_current || !fn_id)
+      return cudaErrorNotSupported;
+    get_current = reinterpret_cast<CtxGetCurrent>(fn_current);
+    get_id = reinterpret_cast<CtxGetId>(fn_id);
+  }
+  void* context = nullptr;
+  if (get_current(&context) != 0 || !context) return cudaErrorDeviceUninitialized;
+  return get_id(context, id) == 0 ? cudaSuccess : cudaErrorDeviceUninitialized;
+}
 }  // namespace
 
-// Device address of g_event_scratch on the current device.  The host-side name
-// of the array is only a stand-in; the first call on each device asks the
-// runtime for the real address (with that device current) and keeps it.
+// Device address of g_event_scratch in the current context.  The host-side name
+// of the array is only a stand-in; the first call in each context asks the
+// runtime for the real address (with that context's device current) and keeps
+// it for later calls in the same context.
 cudaError_t event_noalloc_scratch(void** address) {
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) return err;
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (!g_scratch_address[device]) {
+  unsigned long long context_id = 0;
+  err = current_context_id(&context_id);
+  if (err == cudaErrorDeviceUninitialized) {
+    // No context is current yet: the runtime's symbol lookup makes the
+    // device's primary context current, then ask again.
     void* ptr = nullptr;
     err = cudaGetSymbolAddress(&ptr, g_event_scratch);
     if (err != cudaSuccess) return err;
-    g_scratch_address[device] = ptr;
+    err = current_context_id(&context_id);
   }
-  *address = g_scratch_address[device];
+  if (err != cudaSuccess) return err;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  ScratchEntry& entry = g_scratch_address[device];
+  if (!entry.address || entry.context_id != context_id) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_event_scratch);
+    if (err != cudaSuccess) return err;
+    entry.address = ptr;
+    entry.context_id = context_id;
+  }
+  *address = entry.address;
   return cudaSuccess;
 }
 

@@ -12,8 +12,9 @@
 //    gathered buffer needs no clearing.
 //    * Local mode: the caller all-gathers the buffers (NCCL) before step 2.
 //    * Peer mode (the exchange fused into the kernels): each delta is stored
-//      into every rank's buffer of this tick's parity over NVLink; each thread
-//      fences at system scope, each CTA counts itself done, and the last CTA
+//      into every rank's buffer of this tick's parity over NVLink; after a CTA
+//      barrier one thread per CTA fences at system scope and counts the CTA
+//      done, and the last CTA
 //      adds one to every rank's arrival counter and advances this rank's tick
 //      count (device memory, so CUDA-graph replays need no host epoch).
 // 2. event_scatter_rows_kernel: in peer mode every CTA first waits (bounded)
@@ -75,8 +76,12 @@ event_rows_kernel(TickArgs t, EventRowsArgs e, TickOut out, Out out_emitted, Del
     }
   }
   if (X) {
-    __threadfence_system();  // this thread's peer stores, before the CTA counts itself done
+    // Every thread's peer stores precede the CTA barrier; one system-scope
+    // fence after it (cumulative over the barrier) orders them all before the
+    // CTA counts itself done.  A fence per thread costs ~ one NVLink round trip
+    // each and stalls behind copies in flight.
     __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
     if (threadIdx.x == 0 && atomicAdd(&state->done, 1u) == gridDim.x - 1) {
       // The last CTA of this tick: every CTA has counted itself, so the count
       // can start over for the next tick.

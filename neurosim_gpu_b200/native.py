@@ -853,14 +853,16 @@ class DendriticExtension:
 
 def _event_noalloc(ext: DendriticExtension, state, dendrite, adaptation, params, current,
                    emitted, theta, out_rowptr, dst, out_weight_index, weight, input,
-                   input_scalar, dendritic_input, dendritic_scalar):
+                   input_scalar, dendritic_input, dendritic_scalar, *, out=None):
     """PELS tick through ``nsb_dendritic_event_noalloc``: no workspace from the caller.
 
     For hosts that cannot give the library scratch memory (device memory
     reserved up front by the application's own pool, or a foreign-language host
     without a CUDA allocator).  The library's fixed scratch array is shared by
     all such calls on a GPU, so calls must not overlap on the GPU.  Outputs are
-    allocated here, as in :meth:`DendriticExtension.dendritic_event`.
+    allocated here, as in :meth:`DendriticExtension.dendritic_event`, unless
+    ``out`` gives the four [B, N] float32 tensors (s', d', a', emitted') to
+    write, in which case nothing is allocated on the device.
     """
     _check_state(state)
     tick = _tick(state, dendrite, adaptation, params, input, input_scalar, dendritic_input,
@@ -879,7 +881,14 @@ def _event_noalloc(ext: DendriticExtension, state, dendrite, adaptation, params,
     out_csr = _OutCsr(edges, out_rowptr.data_ptr(), dst.data_ptr() if edges else None,
                       out_weight_index.data_ptr() if (out_weight_index is not None and edges)
                       else None, weight.data_ptr() if edges else None)
-    _, views = _outputs(4, state, neuron_major=False)
+    if out is None:
+        _, views = _outputs(4, state, neuron_major=False)
+    else:
+        _check(len(out) == 4, "four output tensors are required")
+        for view in out:
+            _float_on(view, state)
+            _check(view.shape == state.shape, "output shape mismatch")
+        views = list(out)
     out = _TickOut(_out(views[0]), _out(views[1]), _out(views[2]))
     out_emitted = _out(views[3])
     with torch.cuda.device(state.device):

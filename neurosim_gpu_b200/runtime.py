@@ -186,9 +186,11 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         self.weight_format = weight_format
         self.precision = "fp32"
         self._graphs: dict = {}
+        self._rollout_plan = None
         self._invalidate_precision_cache()
 
     def _invalidate_precision_cache(self) -> None:
+        self._rollout_plan = None
         self._packed_weight = None
         self._packed_weight_version = -1
         self._graphs = {}
@@ -439,71 +441,27 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         return out
 
     def _stream_rollouts(self, drives, out, v, vs):
-        state = self.state
-        device = state.device
-        neurons = state.shape[1]
         slots = self._cluster_slots()
         # A cluster tick takes ~2 us and moves a few KB of copies: uniform
-        # launches of 128 ticks (two prepared launch callables; preparing one
-        # costs more host time than a short launch runs).  The tiled path ramps
-        # 4, 8, 16, 32 so that its first upload (0.7 MB per tick at 166k) is short.
+        # launches of 128 ticks.  The tiled path starts and ends with short
+        # launches (1, 2, 4, ... ticks) so that the upload before the first
+        # launch and the download after the last one (0.66 MB per tick at
+        # 166k, ~15 us each) are short; the next launch's drives (twice as
+        # many ticks) upload within the running launch.
         if slots is not None:
             chunks = _tiled.rollout_chunks(drives.shape[0], cap=128, first=128)
         else:
             chunks = _tiled.rollout_chunks(drives.shape[0])
-        widest = max(chunks)
-        running = tuple(x.clone() for x in (state, self.dendritic_state, self.adaptation_state))
-        drive_ring = [torch.empty((widest, 1, neurons), device=device) for _ in range(2)]
-        history = [torch.empty((widest, 1, neurons), device=device) for _ in range(2)]
-        calls: dict[tuple[int, int], object] = {}
-
-        def call(k: int, length: int):
-            if (k, length) in calls:
-                return calls[k, length]
-            rollout = (neurons, history[k][:length])
-            if slots is not None:
-                weight, scales, scale, _ = self._weights()
-                topology = self.topology
-                launch = self.extension.prepare_run_cluster(
-                    *running, self._parameters(), topology.in_rowptr, topology.in_col, weight,
-                    drive_ring[k][0], 0.0, v, vs, scales, scale, out=running, ticks=length,
-                    max_slots=slots, status=self._status, rollout=rollout)
-            else:
-                launch = self.extension.prepare_step_tiled(
-                    *running, self._parameters(), self._tiled_layout(), drive_ring[k][0], 0.0,
-                    v, vs, out=running, status=self._status, ticks=length, rollout=rollout)
-            calls[k, length] = launch
-            return launch
-
-        compute = torch.cuda.current_stream(device)
-        upload = torch.cuda.Stream(device=device)
-        download = torch.cuda.Stream(device=device)
-        uploaded = [torch.cuda.Event() for _ in range(2)]
-        consumed = [torch.cuda.Event() for _ in range(2)]  # rollout done with ring slot k
-        saved = [torch.cuda.Event() for _ in range(2)]     # history[k] downloaded
-        upload.wait_stream(compute)
-        download.wait_stream(compute)
-        lo = 0
-        for c, length in enumerate(chunks):
-            k, hi = c % 2, lo + length
-            with torch.cuda.stream(upload):
-                if c >= 2:
-                    upload.wait_event(consumed[k])
-                drive_ring[k][:length].copy_(drives[lo:hi], non_blocking=True)
-                uploaded[k].record(upload)
-            compute.wait_event(uploaded[k])
-            if c >= 2:
-                compute.wait_event(saved[k])
-            call(k, length)()
-            consumed[k].record(compute)
-            with torch.cuda.stream(download):
-                download.wait_event(consumed[k])
-                out[lo:hi].copy_(history[k][:length], non_blocking=True)
-                saved[k].record(download)
-            lo = hi
-        compute.wait_stream(download)
-        compute.wait_stream(upload)
-        return running
+        weight, scales, scale, _ = self._weights()
+        key = (slots, self.kernel_path, self._layout_key, self._packed_weight_version,
+               None if v is None else (v.data_ptr(), v.stride()), vs,
+               tuple(p.data_ptr() for p in self._parameters()), weight.data_ptr())
+        plan = self._rollout_plan
+        if plan is None or plan.key != key or plan.capacity < max(chunks):
+            # Rings as long as the longest launch any stream() call makes.
+            capacity = 128 if slots is not None else _tiled.ROLLOUT_CAP
+            plan = self._rollout_plan = _RolloutPlan(self, key, max(capacity, *chunks), v, vs)
+        return plan.run(self, drives, out, chunks)
 
     def _stream_ticks(self, drives, out, v, vs):
         state = self.state
@@ -547,6 +505,91 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         compute.wait_stream(download)
         compute.wait_stream(upload)
         return tuple(x.clone() for x in buffers[ticks % 2])
+
+
+class _RolloutPlan:
+    """What a streamed rollout reuses from one ``stream()`` call to the next.
+
+    The two copy streams, their events, the device rings of drives and soma
+    history, the running state and a prepared launch callable per (ring slot,
+    launch length) are built once per runtime (rebuilt only when the weights,
+    parameters, dendritic drive or the widest launch change), so a call costs
+    its copies and launches, not their set-up (~1.5 ms of host time per call
+    otherwise).  Every launch runs in place on ``running``; the call copies
+    the runtime's state in first and hands out a fresh copy at the end, so
+    tensors returned earlier are never overwritten.
+    """
+
+    def __init__(self, runtime: "NativeDendriticMatrixRuntime", key, widest: int, v, vs) -> None:
+        self.key = key
+        state = runtime.state
+        device = state.device
+        neurons = state.shape[1]
+        self.device = device
+        self.capacity = widest
+        self.block, self.running = _native._outputs(3, state)
+        self.drive_ring = [torch.empty((widest, 1, neurons), device=device) for _ in range(2)]
+        self.history = [torch.empty((widest, 1, neurons), device=device) for _ in range(2)]
+        self.upload = torch.cuda.Stream(device=device)
+        self.download = torch.cuda.Stream(device=device)
+        self.uploaded = [torch.cuda.Event() for _ in range(2)]
+        self.consumed = [torch.cuda.Event() for _ in range(2)]  # rollout done with ring slot k
+        self.saved = [torch.cuda.Event() for _ in range(2)]     # history[k] downloaded
+        self.v, self.vs = v, vs
+        self.calls: dict[tuple[int, int], object] = {}
+
+    def call(self, runtime: "NativeDendriticMatrixRuntime", k: int, length: int):
+        launch = self.calls.get((k, length))
+        if launch is not None:
+            return launch
+        running, neurons = self.running, self.running[0].shape[1]
+        rollout = (neurons, self.history[k][:length])
+        slots = runtime._cluster_slots()
+        if slots is not None:
+            weight, scales, scale, _ = runtime._weights()
+            topology = runtime.topology
+            launch = runtime.extension.prepare_run_cluster(
+                *running, runtime._parameters(), topology.in_rowptr, topology.in_col, weight,
+                self.drive_ring[k][0], 0.0, self.v, self.vs, scales, scale, out=running,
+                ticks=length, max_slots=slots, status=runtime._status, rollout=rollout)
+        else:
+            launch = runtime.extension.prepare_step_tiled(
+                *running, runtime._parameters(), runtime._tiled_layout(), self.drive_ring[k][0],
+                0.0, self.v, self.vs, out=running, status=runtime._status, ticks=length,
+                rollout=rollout)
+        self.calls[k, length] = launch
+        return launch
+
+    def run(self, runtime: "NativeDendriticMatrixRuntime", drives, out, chunks):
+        compute = torch.cuda.current_stream(self.device)
+        upload, download = self.upload, self.download
+        for target, value in zip(self.running, (runtime.state, runtime.dendritic_state,
+                                                runtime.adaptation_state)):
+            target.copy_(value)
+        upload.wait_stream(compute)
+        download.wait_stream(compute)
+        lo = 0
+        for c, length in enumerate(chunks):
+            k, hi = c % 2, lo + length
+            with torch.cuda.stream(upload):
+                if c >= 2:
+                    upload.wait_event(self.consumed[k])
+                self.drive_ring[k][:length].copy_(drives[lo:hi], non_blocking=True)
+                self.uploaded[k].record(upload)
+            compute.wait_event(self.uploaded[k])
+            if c >= 2:
+                compute.wait_event(self.saved[k])
+            self.call(runtime, k, length)()
+            self.consumed[k].record(compute)
+            with torch.cuda.stream(download):
+                download.wait_event(self.consumed[k])
+                out[lo:hi].copy_(self.history[k][:length], non_blocking=True)
+                self.saved[k].record(download)
+            lo = hi
+        compute.wait_stream(download)
+        compute.wait_stream(upload)
+        block = self.block.clone()
+        return tuple(block[i] for i in range(3))
 
 
 class _TickGraph:

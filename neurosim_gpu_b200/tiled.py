@@ -440,14 +440,20 @@ __all__ = ["TiledLayout", "build_tiled_layout", "emulate", "plan_blocks", "cta_r
            "smem_limit", "sm_count", "status_word", "ctypes"]
 
 
-def rollout_chunks(ticks: int, cap: int = 32, first: int = 4) -> list[int]:
-    """Launch lengths of a streamed rollout of ``ticks`` ticks: 4, 8, 16, then
-    ``cap``-tick launches, then 16, 8, 4, so that the upload before the first
-    launch and the download after the last one are short."""
+ROLLOUT_CAP = 32  # longest launch of a streamed rollout on the tiled path
+
+
+def rollout_chunks(ticks: int, cap: int = ROLLOUT_CAP, first: int = 1) -> list[int]:
+    """Launch lengths of a streamed rollout of ``ticks`` ticks: ``first``, then
+    doubling up to ``cap``-tick launches, then halving back down, so that the
+    upload before the first launch and the download after the last one are
+    short and every launch's drives upload while the launch before it runs
+    (the next launch is at most twice as long)."""
     head, size = [], first
     while size < cap and 2 * (sum(head) + size) <= ticks:
         head.append(size)
         size *= 2
     middle = ticks - 2 * sum(head)
-    body = [cap] * (middle // cap) + ([middle % cap] if middle % cap else [])
+    pieces = -(-middle // cap)  # the middle in near-equal launches of at most `cap`
+    body = [middle // pieces + (i < middle % pieces) for i in range(pieces)] if pieces else []
     return head + body + head[::-1]

@@ -7,6 +7,7 @@ dendritic runtimes; the checks follow src/neurosim_gpu/checkpoint.py:121-245.
 
 from __future__ import annotations
 
+import io
 from pathlib import Path
 
 import pytest
@@ -133,3 +134,165 @@ def test_native_pels_checkpoint_round_trip(tmp_path):
             b.step(0.2, dendritic_drive=0.1)
     # The scatter adds with float atomics, so later ticks agree to rounding only.
     torch.testing.assert_close(a.state, b.state, atol=1e-5, rtol=0)
+
+
+# -- row-sharded runs (checkpoint.py:121-282 of the reference: capture / restore of
+# the _TENSOR_FIELDS; a sharded run is captured as one whole-graph payload) -----
+
+
+class _RankStub:
+    """The attributes a row-sharded runtime's capture reads, on the CPU."""
+
+    def __init__(self, rank, world, full_d, full_a, state, model, group=None):
+        from neurosim_gpu_b200.sharded import RowShard
+        batch, n = state.shape
+        self.rank, self.world, self.group = rank, world, group
+        self.batch, self.neurons, self.precision, self._tick = batch, n, "fp32", 9
+        self.shard = RowShard(n, batch, rank, world, torch.device("cpu"))
+        self.shard.load(state)
+        self.state = self.shard.state()
+        self.compartment_dynamics = model
+        self.dendritic_state = full_d[:, self.shard.lo:self.shard.hi].clone()
+        self.adaptation_state = full_a[:, self.shard.lo:self.shard.hi].clone()
+
+    def gather(self, name):
+        from neurosim_gpu_b200.sharded import ShardedDendriticMatrixRuntime
+        return ShardedDendriticMatrixRuntime.gather(self, name)
+
+
+def _sharded_case(n=301, batch=2):
+    g = torch.Generator().manual_seed(4)
+    return (torch.rand(batch, n, generator=g), torch.rand(batch, n, generator=g),
+            torch.rand(batch, n, generator=g))
+
+
+def _gloo_capture(rank, world, port, queue):
+    import io
+    import os
+
+    import torch.distributed as dist
+
+    from neurosim_gpu_b200.checkpoint import capture_sharded_runtime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        state, d, a = _sharded_case()
+        graph = random_topology(301, 3000, device="cpu", seed=3)
+        stub = _RankStub(rank, world, d, a, state, _model(301))
+        payload = capture_sharded_runtime(stub, graph if rank == 0 else None)
+        blob = None
+        if payload is not None:  # serialised: shared tensor storage dies with the child
+            buffer = io.BytesIO()
+            torch.save(payload, buffer)
+            blob = buffer.getvalue()
+        queue.put((rank, blob))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_capture_gathers_every_rank_over_gloo(world):
+    """The collective capture (gloo ranks on the CPU) gathers the rows of every rank
+    into one payload, equal to the in-process capture of the same ranks."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    from neurosim_gpu_b200.checkpoint import capture_sharded_ranks
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_gloo_capture, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(results[r] is None for r in range(1, world))
+    payload = torch.load(io.BytesIO(results[0]), weights_only=True)
+    state, d, a = _sharded_case()
+    for name, want in (("state", state), ("dendritic_state", d), ("adaptation_state", a)):
+        assert torch.equal(payload["tensors"][name], want), name
+    assert payload["runtime_type"] == "NativeDendriticMatrixRuntime"
+    assert payload["scalars"]["_tick"] == 9
+    graph = random_topology(301, 3000, device="cpu", seed=3)
+    model = _model(301)
+    local = capture_sharded_ranks([_RankStub(r, world, d, a, state, model) for r in range(world)],
+                                  graph)
+    assert local["runtime_signature"] == payload["runtime_signature"]
+    for name in ("state", "dendritic_state", "adaptation_state"):
+        assert torch.equal(local["tensors"][name], payload["tensors"][name]), name
+
+
+def test_in_process_capture_rejects_incomplete_ranks():
+    from neurosim_gpu_b200.checkpoint import capture_sharded_ranks
+    state, d, a = _sharded_case()
+    graph = random_topology(301, 3000, device="cpu", seed=3)
+    ranks = [_RankStub(r, 3, d, a, state, _model(301)) for r in range(3)]
+    with pytest.raises(ValueError, match="every rank"):
+        capture_sharded_ranks(ranks[:2], graph)
+    ranks[1]._tick = 10
+    with pytest.raises(ValueError, match="same tick"):
+        capture_sharded_ranks(ranks, graph)
+
+
+def _emulated_ticks(ranks, ticks, drive=0.2):
+    """``ticks`` ticks of ranks that share one GPU; the exchange is a copy."""
+    for _ in range(ticks):
+        dsts = [rt.local_step(drive, dendritic_drive=0.1) for rt in ranks]
+        for rt, dst in zip(ranks, dsts):
+            for other in ranks:
+                lo, hi = other.shard.lo, other.shard.hi
+                rt.shard.buffers[dst][lo:hi] = other.shard.buffers[dst][lo:hi]
+            rt.finish(dst)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision", ["fp32", "nvfp4"])
+def test_sharded_checkpoint_restores_on_one_gpu_and_on_another_world(precision):
+    """A world-2 run (ranks emulated on one GPU) is captured, restored into a
+    single-GPU runtime and into a world-3 run, and all three continue bit for bit."""
+    from neurosim_gpu_b200 import NativeDendriticMatrixRuntime
+    from neurosim_gpu_b200.checkpoint import capture_sharded_ranks, restore_sharded_runtime
+    from neurosim_gpu_b200.sharded import ShardedDendriticMatrixRuntime
+    n = 6001
+    graph = random_topology(n, 180000, device="cpu", seed=9).to("cuda")
+    model = _model(n, "cuda")
+    initial = torch.rand(1, n, generator=torch.Generator().manual_seed(2)).cuda()
+
+    def world_of(size, start):
+        return [ShardedDendriticMatrixRuntime(graph, model, start, precision=precision,
+                                              rank=r, world=size) for r in range(size)]
+
+    two = world_of(2, initial)
+    with torch.inference_mode():
+        _emulated_ticks(two, 10)
+        payload = capture_sharded_ranks(two, graph)
+        _emulated_ticks(two, 6)
+    assert payload["scalars"]["_tick"] == 10
+    single = NativeDendriticMatrixRuntime(graph, model, torch.zeros(1, n, device="cuda"),
+                                          precision=precision, kernel="tiled")
+    restore_runtime(single, payload)
+    three = world_of(3, torch.zeros(1, n, device="cuda"))
+    for rt in three:
+        restore_sharded_runtime(rt, payload)
+        assert rt._tick == 10
+    with torch.inference_mode():
+        for _ in range(6):
+            single.step(0.2, dendritic_drive=0.1)
+        _emulated_ticks(three, 6)
+    torch.cuda.synchronize()
+    assert torch.equal(single.state, two[0].state)
+    for rt in three:
+        assert torch.equal(rt.state, two[0].state)
+        lo, hi = rt.shard.lo, rt.shard.hi
+        assert torch.equal(rt.dendritic_state, single.dendritic_state[:, lo:hi])
+        assert torch.equal(rt.adaptation_state, single.adaptation_state[:, lo:hi])
+        rt.check_status()
+    for rt in two:
+        lo, hi = rt.shard.lo, rt.shard.hi
+        assert torch.equal(rt.dendritic_state, single.dendritic_state[:, lo:hi])

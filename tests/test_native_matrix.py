@@ -360,3 +360,41 @@ def test_stream_equals_steps_with_the_same_drives(ext, kernel, batch, n, m, tick
     streamed.check_status()
     for name in ("state", "dendritic_state", "adaptation_state"):
         assert torch.equal(getattr(streamed, name), getattr(stepped, name)), name
+
+
+@pytest.mark.parametrize("kernel,n,m", [("tiled", 6000, 150000), ("cluster", 1000, 20000)])
+def test_stream_calls_reuse_their_plan(ext, kernel, n, m):
+    """Consecutive stream() calls of different lengths, with step() and run() in
+    between, reuse one rollout plan (rings, copy streams, prepared launches) and
+    still equal step() bit for bit; states handed out earlier stay unchanged."""
+    graph = random_topology(n, m, device="cpu", seed=6).to("cuda")
+    model = bench_model(n)
+    initial = torch.rand(1, n, generator=torch.Generator().manual_seed(3)).cuda()
+    drives = (torch.rand(60, 1, n, generator=torch.Generator().manual_seed(4)) * 0.4).pin_memory()
+    stepped = NativeDendriticMatrixRuntime(graph, model, initial.clone(), kernel=kernel)
+    streamed = NativeDendriticMatrixRuntime(graph, model, initial.clone(), kernel=kernel)
+    with torch.inference_mode():
+        first = streamed.stream(drives[:20], dendritic_drive=0.1)
+        kept = streamed.state
+        kept_copy = kept.clone()
+        plan = streamed._rollout_plan
+        streamed.step(0.3, dendritic_drive=0.1)
+        streamed.run(3, 0.25, dendritic_drive=0.1)
+        second = streamed.stream(drives[20:], dendritic_drive=0.1)
+        assert streamed._rollout_plan is plan
+        states = []
+        for t in range(20):
+            states.append(stepped.step(drives[t].cuda(), dendritic_drive=0.1).clone())
+        stepped.step(0.3, dendritic_drive=0.1)
+        for _ in range(3):
+            stepped.step(0.25, dendritic_drive=0.1)
+        for t in range(20, 60):
+            states.append(stepped.step(drives[t].cuda(), dendritic_drive=0.1).clone())
+    torch.cuda.synchronize()
+    assert torch.equal(kept, kept_copy)
+    for t in range(60):
+        got = first[t] if t < 20 else second[t - 20]
+        assert torch.equal(got, states[t].cpu()), t
+    for name in ("state", "dendritic_state", "adaptation_state"):
+        assert torch.equal(getattr(streamed, name), getattr(stepped, name)), name
+    streamed.check_status()

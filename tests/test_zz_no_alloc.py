@@ -69,3 +69,36 @@ def test_noalloc_event_rejects_sizes_beyond_its_scratch():
         ext.dendritic_event_noalloc(state, state, state, model.parameters(), state.clone(), state,
                                     torch.zeros(n, device="cuda"), graph.out_rowptr, graph.dst,
                                     None, graph.weight, None, 0.0, None, 0.0)
+
+
+def test_noalloc_event_allocates_no_device_memory():
+    """The property the entry point exists for: with the caller's outputs given,
+    repeated calls leave the device's free memory and torch's allocator alone."""
+    ext = load_native_extension()
+    graph, model, state = _case()
+    params = model.parameters()
+    theta = torch.full((graph.n_neurons,), 0.01, device="cuda")
+    current = torch.zeros_like(state)
+    states = [[state.clone(), torch.zeros_like(state), torch.zeros_like(state),
+               torch.zeros_like(state)] for _ in range(2)]
+
+    def call(k):
+        s, d, a, e = states[k]
+        ext.dendritic_event_noalloc(s, d, a, params, current, e, theta, graph.out_rowptr,
+                                    graph.dst, None, graph.weight, None, 0.3, None, 0.1,
+                                    out=states[1 - k])
+
+    call(0)  # the first call in this context looks up the scratch address
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    allocated_before = torch.cuda.memory_allocated()
+    reserved_before = torch.cuda.memory_reserved()
+    for k in (1, 0, 1, 0):
+        call(k)
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before
+    assert torch.cuda.memory_allocated() == allocated_before
+    assert torch.cuda.memory_reserved() == reserved_before
+    assert bool(torch.isfinite(states[1][0]).all())
+    assert int((states[1][3] != 0).sum()) > 0  # sources did emit
