@@ -488,7 +488,7 @@ def run_native(args, workload: str) -> dict:
                      "frac": achieved / peak, "traffic": ncu_traffic(workload),
                      "algorithmic_bytes_per_launch": algo, "peak_source": peak_kind,
                      "kernel": {"tiled": "tiled_tick_kernel", "cluster": "cluster_tick_kernel"}
-                     .get(path, "csr_tick_kernel"),
+                     .get(path, "csr_batch_kernel" if batch > 1 else "csr_tick_kernel"),
                      "per": "tick",
                      "streamed_bytes_per_tick": (layout.stream_bytes() + 28 * batch * neurons
                                                  + 8 * layout.blocks * layout.splits * neurons

@@ -19,17 +19,22 @@
 //
 // Batched variant (csr_batch_kernel, every B >= 2; fastest when the batch rows
 // of a source are contiguous, the [N, B] state layout the runtime keeps):
-//   * One warp per destination row.  Lane l works on batch row b = l % BT of
-//     edge slot l / BT, so one gather instruction of the warp fetches the BT
-//     contiguous floats of 32 / BT edges (for BT = 8: four 32-byte sectors in
-//     one request) instead of one load per (edge, batch row).
-//   * The warp loads 32 edges' columns and weights with one coalesced load
-//     each and hands them to the (edge, batch) lanes with shuffles; all of a
-//     batch's gathers are issued before its FMAs.
-//   * Lane sums (edges l / BT, l / BT + 32/BT, ... in order) are reduced over
-//     the lanes of a batch row with a fixed xor tree; lanes 0..BT-1 then apply
-//     the pointwise update for their batch row.
+//   * G lanes (8, 16 or 32, from the mean degree) own one destination row and a
+//     tile of BT <= 8 batch rows.  Lane l of the group takes the row's edges
+//     e0 + l, e0 + l + G, ... (two in flight), and for each one loads the
+//     BT batch values of its source: with the [N, B] layout that is ONE vector
+//     load of BT contiguous floats (for BT = 8 a 256-bit load, one 32-byte
+//     sector), otherwise BT scalar loads -- the arithmetic is the same either
+//     way, so the result does not depend on the state's layout.
+//   * Each lane accumulates BT sums in CSR order over its edges.  The group
+//     then reduces its BT x G partial sums with a transposing butterfly (step
+//     s halves the values a lane keeps, exchanging the other half with the
+//     lane G >> (s + 1) away), ending with batch row b on lanes
+//     b * G / BT .. (b + 1) * G / BT - 1; a fixed xor tree finishes the sum.
+//   * The first lane of each batch row's lanes applies the pointwise update;
+//     with the [N, B] layout the BT updating lanes write one contiguous span.
 #include <algorithm>
+#include <type_traits>
 
 #include "nsb_launch.h"
 
@@ -37,6 +42,10 @@ namespace nsb {
 namespace {
 
 constexpr int kThreads = 256;
+
+bool aligned(const void* p, uintptr_t bytes) {
+  return (reinterpret_cast<uintptr_t>(p) % bytes) == 0;
+}
 
 template <int G, int BT, bool UPDATE, typename W>
 __global__ void __launch_bounds__(kThreads)
@@ -131,59 +140,116 @@ csr_tick_kernel(TickArgs t, View x, const int32_t* __restrict__ rowptr,
   }
 }
 
-template <int BT, bool UPDATE, typename W>
+// BT floats of one source for the batch tile: one vector load from a
+// BT * 4-byte aligned address (VEC), else BT strided scalar loads (entries
+// past the batch read as 0).
+template <int BT, bool VEC>
+__device__ __forceinline__ void load_batch(const float* p, int64_t sb, int valid, float (&v)[BT]) {
+  if constexpr (VEC && BT == 8) {
+    asm("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]),
+          "=f"(v[7])
+        : "l"(p));
+  } else if constexpr (VEC && BT == 4) {
+    asm("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];"
+        : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
+        : "l"(p));
+  } else if constexpr (VEC && BT == 2) {
+    asm("ld.global.nc.v2.f32 {%0,%1}, [%2];" : "=f"(v[0]), "=f"(v[1]) : "l"(p));
+  } else {
+#pragma unroll
+    for (int b = 0; b < BT; ++b) v[b] = b < valid ? __ldg(p + b * sb) : 0.0f;
+  }
+}
+
+// One edge's weight: the edge stream is read once per tick, so fp32 weights
+// bypass L1 and are evict-first in L2 (the narrower formats go through
+// their decoders).
+template <typename W>
+__device__ __forceinline__ float edge_weight(const W& w, int64_t e, uint64_t pol) {
+  if constexpr (std::is_same<W, WeightsF32>::value) {
+    float r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;"
+                 : "=f"(r)
+                 : "l"(w.w + e), "l"(pol));
+    return r;
+  } else {
+    return w.one(e);
+  }
+}
+
+template <int BT, int G, bool UPDATE, bool VEC, typename W>
 __global__ void __launch_bounds__(kThreads)
 csr_batch_kernel(TickArgs t, View x, const int32_t* __restrict__ rowptr,
                  const int32_t* __restrict__ col, W weights, TickOut out, Out product) {
-  constexpr int kEdgesPerStep = 32 / BT;
+  static_assert(G >= BT && G <= 32 && 32 % G == 0, "group width");
+  constexpr int kPerBatch = G / BT;  // lanes of a group that end with one batch row
   const int lane = threadIdx.x & 31;
-  const int b = lane % BT;
-  const int slot = lane / BT;
+  const int lg = lane % G;
   const int64_t neurons = t.neurons;
-  const int64_t batch = t.batch;
   const int64_t b0 = static_cast<int64_t>(blockIdx.y) * BT;
-  const bool active = b0 + b < batch;
-  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int valid = static_cast<int>(t.batch - b0 < BT ? t.batch - b0 : BT);
+  const int64_t group = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / G;
+  const int64_t n_groups = static_cast<int64_t>(gridDim.x) * blockDim.x / G;
   const uint64_t pol = evict_first_policy();
-  const float* __restrict__ xb = x.data + (active ? (b0 + b) * x.sb : 0);
+  const float* __restrict__ xb = x.data + b0 * x.sb;
 
-  for (int64_t n = warp; n < neurons; n += n_warps) {
-    const int64_t e0 = rowptr[n];
-    const int64_t e1 = rowptr[n + 1];
-    float acc = -0.0f;  // -0.0 is the exact additive identity
-    for (int64_t e = e0; e < e1; e += 32) {
-      const int count = static_cast<int>(e1 - e < 32 ? e1 - e : 32);
-      int c = 0;
-      float w = 0.0f;
-      if (lane < count) {
-        c = static_cast<int>(stream_load_u32(reinterpret_cast<const uint32_t*>(col + e + lane), pol));
-        w = weights.one(e + lane);
-      }
-      float v[BT];
+  for (int64_t base = group - lane / G; base < neurons; base += n_groups) {
+    const int64_t n = base + lane / G;  // the groups of a warp take consecutive rows
+    float acc[BT];
 #pragma unroll
-      for (int i = 0; i < BT; ++i) {  // gathers first: BT independent loads in flight
-        const int k = i * kEdgesPerStep + slot;
-        const int ck = __shfl_sync(0xffffffffu, c, k);
-        v[i] = (k < count && active) ? __ldg(xb + static_cast<int64_t>(ck) * x.sn) : 0.0f;
-      }
+    for (int b = 0; b < BT; ++b) acc[b] = -0.0f;  // -0.0 is the exact additive identity
+    if (n < neurons) {
+      const int64_t e1 = __ldg(rowptr + n + 1);
+      int64_t e = __ldg(rowptr + n) + lg;
+      for (; e + G < e1; e += 2 * G) {  // two edges per lane in flight
+        const int c0 = static_cast<int>(stream_load_u32(reinterpret_cast<const uint32_t*>(col + e), pol));
+        const int c1 = static_cast<int>(stream_load_u32(reinterpret_cast<const uint32_t*>(col + e + G), pol));
+        const float w0 = edge_weight(weights, e, pol);
+        const float w1 = edge_weight(weights, e + G, pol);
+        float v0[BT], v1[BT];
+        load_batch<BT, VEC>(xb + static_cast<int64_t>(c0) * x.sn, x.sb, valid, v0);
+        load_batch<BT, VEC>(xb + static_cast<int64_t>(c1) * x.sn, x.sb, valid, v1);
 #pragma unroll
-      for (int i = 0; i < BT; ++i) {
-        const int k = i * kEdgesPerStep + slot;
-        const float wk = __shfl_sync(0xffffffffu, w, k);
-        if (k < count) acc = fmaf(wk, v[i], acc);
+        for (int b = 0; b < BT; ++b) acc[b] = fmaf(w0, v0[b], acc[b]);
+#pragma unroll
+        for (int b = 0; b < BT; ++b) acc[b] = fmaf(w1, v1[b], acc[b]);
+      }
+      if (e < e1) {
+        const int c0 = static_cast<int>(stream_load_u32(reinterpret_cast<const uint32_t*>(col + e), pol));
+        const float w0 = edge_weight(weights, e, pol);
+        float v0[BT];
+        load_batch<BT, VEC>(xb + static_cast<int64_t>(c0) * x.sn, x.sb, valid, v0);
+#pragma unroll
+        for (int b = 0; b < BT; ++b) acc[b] = fmaf(w0, v0[b], acc[b]);
+      }
+    }
+    // Transposing butterfly: after step s a lane keeps BT >> (s + 1) sums; the
+    // upper lane of each pair keeps the upper half of the values.
+#pragma unroll
+    for (int s = 0; (BT >> s) > 1; ++s) {
+      const int off = G >> (s + 1);
+      const int half = (BT >> s) / 2;
+      const bool upper = (lg & off) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = upper ? acc[i] : acc[half + i];
+        const float keep = upper ? acc[half + i] : acc[i];
+        acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
       }
     }
 #pragma unroll
-    for (int off = BT; off < 32; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane < BT && active) {
+    for (int off = kPerBatch / 2; off > 0; off >>= 1)
+      acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], off);
+    const int b = lg / kPerBatch;
+    if (n < neurons && lg % kPerBatch == 0 && b < valid) {
       if constexpr (UPDATE) {
-        const Update r = advance_at(t, acc, b0 + b, n);
+        const Update r = advance_at(t, acc[0], b0 + b, n);
         out.s.put(b0 + b, n, r.s);
         out.d.put(b0 + b, n, r.d);
         out.a.put(b0 + b, n, r.a);
       } else {
-        product.put(b0 + b, n, acc);
+        product.put(b0 + b, n, acc[0]);
       }
     }
   }
@@ -221,10 +287,10 @@ cudaError_t launch_variant(const TickArgs& t, const View& x, const Csr& csr, con
   return cudaGetLastError();
 }
 
-template <int BT, bool UPDATE, typename W>
+template <int BT, int G, bool UPDATE, bool VEC, typename W>
 cudaError_t launch_batch_variant(const TickArgs& t, const View& x, const Csr& csr, const W& weights,
                                  const TickOut& out, const Out& product, cudaStream_t stream) {
-  auto kernel = csr_batch_kernel<BT, UPDATE, W>;
+  auto kernel = csr_batch_kernel<BT, G, UPDATE, VEC, W>;
   static int occupancy[64] = {0};
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
@@ -234,7 +300,7 @@ cudaError_t launch_batch_variant(const TickArgs& t, const View& x, const Csr& cs
   if (err != cudaSuccess) return err;
   int& occ = occupancy[device & 63];
   if (occ == 0) occ = resident_blocks(kernel);
-  const int64_t rows_per_block = kThreads / 32;
+  const int64_t rows_per_block = kThreads / G;
   const int64_t needed = (t.neurons + rows_per_block - 1) / rows_per_block;
   const int64_t cap = static_cast<int64_t>(info.sm_count) * occ;
   const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, std::min(needed, cap))),
@@ -243,12 +309,30 @@ cudaError_t launch_batch_variant(const TickArgs& t, const View& x, const Csr& cs
   return cudaGetLastError();
 }
 
+template <int BT, bool UPDATE, typename W>
+cudaError_t dispatch_batch_tile(const TickArgs& t, const View& x, const Csr& csr, const W& w,
+                                const TickOut& out, const Out& product, cudaStream_t stream) {
+  // One vector load per (edge, batch tile) needs every tile full and its BT
+  // floats contiguous and BT * 4-byte aligned.
+  const bool vec = x.sb == 1 && x.sn % BT == 0 && t.batch % BT == 0 &&
+                   aligned(x.data, static_cast<uintptr_t>(BT) * 4);
+  // Lanes per row from the mean degree: each lane takes two edges per step.
+  const double degree = static_cast<double>(csr.n_edges) / static_cast<double>(std::max<int64_t>(t.neurons, 1));
+#define NSB_BATCH(G)                                                                          \
+  return vec ? launch_batch_variant<BT, G, UPDATE, true>(t, x, csr, w, out, product, stream)  \
+             : launch_batch_variant<BT, G, UPDATE, false>(t, x, csr, w, out, product, stream);
+  if (degree <= 24.0 && BT <= 8) { NSB_BATCH(8) }
+  if (degree <= 64.0) { NSB_BATCH(16) }
+  NSB_BATCH(32)
+#undef NSB_BATCH
+}
+
 template <bool UPDATE, typename W>
 cudaError_t dispatch_batch(const TickArgs& t, const View& x, const Csr& csr, const W& w,
                            const TickOut& out, const Out& product, cudaStream_t stream) {
-  if (t.batch <= 2) return launch_batch_variant<2, UPDATE>(t, x, csr, w, out, product, stream);
-  if (t.batch <= 4) return launch_batch_variant<4, UPDATE>(t, x, csr, w, out, product, stream);
-  return launch_batch_variant<8, UPDATE>(t, x, csr, w, out, product, stream);
+  if (t.batch <= 2) return dispatch_batch_tile<2, UPDATE>(t, x, csr, w, out, product, stream);
+  if (t.batch <= 4) return dispatch_batch_tile<4, UPDATE>(t, x, csr, w, out, product, stream);
+  return dispatch_batch_tile<8, UPDATE>(t, x, csr, w, out, product, stream);
 }
 
 template <bool UPDATE, typename W>
@@ -274,10 +358,6 @@ cudaError_t dispatch_group(const TickArgs& t, const View& x, const Csr& csr, con
     default: { NSB_BT(32) }
   }
 #undef NSB_BT
-}
-
-bool aligned(const void* p, uintptr_t bytes) {
-  return (reinterpret_cast<uintptr_t>(p) % bytes) == 0;
 }
 
 }  // namespace
