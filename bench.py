@@ -501,6 +501,15 @@ def run_native(args, workload: str) -> dict:
         "gpu_launches": 1 if tiled else steps,
         "clocks": sampler.summary(),
     }
+    if not args.skip_strong and workload == DEFAULT_WORKLOAD:
+        # The multi-GPU configuration's graph on this one GPU: the T(1) of the
+        # strong-scaling curve that the --gpus N lines continue.
+        cpu_graph_arrays = {f: getattr(graph, f).detach().cpu() for f in TOPOLOGY_FIELDS}
+        del runtime, graph
+        torch.cuda.empty_cache()
+        result["strong_scaling"] = strong_scaling_record(args, 1, 0, device)
+        from neurosim_gpu_b200 import SparseTopology
+        graph = SparseTopology(n_neurons=neurons, **cpu_graph_arrays)
     if not args.skip_cpu_baseline:
         rate_cpu, per_tick, ticks, cores = cpu_oracle_rate(graph, batch, seconds=args.cpu_seconds)
         port = {"value": rate_cpu, "unit": "synapse-updates/s", "cores": cores, "kind": "port",
@@ -614,6 +623,93 @@ def run_sharded_pels(args) -> dict:
     return result if rank == 0 else None
 
 
+STRONG_GRAPH = (1_330_000, 200_000_000)  # the scaled graph of the multi-GPU configuration
+
+
+def strong_scaling_record(args, world: int, rank: int, device) -> dict | None:
+    """The 1.33M / 200M graph (fp32, B = 1) on this run's ``world`` GPUs, so that
+    every line of a 1 -> N curve carries the same graph: ms/tick, synapse-updates/s
+    and the per-GPU HBM fraction.  One GPU: the single-GPU runtime; N GPUs: rows
+    split over the ranks with the fused peer exchange.  ``--steps`` ticks in one
+    persistent launch per rank, timed on the device (max over ranks), after an
+    L2 flush and a warm-up launch of the same length.  Rank 0 returns the record."""
+    import torch.distributed as dist
+
+    neurons, edges = STRONG_GRAPH
+    ticks = max(args.steps, 1)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world == 1:
+        graph = build_graph(neurons, edges, device)
+        m = graph.n_edges
+        runtime = NativeDendriticMatrixRuntime(graph, bench_model(neurons, device),
+                                               torch.zeros(1, neurons, device=device))
+        with torch.inference_mode():
+            runtime.run(ticks, 0.2, dendritic_drive=0.1)  # warm-up (builds the layout)
+            u, us = runtime._drive(0.2)
+            v, vs = runtime._drive(0.1, "dendritic_drive")
+            _, views = _outputs(3, runtime.state)
+            launch = runtime._prepare(runtime.state, runtime.dendritic_state,
+                                      runtime.adaptation_state, u, us, v, vs, views, ticks=ticks)
+            torch.cuda.synchronize()
+            flush.zero_()
+            e0.record()
+            launch()
+            e1.record()
+            e1.synchronize()
+            runtime.check_status()
+        tick_ms = e0.elapsed_time(e1) / ticks
+        rows, local_edges = neurons, m
+        layout = runtime._tiled_layout()
+        blocks = layout.blocks if layout is not None else None
+        path = runtime.kernel_path
+        del runtime, graph
+    else:
+        from neurosim_gpu_b200.sharded import ShardedDendriticMatrixRuntime, broadcast_graph
+        graph = broadcast_graph(neurons, edges, seed=0, device=device)
+        m = int(graph[1].numel())
+        runtime = ShardedDendriticMatrixRuntime(graph, bench_model(neurons, device),
+                                                torch.zeros(1, neurons, device=device))
+        with torch.inference_mode():
+            runtime.run(ticks, 0.2, dendritic_drive=0.1)  # warm-up (same launch length)
+            launch = (runtime.prepare_run(ticks, 0.2, dendritic_drive=0.1)
+                      if runtime.exchange == "peer" else None)
+            torch.cuda.synchronize()
+            dist.barrier()
+            flush.zero_()
+            e0.record()
+            if launch is not None:
+                launch()
+            else:
+                runtime.run(ticks, 0.2, dendritic_drive=0.1)
+            e1.record()
+            e1.synchronize()
+            runtime.check_status()
+        elapsed = torch.tensor([e0.elapsed_time(e1)], device=device)
+        dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
+        tick_ms = float(elapsed.item()) / ticks
+        rows, local_edges = runtime.shard.rows, runtime.local_edges
+        blocks = runtime.layout.blocks if runtime.layout is not None else None
+        path = f"{runtime.kernel_path}, {runtime.exchange} exchange"
+        runtime.release_graphs()
+        runtime.close()
+        del runtime, graph
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    peak, peak_kind = hbm_peak()
+    per_gpu = algorithmic_bytes(rows, local_edges, 1, "fp32")
+    return {"graph": "matrix_n1330k_m200M_b1_fp32", "neurons": neurons, "edges": m,
+            "n_gpus": world, "ticks": ticks, "ms_per_tick": tick_ms,
+            "value": m / (tick_ms * 1e-3), "unit": "synapse-updates/s",
+            "kernel_path": path, "column_blocks": blocks,
+            "rank0_rows": rows, "rank0_edges": local_edges,
+            "hbm_frac_per_gpu": per_gpu / (tick_ms * 1e-3) / 1e9 / peak,
+            "peak_source": peak_kind,
+            "note": "strong scaling: the same graph at every N; T(1) / T(N) is the speed-up"}
+
+
 def run_sharded(args, explicit_workload: bool) -> dict:
     """Row-sharded ticks on every rank of the torchrun job; rank 0 reports."""
     import datetime
@@ -641,12 +737,15 @@ def run_sharded(args, explicit_workload: bool) -> dict:
     runtime = ShardedDendriticMatrixRuntime(graph, model, torch.zeros(batch, neurons, device=device),
                                             precision=precision, exchange=args.exchange)
     chunk = 32
-    steps = max(args.steps - args.steps % chunk, chunk)
+    steps = max(args.steps, 1)  # exactly K ticks are timed
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
 
-    def timed(fn) -> float:
+    def timed(fn, flush_first: bool = False) -> float:
         dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if flush_first:
+            flush.zero_()
         e0.record()
         fn()
         e1.record()
@@ -657,11 +756,19 @@ def run_sharded(args, explicit_workload: bool) -> dict:
 
     with torch.inference_mode():
         runtime.run(max(args.warmup, chunk), 0.2, dendritic_drive=0.1, graph_ticks=chunk)
+        runtime.run(steps, 0.2, dendritic_drive=0.1, graph_ticks=chunk)  # same length, untimed
         torch.cuda.synchronize()
         sampler = ClockSampler(local_rank) if rank == 0 else None
         if sampler:
             sampler.__enter__()
-        total_ms = timed(lambda: runtime.run(steps, 0.2, dendritic_drive=0.1, graph_ticks=chunk))
+        if runtime.exchange == "peer":
+            # The persistent launch is prepared (a cross-rank barrier, argument
+            # checks) before the timed region; an L2 flush precedes it.
+            launch = runtime.prepare_run(steps, 0.2, dendritic_drive=0.1)
+            total_ms = timed(launch, flush_first=True)
+        else:
+            total_ms = timed(lambda: runtime.run(steps, 0.2, dendritic_drive=0.1,
+                                                 graph_ticks=chunk), flush_first=True)
         if sampler:
             sampler.__exit__(None, None, None)
         tick_ms = total_ms / steps
@@ -708,7 +815,13 @@ def run_sharded(args, explicit_workload: bool) -> dict:
     }
     runtime.release_graphs()
     runtime.close()
+    del runtime, graph
     torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if not args.skip_strong:
+        strong = strong_scaling_record(args, world, rank, device)
+        if strong is not None:
+            result["strong_scaling"] = strong
     dist.barrier()
     dist.destroy_process_group()
     return result
@@ -812,6 +925,8 @@ def main() -> None:
     parser.add_argument("--workload", choices=sorted(WORKLOADS), default=None)
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--skip-cpu-baseline", action="store_true")
+    parser.add_argument("--skip-strong", action="store_true",
+                        help="leave out the 1.33M / 200M strong-scaling record")
     parser.add_argument("--kernel", choices=("auto", "csr", "tiled", "cluster"), default="auto",
                         help="matrix tick path (auto: cluster for small graphs, tiled at B = 1)")
     parser.add_argument("--exchange", choices=("auto", "nccl", "peer"), default="auto",

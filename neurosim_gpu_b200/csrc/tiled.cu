@@ -504,10 +504,18 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
       // L2 prefetch of this tick's tasks, kPrefetchAhead tasks ahead of the
       // hand-out counter, then of the next tick's first round (one task per
       // consumer warp), which keeps DRAM busy across the barriers and the update.
+      // Tasks that consumers already took are prefetched too: the prefetched
+      // lines enter L2 at normal priority, unlike the evict-first stream, so
+      // part of this tick's edges is still in L2 for the next tick (at 166k /
+      // 25M fp32 that saves a third of the DRAM reads).  Once every task has
+      // been handed out the backlog is dropped, so this warp never holds the
+      // CTA back from the grid barrier (layouts of many short tasks).
       const volatile int* handed = next_task;
       long long polls = 0;
       while (prefetched < task_count) {
-        const int limit = min(task_count, __shfl_sync(0xffffffffu, *handed, 0) + L.prefetch_ahead);
+        const int taken = __shfl_sync(0xffffffffu, *handed, 0);
+        if (taken >= task_count + kConsumerWarps) break;  // every consumer found the list empty
+        const int limit = min(task_count, taken + L.prefetch_ahead);
         if (prefetched >= limit) {
           if (++polls > kWaitLimit) {  // consumers stalled: stop prefetching
             if (lane == 0) atomicExch(st, 5);
@@ -516,7 +524,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
           __nanosleep(256);
           continue;
         }
-        prefetch_upto(limit);
+        prefetch_upto(min(limit, prefetched + 32));  // one round, then look again
       }
       prefetched = 0;
       if (tick + 1 < ticks) prefetch_upto(min(task_count, L.prefetch_first));

@@ -141,6 +141,7 @@ class ShardedDendriticMatrixRuntime:
         self.precision = precision
         self.status = _tiled.status_word(device)
         self._graphs: dict = {}
+        self._rollout_plan = None
         self._tick = 0
 
         rowptr = in_rowptr.to(torch.int64)
@@ -230,6 +231,7 @@ class ShardedDendriticMatrixRuntime:
 
     def close(self) -> None:
         """Unmap the other ranks' buffers (collective: every rank calls it)."""
+        self._rollout_plan = None  # its argument blocks point into the peers' buffers
         if self._peer is not None:
             torch.cuda.synchronize(self.shard.device)
             dist.barrier(group=self.group)
@@ -312,6 +314,20 @@ class ShardedDendriticMatrixRuntime:
     def _run_peer(self, ticks: int, drive, dendritic_drive) -> torch.Tensor:
         """All ``ticks`` ticks in one cooperative launch per rank, exchanging the
         soma vector inside the kernel (peer stores + a cross-GPU barrier)."""
+        self.prepare_run(ticks, drive, dendritic_drive=dendritic_drive)()
+        return self.state
+
+    def prepare_run(self, ticks: int, drive=0.0, *, dendritic_drive=0.0):
+        """A callable that enqueues :meth:`run`'s single persistent launch of
+        ``ticks`` ticks (peer exchange only; every rank prepares and calls it).
+
+        The preparation -- a synchronisation with every rank's earlier work on
+        the gathered buffers, a barrier, argument checks -- happens here, so
+        the callable itself only launches.  The runtime's state advances when
+        the callable is called.
+        """
+        if self._peer is None or ticks < 1:
+            raise ValueError("prepare_run needs the peer exchange and ticks >= 1")
         u, us, v, vs = self._drives(drive, dendritic_drive)
         # Every rank's earlier work on the gathered buffers (NCCL exchanges of
         # step()) must be finished before any rank's kernel writes into them.
@@ -320,15 +336,19 @@ class ShardedDendriticMatrixRuntime:
         s_rows = self.shard.own(self.shard.current)
         out_d = torch.empty_like(self.dendritic_state)
         out_a = torch.empty_like(self.adaptation_state)
-        self.extension.prepare_run_tiled_peers(
+        launch = self.extension.prepare_run_tiled_peers(
             s_rows, self.dendritic_state, self.adaptation_state, self.params, self.layout,
             u, us, v, vs, out=(s_rows, out_d, out_a), ticks=ticks, exchange=self._exchange(),
-            status=self.status)()
-        self.dendritic_state, self.adaptation_state = out_d, out_a
-        self.shard.current = (self.shard.current + ticks) % 2
-        self._peer_epoch += ticks
-        self._tick += ticks
-        return self.state
+            status=self.status)
+
+        def run() -> None:
+            launch()
+            self.dendritic_state, self.adaptation_state = out_d, out_a
+            self.shard.current = (self.shard.current + ticks) % 2
+            self._peer_epoch += ticks
+            self._tick += ticks
+
+        return run
 
     def stream(self, drives: torch.Tensor, out: torch.Tensor | None = None, *,
                dendritic_drive=0.0) -> torch.Tensor:
@@ -376,53 +396,17 @@ class ShardedDendriticMatrixRuntime:
         return out
 
     def _stream_peer(self, drives, out, dendritic_drive) -> None:
-        device = self.shard.device
-        rows = self.shard.rows
         _, _, v, vs = self._drives(0.0, dendritic_drive)
-        # As in _run_peer: earlier NCCL exchanges end on every rank first.
-        torch.cuda.current_stream(device).synchronize()
+        # As in prepare_run: earlier NCCL exchanges end on every rank first.
+        torch.cuda.current_stream(self.shard.device).synchronize()
         dist.barrier(group=self.group)
         chunks = _tiled.rollout_chunks(drives.shape[0])
-        widest = max(chunks)
-        d, a = self.dendritic_state.clone(), self.adaptation_state.clone()
-        drive_ring = [torch.empty((widest, 1, rows), device=device) for _ in range(2)]
-        history = [torch.empty((widest, 1, rows), device=device) for _ in range(2)]
-        compute = torch.cuda.current_stream(device)
-        upload = torch.cuda.Stream(device=device)
-        download = torch.cuda.Stream(device=device)
-        uploaded = [torch.cuda.Event() for _ in range(2)]
-        consumed = [torch.cuda.Event() for _ in range(2)]  # launch done with ring slot k
-        saved = [torch.cuda.Event() for _ in range(2)]     # history[k] downloaded
-        upload.wait_stream(compute)
-        download.wait_stream(compute)
-        lo = 0
-        for c, length in enumerate(chunks):
-            k, hi = c % 2, lo + length
-            with torch.cuda.stream(upload):
-                if c >= 2:
-                    upload.wait_event(consumed[k])
-                drive_ring[k][:length].copy_(drives[lo:hi], non_blocking=True)
-                uploaded[k].record(upload)
-            compute.wait_event(uploaded[k])
-            if c >= 2:
-                compute.wait_event(saved[k])
-            s_rows = self.shard.own(self.shard.current)
-            self.extension.prepare_run_tiled_peers(
-                s_rows, d, a, self.params, self.layout, drive_ring[k][0], 0.0, v, vs,
-                out=(s_rows, d, a), ticks=length, exchange=self._exchange(), status=self.status,
-                rollout=(rows, history[k][:length]))()
-            self.shard.current = (self.shard.current + length) % 2
-            self._peer_epoch += length
-            self._tick += length
-            consumed[k].record(compute)
-            with torch.cuda.stream(download):
-                download.wait_event(consumed[k])
-                out[lo:hi].copy_(history[k][:length], non_blocking=True)
-                saved[k].record(download)
-            lo = hi
-        compute.wait_stream(download)
-        compute.wait_stream(upload)
-        self.dendritic_state, self.adaptation_state = d, a
+        key = (None if v is None else (v.data_ptr(), v.stride()), vs)
+        plan = self._rollout_plan
+        if plan is None or plan.key != key or plan.capacity < max(chunks):
+            plan = self._rollout_plan = _ShardedRolloutPlan(
+                self, key, max(_tiled.ROLLOUT_CAP, *chunks), v, vs)
+        self.dendritic_state, self.adaptation_state = plan.run(self, drives, out, chunks)
 
     def _run_graph(self, ticks: int, drive, dendritic_drive, graph_ticks: int) -> torch.Tensor:
         """``ticks`` ticks with fixed drives, replaying a CUDA graph of ticks + all-gathers."""
@@ -489,6 +473,85 @@ class ShardedDendriticMatrixRuntime:
         parts = [torch.empty_like(padded) for _ in range(self.world)]
         dist.all_gather(parts, padded.contiguous(), group=self.group)
         return torch.cat(parts, dim=1)[:, : self.neurons]
+
+
+class _ShardedRolloutPlan:
+    """What one rank's streamed rollouts reuse from call to call: the two copy
+    streams and their events, the rings of drives and soma history, the
+    running dendrite / adaptation rows, one peer-exchange argument block per
+    parity of the gathered buffers and a prepared launch per (ring slot, launch
+    length, parity).  Only the exchange's epoch changes between launches; it is
+    written into the argument block just before each launch.
+    """
+
+    def __init__(self, runtime: ShardedDendriticMatrixRuntime, key, capacity: int, v, vs) -> None:
+        device = runtime.shard.device
+        rows = runtime.shard.rows
+        self.key, self.capacity, self.v, self.vs = key, capacity, v, vs
+        self.device = device
+        self.d = torch.empty_like(runtime.dendritic_state)
+        self.a = torch.empty_like(runtime.adaptation_state)
+        self.drive_ring = [torch.empty((capacity, 1, rows), device=device) for _ in range(2)]
+        self.history = [torch.empty((capacity, 1, rows), device=device) for _ in range(2)]
+        self.upload = torch.cuda.Stream(device=device)
+        self.download = torch.cuda.Stream(device=device)
+        self.uploaded = [torch.cuda.Event() for _ in range(2)]
+        self.consumed = [torch.cuda.Event() for _ in range(2)]  # launch done with ring slot k
+        self.saved = [torch.cuda.Event() for _ in range(2)]     # history[k] downloaded
+        current = runtime.shard.current
+        self.exchange = []
+        for parity in range(2):
+            runtime.shard.current = parity
+            self.exchange.append(runtime._exchange())
+        runtime.shard.current = current
+        self.calls: dict[tuple[int, int, int], object] = {}
+
+    def call(self, runtime: ShardedDendriticMatrixRuntime, k: int, length: int, parity: int):
+        launch = self.calls.get((k, length, parity))
+        if launch is None:
+            rows = runtime.shard.rows
+            s_rows = runtime.shard.own(parity)
+            launch = runtime.extension.prepare_run_tiled_peers(
+                s_rows, self.d, self.a, runtime.params, runtime.layout, self.drive_ring[k][0],
+                0.0, self.v, self.vs, out=(s_rows, self.d, self.a), ticks=length,
+                exchange=self.exchange[parity], status=runtime.status,
+                rollout=(rows, self.history[k][:length]))
+            self.calls[k, length, parity] = launch
+        return launch
+
+    def run(self, runtime: ShardedDendriticMatrixRuntime, drives, out, chunks):
+        compute = torch.cuda.current_stream(self.device)
+        upload, download = self.upload, self.download
+        self.d.copy_(runtime.dendritic_state)
+        self.a.copy_(runtime.adaptation_state)
+        upload.wait_stream(compute)
+        download.wait_stream(compute)
+        lo = 0
+        for c, length in enumerate(chunks):
+            k, hi = c % 2, lo + length
+            with torch.cuda.stream(upload):
+                if c >= 2:
+                    upload.wait_event(self.consumed[k])
+                self.drive_ring[k][:length].copy_(drives[lo:hi], non_blocking=True)
+                self.uploaded[k].record(upload)
+            compute.wait_event(self.uploaded[k])
+            if c >= 2:
+                compute.wait_event(self.saved[k])
+            parity = runtime.shard.current
+            self.exchange[parity].epoch = runtime._peer_epoch
+            self.call(runtime, k, length, parity)()
+            runtime.shard.current = (parity + length) % 2
+            runtime._peer_epoch += length
+            runtime._tick += length
+            self.consumed[k].record(compute)
+            with torch.cuda.stream(download):
+                download.wait_event(self.consumed[k])
+                out[lo:hi].copy_(self.history[k][:length], non_blocking=True)
+                self.saved[k].record(download)
+            lo = hi
+        compute.wait_stream(download)
+        compute.wait_stream(upload)
+        return self.d.clone(), self.a.clone()
 
 
 def broadcast_graph(neurons: int, edges: int, *, seed: int, device: torch.device, group=None):
