@@ -16,7 +16,9 @@ the CUDA tick consumes are the ones the reference builds:
 ``random_topology`` draws exactly the reference's random stream (``randint``
 for sources, ``randint`` for destinations, ``randn`` for weights, one
 ``torch.Generator`` seeded with ``seed``), so a graph built here equals the
-reference graph bit for bit (checked against SHA-256 fixtures).  A
+reference graph bit for bit: tests/test_topology_golden.py compares the SHA-256
+of every array with the reference's digests, for CPU and CUDA
+canonicalisation up to the 1.33M-neuron, 200M-edge graph.  A
 ``build_device`` may differ from the generator device: the random draws stay
 on the generator device and the sort / coalesce runs on ``build_device``
 (for example CPU draws, CUDA canonicalisation of a 200M-edge graph).
