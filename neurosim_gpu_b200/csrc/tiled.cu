@@ -299,6 +299,7 @@ struct TiledArgs {
   int32_t prefetch_first;      // tasks of the next tick's first round prefetched (0 or warps)
   int32_t splits;              // sub-task planes per block
   int32_t split_chunks;        // chunks of one sub-task
+  int32_t stage_rows;          // staged update: rows per chunk (a multiple of 4; 0: loads)
   int64_t rows;                // destination rows
   int64_t cols;                // length of the gathered source vector
 };
@@ -396,6 +397,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);            // [2]
   uint64_t* empty = full + 2;                                         // [2]
   int* next_task = reinterpret_cast<int*>(empty + 2);
+  uint64_t* upd = empty + 3;                                          // staged update
   float* sbuf = reinterpret_cast<float*>(smem_raw + kTiledHeader);    // [nbuf][cb_pad]
   int* st = status ? status : &g_tiled_status;
   // A gated launch whose count is below its minimum leaves at once: every CTA
@@ -412,8 +414,10 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
   const int task_first = L.task_ptr[c];
   const int task_count = L.task_ptr[c + 1] - task_first;
   const int uses = ticks * stages;  // stage uses of this launch, in order
-  const int64_t update_lo = L.rows * c / gridDim.x;
-  const int64_t update_hi = L.rows * (c + 1) / gridDim.x;
+  // Update rows of this CTA; a staged update needs them in groups of 4 (rows % 4 == 0).
+  const int64_t update_lo = L.stage_rows ? 4 * ((L.rows >> 2) * c / gridDim.x) : L.rows * c / gridDim.x;
+  const int64_t update_hi =
+      L.stage_rows ? 4 * ((L.rows >> 2) * (c + 1) / gridDim.x) : L.rows * (c + 1) / gridDim.x;
 
   if (threadIdx.x < 4 * nbuf) sbuf[(threadIdx.x >> 2) * cb_pad + L.block_cols + (threadIdx.x & 3)] = 0.0f;
   if (threadIdx.x == 0) {
@@ -421,6 +425,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
       mbar_init(full + b, 1);
       mbar_init(empty + b, kConsumerWarps);
     }
+    mbar_init(upd, 1);
     *next_task = kConsumerWarps;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -441,6 +446,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
   // that counter, and the next tick's first round before the tick ends, so
   // DRAM keeps streaming through the barriers and the update.
   int prefetched = 0;  // producer: tasks of the current tick already prefetched
+  int upd_uses = 0;    // completed phases of the staged-update mbarrier
   // Consumer bookkeeping of stage uses (running over all ticks of the launch).
   int waited = -1;  // highest use whose full barrier this warp has observed
   int current = 0;  // lowest use this warp has not left yet
@@ -652,6 +658,63 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
     if (threadIdx.x == 0) *next_task = kConsumerWarps;
     grid_barrier(L.barrier, st);  // every row sum of this tick is in part
 
+    const int planes = static_cast<int>((L.cols + L.block_cols - 1) / L.block_cols) * L.splits;
+    if (L.stage_rows > 0 && update) {
+      // Staged update: the state block in shared memory is free until the
+      // next tick's staging, so thread 0 bulk-copies the operands of a chunk
+      // of this CTA's rows there -- the parameter vectors, s, d, a and every
+      // row-sum plane, contiguous runs of 16-byte multiples -- and the threads
+      // update the rows from shared memory: one bulk round trip per chunk
+      // instead of a round of dependent L2 loads per 1,024 rows.
+      const int cap = L.stage_rows;
+      float* op = sbuf;  // [6 params | s | d | a | planes][cap]
+      for (int64_t c0 = update_lo; c0 < update_hi; c0 += cap) {
+        const int rc = static_cast<int>(min(static_cast<int64_t>(cap), update_hi - c0));
+        if (threadIdx.x == 0) {
+          // Generic writes (the previous tick's d, a and s by this CTA, the
+          // row sums by every CTA) before the async-proxy reads; generic
+          // reads of shared memory before its async-proxy writes.
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          fence_proxy_async_smem();
+          const uint32_t bytes = static_cast<uint32_t>(rc) * 4u;
+          int copies = 3 + planes;
+          for (int i = 0; i < 6; ++i) copies += t.p.stride[i] != 0;
+          mbar_arrive_expect_tx(upd, bytes * static_cast<uint32_t>(copies));
+          for (int i = 0; i < 6; ++i)  // a parameter broadcast from one value is read directly
+            if (t.p.stride[i] != 0) bulk_copy_to_smem(op + i * cap, t.p.data[i] + c0, bytes, upd);
+          const float* s_src = exchange ? px.gathered[px.rank][tick & 1] + px.row_offset + c0
+                               : tick == 0 ? t.s.data + c0 : out.s.data + c0;
+          bulk_copy_to_smem(op + 6 * cap, s_src, bytes, upd);
+          bulk_copy_to_smem(op + 7 * cap, (tick == 0 ? t.d.data : out.d.data) + c0, bytes, upd);
+          bulk_copy_to_smem(op + 8 * cap, (tick == 0 ? t.a.data : out.a.data) + c0, bytes, upd);
+          for (int k = 0; k < planes; ++k)
+            bulk_copy_to_smem(op + (9 + k) * cap, L.part + k * L.rows + c0, bytes, upd);
+        }
+        if (!mbar_wait(upd, upd_uses & 1)) atomicExch(st, 9);
+        ++upd_uses;
+        auto param = [&](int k, int i) {
+          return t.p.stride[k] != 0 ? op[k * cap + i] : __ldg(t.p.data[k]);
+        };
+        for (int i = threadIdx.x; i < rc; i += blockDim.x) {
+          const int64_t n = c0 + i;
+          float j = op[9 * cap + i];  // (block, split) order: ((p0 + p1) + p2) + ...
+          for (int k = 1; k < planes; ++k) j = j + op[(9 + k) * cap + i];
+          for (int k = 0; k < planes; ++k) L.part[n + k * L.rows] = 0.0f;
+          const Update q = advance(j, op[6 * cap + i], op[7 * cap + i], op[8 * cap + i],
+                                   t.u.at(tick, n), t.v.at(0, n), param(0, i), param(1, i),
+                                   param(2, i), param(3, i), param(4, i), param(5, i));
+          if (exchange) {
+            for (int p = 0; p < px.world; ++p) px.gathered[p][(tick + 1) & 1][px.row_offset + n] = q.s;
+          } else {
+            out.s.put(0, n, q.s);
+          }
+          out.d.put(0, n, q.d);
+          out.a.put(0, n, q.a);
+          if (product.data) product.put(tick, n, q.s);  // a rollout's soma history
+        }
+        __syncthreads();  // the chunk's operands are read before the next copies
+      }
+    } else
     // Update of rows [update_lo, update_hi), one row per thread per round:
     // every operand of the row is loaded before any store, so a round costs
     // one memory round trip.  The row sums and the state written by earlier
@@ -659,7 +722,6 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
     // save a round for the few threads with a second row, but its operands
     // raise the kernel's register need, and the spills that follow slow the
     // streaming loop: 41.0 against 37.6 us per tick at 166k / 25M fp32.)
-    const int planes = static_cast<int>((L.cols + L.block_cols - 1) / L.block_cols) * L.splits;
     for (int64_t n0 = update_lo + threadIdx.x; n0 < update_hi; n0 += blockDim.x) {
       float j[1], s0[1], d0[1], a0[1], u[1], v[1], pr[1][6];
 #pragma unroll
@@ -838,6 +900,30 @@ cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, cons
                                     std::min(4096.0, kPrefetchBudget / std::max(task_bytes, 1.0)))
                               : 0;
   L.prefetch_first = prefetch ? kConsumerWarps : 0;
+  // Staged update (the tick's row operands bulk-copied into the idle state
+  // buffer): every operand a contiguous, 16-byte aligned vector and the rows a
+  // multiple of 4 (so each CTA's rows and every plane start on 16 bytes).
+  L.stage_rows = 0;
+  if (update && !gate.count && layout.rows % 4 == 0) {
+    auto ok = [](const void* p, int64_t stride) {
+      return p != nullptr && stride == 1 && reinterpret_cast<uintptr_t>(p) % 16 == 0;
+    };
+    auto ok_param = [&](const float* p, int64_t stride) { return p != nullptr && (stride == 0 || ok(p, stride)); };
+    bool staged = ok(t.d.data, t.d.sn) && ok(t.a.data, t.a.sn) && ok(out.d.data, out.d.sn) &&
+                  ok(out.a.data, out.a.sn);
+    for (int i = 0; i < 6; ++i) staged = staged && ok_param(t.p.data[i], t.p.stride[i]);
+    if (exchange) {
+      staged = staged && exchange->row_offset % 4 == 0;
+      for (int p = 0; p < exchange->world; ++p)
+        staged = staged && ok(exchange->gathered[p][0], 1) && ok(exchange->gathered[p][1], 1);
+    } else {
+      staged = staged && ok(t.s.data, t.s.sn) && (ticks == 1 || ok(out.s.data, out.s.sn));
+    }
+    const int64_t planes = static_cast<int64_t>(layout.blocks) * layout.splits;
+    const int64_t floats = static_cast<int64_t>(layout.buffers) * (layout.block_cols + 4);
+    const int64_t cap = floats / (9 + planes) / 4 * 4;
+    if (staged && cap >= 64) L.stage_rows = static_cast<int32_t>(std::min<int64_t>(cap, 1 << 20));
+  }
   const int ctas = layout.ctas;
   if (gate.count) {  // the hybrid PELS propagate: float32 weights only (checked by the caller)
     return launch_tiled_kernel<ChunkF32, 4, false, true>(

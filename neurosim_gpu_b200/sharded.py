@@ -1,7 +1,8 @@
 """Row-sharded matrix tick across the GPUs of one node (one process per GPU).
 
 Destination rows are cut into ``world`` equal ranges: rank r owns rows
-``[r*R, min(N, (r+1)*R))`` with ``R = ceil(N / world)``.  Every tick each rank
+``[r*R, min(N, (r+1)*R))`` with ``R = ceil(N / world)`` rounded up to a
+multiple of 4.  Every tick each rank
 
 1. runs the native tick on its own rows, gathering from the full soma vector
    ``x`` (all N neurons, laid out ``[world*R, B]`` so neuron n sits at row n on
@@ -44,7 +45,9 @@ class RowShard:
     device: torch.device
 
     def __post_init__(self) -> None:
-        self.rows_per_rank = math.ceil(self.neurons / self.world)
+        # A multiple of 4 rows per rank keeps every rank's first row and its
+        # slices of the state 16-byte aligned (bulk copies in the tick kernel).
+        self.rows_per_rank = 4 * math.ceil(self.neurons / self.world / 4)
         self.lo = min(self.neurons, self.rank * self.rows_per_rank)
         self.hi = min(self.neurons, self.lo + self.rows_per_rank)
         self.cols = self.world * self.rows_per_rank
