@@ -62,9 +62,10 @@ WARPS = 31                    # consumer warps of a CTA
 # Split length of sub-tasks in chunks (4 edges), by weight format (0: tasks
 # are not split).  Splitting shortens the tail of a tick but adds row-sum
 # planes that the update reads; measured at 166k / 25M it pays off for fp32
-# (39.7 vs 42.6 us with splits of 9 chunks) and costs the narrower formats
-# (fp16 30.6 vs 33.7 us).  A constant length cuts every row at the same edges
-# whatever rows a layout holds, so sharded sums stay bit-identical.
+# (36.9 vs 38.8 us with splits of 9 chunks) and costs the narrower formats
+# (fp16 32.1 vs 30.5 us, NVFP4 38.5 vs 33.8 us).  A constant length cuts every
+# row at the same edges whatever rows a layout holds, so sharded sums stay
+# bit-identical.
 SPLIT_CHUNKS = {native.F32: 9, native.F16: 0, native.E4M3: 0, native.NVFP4: 0}
 MAX_PLANES = 32               # cap on blocks x splits (only degree-skewed graphs reach it)
 
@@ -337,9 +338,16 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
         task_rows[pair_task, pair_lane] = pair_row
         tiled_weight = torch.zeros(slots, dtype=weight.dtype, device=device)
         tiled_weight[slot] = weight
-    # Sub-tasks: chunks [h * split, (h + 1) * split) of a task.
+    # Sub-tasks: chunks [h * split, (h + 1) * split) of a task.  Splitting
+    # only pays when a mean row piece (edges per (row, block)) is longer than
+    # one split (166k / 25M fp32: 50 edges per piece, 36.9 vs 38.8 us with
+    # splits of 9 chunks; 166k / 10M: 20 edges, 19.2 unsplit vs 19.7 us).  The
+    # mean is a property of the graph's density, so the row blocks of a
+    # sharded graph decide as the whole graph does.
     longest = int(task_chunks.max()) if n_tasks else 1
     split = SPLIT_CHUNKS.get(fmt, 0)
+    if split > 0 and m < split * CHUNK * n * blocks:
+        split = 0
     if split > 0:
         if blocks * -(-longest // split) > MAX_PLANES:  # a degree-skewed graph
             split = -(-longest // max(1, MAX_PLANES // blocks))

@@ -233,8 +233,9 @@ def test_in_kernel_decoders_exhaustive():
 
 
 def test_sharded_layouts_split_rows_like_the_whole_graph_cpu():
-    """Split points depend only on the graph, not on which rows a layout holds."""
-    n, m = 9001, 600000
+    """Split points depend only on the graph, not on which rows a layout holds
+    (a graph dense enough for split sub-tasks: ~55 edges per row piece)."""
+    n, m = 9001, 2000000
     graph = random_topology(n, m, device="cpu", seed=6)
     rowptr = graph.in_rowptr.long()
     smem = _smem_bytes()
