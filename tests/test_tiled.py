@@ -250,3 +250,37 @@ def test_sharded_layouts_split_rows_like_the_whole_graph_cpu():
                                   smem_bytes=smem)
         assert (part.blocks, part.block_cols, part.split_chunks) == \
             (whole.blocks, whole.block_cols, whole.split_chunks)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["fp32", "nvfp4"])
+@pytest.mark.parametrize("rows_per_cta", [None, 40])
+def test_staged_update_equals_direct_update_bitwise(fmt, rows_per_cta):
+    """The update after the grid barrier reads its operands through shared
+    memory (bulk copies, when every operand is a contiguous 16-byte aligned
+    vector) or straight from L2 (strided parameters): same states bit for bit,
+    over several ticks of one launch and with more rows per CTA than one
+    staged chunk holds (small shared memory: the rows go in several chunks)."""
+    ext = load_native_extension()
+    n = 8000  # a multiple of 4
+    graph = random_topology(n, 240000, device="cpu", seed=21).to("cuda")
+    weight, scales, scale, _ = _packed(graph, fmt)
+    smem = 232448 if rows_per_cta is None else 12000
+    layout = build_tiled_layout(graph.in_rowptr, graph.in_col, weight, neurons=n,
+                                ctas=8 if rows_per_cta is None else n // rows_per_cta // 25,
+                                smem_limit=smem, block_scales=scales, global_scale=scale)
+    model = bench_model(n)
+    contiguous = [p.contiguous().clone() for p in model.parameters()]
+    strided = [torch.empty(2 * n, device="cuda")[::2].copy_(p) for p in contiguous]
+    s0 = torch.rand(1, n, generator=torch.Generator().manual_seed(5)).cuda()
+    results = []
+    for params in (contiguous, strided):
+        out = [torch.empty_like(s0) for _ in range(3)]
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        ext.prepare_step_tiled(s0, torch.zeros_like(s0), torch.zeros_like(s0), params, layout,
+                               None, 0.2, None, 0.1, out=out, status=status, ticks=9)()
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        results.append(out)
+    for got, want in zip(*results):
+        assert torch.equal(got, want)
