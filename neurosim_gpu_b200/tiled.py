@@ -451,7 +451,7 @@ __all__ = ["TiledLayout", "build_tiled_layout", "emulate", "plan_blocks", "cta_r
 ROLLOUT_CAP = 32  # longest launch of a streamed rollout on the tiled path
 
 
-def rollout_chunks(ticks: int, cap: int = ROLLOUT_CAP, first: int = 1) -> list[int]:
+def rollout_chunks(ticks: int, cap: int = ROLLOUT_CAP, first: int = 2) -> list[int]:
     """Launch lengths of a streamed rollout of ``ticks`` ticks: ``first``, then
     doubling up to ``cap``-tick launches, then halving back down, so that the
     upload before the first launch and the download after the last one are
