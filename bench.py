@@ -836,6 +836,9 @@ def run_profile(args, workload: str) -> None:
     """
     neurons, edges, batch, precision = WORKLOADS[workload]
     device = torch.device("cuda", 0)
+    if args.profile_shard:
+        run_profile_shard(args, workload, device)
+        return
     graph = build_graph(neurons, edges, device)
     runtime = NativeDendriticMatrixRuntime(graph, bench_model(neurons, device),
                                            torch.zeros(batch, neurons, device=device),
@@ -852,6 +855,90 @@ def run_profile(args, workload: str) -> None:
     torch.cuda.synchronize()
     print(json.dumps({"profile": workload, "ticks": args.warmup + args.steps,
                       "state_mean": float(runtime.state.mean())}))
+
+
+def run_profile_shard(args, workload: str, device) -> None:
+    """``--profile-shard R/W``: rank R's share of a W-way row split of the
+    workload's graph, built and launched on one GPU (the rank's tiled tick with
+    no exchange: what each rank of a W-GPU run launches, minus the peer stores).
+    Only the rank's destination CSR and layout stay on the device."""
+    from neurosim_gpu_b200.sharded import ShardedDendriticMatrixRuntime
+
+    rank, world = (int(v) for v in args.profile_shard.split("/"))
+    neurons, edges, batch, precision = WORKLOADS[workload]
+    graph = build_graph(neurons, edges, device)
+    csr = (graph.in_rowptr.to(device), graph.in_col.to(device), graph.in_weight.to(device))
+    del graph
+    runtime = ShardedDendriticMatrixRuntime(csr, bench_model(neurons, device),
+                                            torch.zeros(batch, neurons, device=device),
+                                            precision=precision, rank=rank, world=world)
+    del csr
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()  # release the graph build's blocks before the captured launches
+    with torch.inference_mode():
+        if args.launch_ticks > 1:
+            us_per_tick = _profile_shard_runs(args, runtime)
+        else:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            for i in range(args.warmup + args.steps):
+                if i == args.warmup:
+                    e0.record()
+                runtime.finish(runtime.local_step(0.2, dendritic_drive=0.1))
+            e1.record()
+            e1.synchronize()
+            us_per_tick = e0.elapsed_time(e1) * 1e3 / max(args.steps, 1)
+    torch.cuda.synchronize()
+    runtime.check_status()
+    layout = runtime.layout
+    print(json.dumps({"profile": workload, "shard": args.profile_shard,
+                      "rows": runtime.shard.rows, "edges": runtime.local_edges,
+                      "kernel_path": runtime.kernel_path,
+                      "column_blocks": layout.blocks if layout is not None else None,
+                      "splits": layout.splits if layout is not None else None,
+                      "slots": layout.n_slots if layout is not None else None,
+                      "padding_fraction": layout.padding_fraction if layout is not None else None,
+                      "ticks_per_launch": args.launch_ticks,
+                      "us_per_tick_diagnostic": us_per_tick,
+                      "launches": args.warmup + args.steps,
+                      "state_mean": float(runtime.state.mean())}))
+
+
+def _profile_shard_runs(args, runtime) -> float:
+    """Persistent launches of ``--launch-ticks`` ticks of one rank's share with
+    the in-kernel exchange over a world of one: the rank stores its rows' new
+    state into its own gathered buffer only and its end-of-tick barrier counts
+    its own arrivals, so every other step of an N-GPU rank's launch runs as it
+    does there (the stores to N - 1 peers and the wait for them excepted)."""
+    from neurosim_gpu_b200.native import _PeerExchange
+
+    shard = runtime.shard
+    counter = torch.zeros(32, dtype=torch.int64, device=shard.device)
+    u, us, v, vs = runtime._drives(0.2, 0.1)
+    epoch = 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(args.warmup + args.steps):
+        if i == args.warmup:
+            e0.record()
+        x = _PeerExchange()
+        x.world, x.rank, x.row_offset = 1, 0, shard.lo
+        cur = shard.current
+        x.gathered[0][0] = shard.buffers[cur].data_ptr()
+        x.gathered[0][1] = shard.buffers[1 - cur].data_ptr()
+        x.counters[0] = counter.data_ptr()
+        x.epoch = epoch
+        s_rows = shard.own(cur)
+        out_d = torch.empty_like(runtime.dendritic_state)
+        out_a = torch.empty_like(runtime.adaptation_state)
+        runtime.extension.prepare_run_tiled_peers(
+            s_rows, runtime.dendritic_state, runtime.adaptation_state, runtime.params,
+            runtime.layout, u, us, v, vs, out=(s_rows, out_d, out_a), ticks=args.launch_ticks,
+            exchange=x, status=runtime.status)()
+        runtime.dendritic_state, runtime.adaptation_state = out_d, out_a
+        shard.current = (cur + args.launch_ticks) % 2
+        epoch += args.launch_ticks
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / max(args.steps * args.launch_ticks, 1)
 
 
 def run_profile_suite(args) -> None:
@@ -935,6 +1022,8 @@ def main() -> None:
                         help="eager launches only, for ncu captures (prints no bench line)")
     parser.add_argument("--profile-suite", action="store_true",
                         help="two launches of each non-headline kernel on small cases, for ncu")
+    parser.add_argument("--profile-shard", default=None, metavar="R/W",
+                        help="with --profile: rank R's share of a W-way row split, on one GPU")
     parser.add_argument("--launch-ticks", type=int, default=1,
                         help="with --profile: ticks per launch of the persistent tiled kernel")
     args = parser.parse_args()

@@ -45,7 +45,7 @@ extern "C" {
 #define NSB_API
 #endif
 
-#define NSB_ABI_VERSION 11
+#define NSB_ABI_VERSION 12
 
 enum nsb_status {
   NSB_OK = 0,
@@ -210,12 +210,17 @@ NSB_API int nsb_dendritic_event_noalloc(const nsb_tick* tick, float* current,
  *    and a range of destination rows; CTA c runs stages stage_ptr[c] ..
  *    stage_ptr[c+1]-1 (block stage_block[s]) with `buffers` (1 or 2) state
  *    blocks in shared memory.
- *  - Tasks of CTA c are task_ptr[c] .. task_ptr[c+1]-1.  A task is split h
- *    (h < splits) of 32 rows' pieces in the stage's block: the lanes' edges
- *    16*split_chunks*h + j, j < 4C.  tasks[4q..4q+3] = first slot, chunks C,
- *    stage (index among the CTA's stages) | h << 16, first scale pair.  Lane i
- *    owns row task_rows[32q+i] & 0x0FFFFFFF (0x0FFFFFFF: no row); its edge
- *    16*split_chunks*h + j sits at slot first + 128*(j/4) + 4*i + j%4.
+ *  - Tasks of CTA c are task_ptr[c] .. task_ptr[c+1]-1.  tasks[4q..4q+3] =
+ *    first slot, chunks C, stage (index among the CTA's stages) | h << 16 |
+ *    S << 26, and a fourth word.  A task is split h (h < splits) of 32 rows'
+ *    pieces in the stage's block: the lanes' edges 16*split_chunks*h + j,
+ *    j < 4C, lane i's edge 16*split_chunks*h + j at slot
+ *    first + 128*(j/4) + 4*i + j%4.  With S > 0 (h = 0) the task is C/S such
+ *    segments of S chunks one after the other, each for its own 32 rows.
+ *    fp32: the fourth word is a row group g, and lane i of segment k owns row
+ *    task_rows[32(g+k)+i] & 0x0FFFFFFF (0x0FFFFFFF: no row; S = 0: k = 0).
+ *    Other formats (S = 0): lane i owns row task_rows[32q+i] & 0x0FFFFFFF and
+ *    the fourth word is the first scale pair (NVFP4).
  *  - col[slot] is the column minus the block start (uint16); padding slots
  *    hold block_cols and weight 0.  n_slots is a multiple of 128.
  *  - NVFP4: codes are packed two per byte by slot (even slot in the low
@@ -241,7 +246,7 @@ typedef struct nsb_tiled_layout {
   const int32_t* stage_block;  /* [n_stages]          */
   const int32_t* task_ptr;     /* [ctas+1]            */
   const int32_t* tasks;        /* [n_tasks*4]         */
-  const int32_t* task_rows;    /* [n_tasks*32]        */
+  const int32_t* task_rows;    /* fp32 [row groups*32], else [n_tasks*32] */
   const uint16_t* col;         /* [n_slots]           */
   const void* weight;          /* [n_slots] (NVFP4: [n_slots/2]) */
   const uint16_t* scale_pairs; /* NVFP4: [n_scale_pairs] */

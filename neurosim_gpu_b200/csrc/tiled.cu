@@ -10,14 +10,17 @@
 //
 // Data layout (built once per weight version by neurosim_gpu_b200/tiled.py):
 //   * CTA c runs stages stage_ptr[c] .. stage_ptr[c+1]-1 (normally one).
-//   * A task is 32 rows x the stage's block.  Lane i owns row
-//     task_rows[32q+i] & 0x0FFFFFFF; its edges in the block form a contiguous
-//     run of its CSR row (the "piece").  The task has C chunks; chunk c of
-//     lane i holds the lane's edges 4c..4c+3 at slots first + 128c + 4i +
-//     (0..3), so one 8-byte load of the 16-bit columns and one vector load of
-//     the weights serve four edges, and a warp's loads cover 128 consecutive
-//     slots.  Padding slots hold column `block_cols` (a shared-memory zero)
-//     and weight 0.
+//   * A segment is 32 rows x the stage's block: lane i owns one row, and its
+//     edges in the block form a contiguous run of its CSR row (the "piece").
+//     A segment has C chunks; chunk c of lane i holds the lane's edges
+//     4c..4c+3 at slots first + 128c + 4i + (0..3), so one 8-byte load of the
+//     16-bit columns and one vector load of the weights serve four edges, and
+//     a warp's loads cover 128 consecutive slots.  Padding slots hold column
+//     `block_cols` (a shared-memory zero) and weight 0.  A task is one
+//     segment (lane i's row: task_rows[32q+i] & 0x0FFFFFFF), or, for fp32,
+//     several equal segments one after the other (segment k's rows: row group
+//     tasks[q].w + k of task_rows), so short pieces do not cost one task
+//     hand-out per 32 of them.
 //   * NVFP4: the nibble of slot s is in byte s/2 (even slot low).  Edge j of a
 //     lane sits at CSR position o + j and takes the E4M3 scale of CSR block
 //     (o + j) / 16.  Per task, scale_pairs[first pair + 32b + i] = (scale of
@@ -288,8 +291,9 @@ struct TiledArgs {
   const int32_t* stage_ptr;    // [C+1]
   const int32_t* stage_block;  // [stages]
   const int32_t* task_ptr;     // [C+1]
-  const int4* tasks;           // [T]: first slot, chunks, stage | split << 16, first scale pair
-  const int32_t* task_rows;    // [T*32]: row | phase << 28
+  const int4* tasks;           // [T]: first slot, chunks, stage | split << 16 | segment << 26,
+                               //      NVFP4: first scale pair, else: first row group
+  const int32_t* task_rows;    // NVFP4 [T*32]: row | phase << 28; else [groups*32]: row
   const uint16_t* col;         // [S] column relative to the block, block_cols = padding
   const float* global_scale;   // E4M3 / NVFP4: one float
   float* part;                 // workspace: [blocks][splits][rows] row sums (zero between launches)
@@ -435,11 +439,16 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
   W w = weights;
   if (L.global_scale) w.set_scale(__ldg(L.global_scale));
   const uint64_t pol = evict_first_policy();
-  // Bulk L2 prefetch of one task's edges (lane 0 of a consumer warp).
+  // Bulk L2 prefetch of one task's edges (one lane of the producer warp).  Of
+  // a task of several segments only the first segment is prefetched (166k
+  // rows x 1.33M columns, 8-chunk tasks of 1-4 chunk segments: 58.4 us per
+  // tick with the whole task prefetched, 54.7 us with the first segment).
   auto prefetch_task = [&](const int4& m) {
-    if (m.y > 0) {
-      prefetch_l2(L.col + m.x, static_cast<uint32_t>(m.y) * kChunkSlots * 2u);
-      w.prefetch(m.x, m.y, m.w, (m.z >> 16) * L.split_chunks);
+    const int segment = (m.z >> 26) & 63;
+    const int chunks = segment ? segment : m.y;
+    if (chunks > 0) {
+      prefetch_l2(L.col + m.x, static_cast<uint32_t>(chunks) * kChunkSlots * 2u);
+      w.prefetch(m.x, chunks, m.w, ((m.z >> 16) & 0x3FF) * L.split_chunks);
     }
   };
   // Warp w starts every tick with task w; the rest are handed out in order by
@@ -563,6 +572,17 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
       }
     } else {
       // ---- load side: task cursor (the next task is fetched one task ahead) --
+      // fp32: a task is one or more segments of S chunks (S = 0: one segment),
+      // each 32 rows' pieces, lane i's row being word i of the segment's row
+      // group.  A segment's row word is read with the issue of its last chunk,
+      // straight into that ring entry, where only the store of the segment's
+      // sum waits for it: the hand-out chain (grab, then the task) carries no
+      // row words, and short pieces come in long tasks (166k rows x 1.33M
+      // columns, ~2 chunks per piece: 71.2 -> 57.6 us per tick).  The narrower
+      // formats keep one segment per task with its row word (NVFP4: and the
+      // lane's decode phase) read with the task: their kernels have fewer
+      // registers to spare (fp16 at 166k / 25M: 30.6 -> 32.9 us segmented).
+      constexpr bool kPhased = !std::is_same<W, ChunkF32>::value;
       auto grab = [&]() {
         int q = 0;
         if (lane == 0) q = atomicAdd(next_task, 1);
@@ -575,22 +595,25 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
         if (next_q < task_count) {
           const int64_t task = task_first + next_q;
           next_meta = __ldg(L.tasks + task);
-          next_row = static_cast<uint32_t>(__ldg(L.task_rows + task * 32 + lane));
+          if (kPhased) next_row = static_cast<uint32_t>(__ldg(L.task_rows + task * 32 + lane));
         }
       };
       fetch();
       int slot = 0;          // next slot of this lane to load
       int entry = 0;         // NVFP4: this lane's column in the task's scale table
       int left = 0;          // chunks of the current task not yet loaded
-      int chunk = 0;         // index of the next chunk in its task
+      int chunk = 0;         // NVFP4: index of the next chunk in the lane's piece
       int phase = 0;         // NVFP4 phase of this lane's piece
-      uint32_t row = kRowMask;
+      uint32_t row = kRowMask;  // NVFP4: the task's row word
+      int seg = 0;           // chunks of one segment
+      int seg_left = 0;      // chunks of the current segment not yet loaded
+      int group = 0;         // row group of the current segment
       uint32_t tag_base = 0;
       // Issue the loads of the next chunk into one ring entry (tag 0: none left).
       auto issue = [&](typename W::Raw& raw, uint2& cols, uint32_t& tag, uint32_t& tag_row) {
         // On a task switch the next task (already fetched) becomes current and
         // the look-ahead is refilled: a shared-counter grab, then the metadata
-        // loads, which wait for the grab.  For fp32 the refill comes after
+        // load, which waits for the grab.  For fp32 the refill comes after
         // this chunk's loads, so those never wait behind the grab (166k / 25M
         // 37.4 -> 36.1 us, 1.33M / 200M 653 -> 629 us per tick); the narrower
         // formats refill first, which keeps the hand-out counter, and with it
@@ -608,12 +631,19 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
           }
           slot = next_meta.x + lane * kChunk;
           left = next_meta.y;
-          chunk = (next_meta.z >> 16) * L.split_chunks;  // chunk index within the lane's piece
-          entry = next_meta.w + lane;
-          phase = static_cast<int>(next_row >> 28);
-          row = next_row & kRowMask;
+          if (kPhased) {
+            chunk = ((next_meta.z >> 16) & 0x3FF) * L.split_chunks;  // chunk index within the piece
+            entry = next_meta.w + lane;
+            phase = static_cast<int>(next_row >> 28);
+            row = next_row & kRowMask;
+          } else {
+            const int s = (next_meta.z >> 26) & 63;
+            seg = s ? s : left;
+            seg_left = seg;
+            group = next_meta.w;
+          }
           tag_base = kTagValid | (static_cast<uint32_t>(next_meta.z & 0xFFFF) << kTagStage) |
-                     (static_cast<uint32_t>(next_meta.z >> 16) << kTagSplit);
+                     (static_cast<uint32_t>((next_meta.z >> 16) & 0x3FF) << kTagSplit);
           refill = true;
           if (!kLoadsFirst) {
             next_q = grab();
@@ -621,15 +651,25 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
             refill = false;
           }
         }
-        const int p = phase + chunk * kChunk;
+        const int p = kPhased ? phase + chunk * kChunk : 0;
         raw = w.load(slot, entry + (p >> 4) * 32, pol);
         cols = ld_stream_v2(L.col + slot, pol);
         if (refill) {
           next_q = grab();
           fetch();
         }
-        tag = tag_base | (static_cast<uint32_t>(p & 15) << kTagPhase) | (left == 1 ? kTagLast : 0u);
-        tag_row = row;
+        const bool last = kPhased ? left == 1 : seg_left == 1;
+        tag = tag_base | (kPhased ? static_cast<uint32_t>(p & 15) << kTagPhase : 0u) |
+              (last ? kTagLast : 0u);
+        if (kPhased) {
+          tag_row = row;
+        } else if (last) {
+          tag_row = static_cast<uint32_t>(__ldg(L.task_rows + static_cast<int64_t>(group) * 32 + lane));
+          ++group;
+          seg_left = seg;
+        } else {
+          --seg_left;
+        }
         slot += kChunkSlots;
         ++chunk;
         --left;

@@ -217,7 +217,7 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
         getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
-    if lib.nsb_abi_version() != 11:
+    if lib.nsb_abi_version() != 12:
         raise RuntimeError("libneurosim_b200.so ABI version mismatch")
     return lib
 

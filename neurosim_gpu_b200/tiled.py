@@ -14,12 +14,16 @@ and streams the edges with vector loads:
   block is then staged once per tick.  (With more blocks than CTAs, CTA ``c``
   runs the full-row stages of blocks ``c, c + ctas, ...``, double-buffered.)
 * For each stage, the rows' non-empty pieces (their edges inside the block, a
-  contiguous run of the original CSR row) are sorted by length and grouped 32
-  at a time into tasks.  A task has ``chunks`` chunks; lane ``i`` owns one row
+  contiguous run of the original CSR row) are sorted by chunk count (then by
+  row) and grouped 32 at a time into tasks.  A task has ``chunks`` chunks;
+  lane ``i`` owns one row
   and its edge ``j`` sits at slot ``first + 128 * (j // 4) + 4 * i + j % 4``,
   so one lane reads four edges with one vector load and a warp's loads cover
   128 consecutive slots.  Shorter pieces are padded with column ``block_cols``
-  (a zero in shared memory) and weight 0.
+  (a zero in shared memory) and weight 0.  Consecutive groups of one stage
+  with the same chunk count are merged into tasks of several such segments
+  (up to ``MERGE_CHUNKS`` chunks; fp32 only), each segment's 32 rows being
+  one row group of ``task_rows``.
 * Columns are stored relative to their block as uint16 (2 bytes per edge
   instead of the CSR's 4).
 * A task is cut into sub-tasks of ``split_chunks`` chunks (edges
@@ -68,6 +72,14 @@ WARPS = 31                    # consumer warps of a CTA
 # bit-identical.
 SPLIT_CHUNKS = {native.F32: 9, native.F16: 0, native.E4M3: 0, native.NVFP4: 0}
 MAX_PLANES = 32               # cap on blocks x splits (only degree-skewed graphs reach it)
+# Chunks a task of several 32-piece segments holds at most (unsplit layouts;
+# split layouts merge up to one split).  Layouts of short pieces otherwise
+# hand out one task per ~2 chunks.  Measured on one rank's share of the 1.33M /
+# 200M graph (166k rows x 1.33M columns, 23 blocks, 1-4 chunk pieces): 74.3 us
+# per tick unmerged, 56.0 / 54.9 / 54.6 / 54.9 us with tasks of up to
+# 6 / 7 / 8 / 10 chunks.
+MERGE_CHUNKS = 8
+MAX_SEGMENT_CHUNKS = 63       # 6-bit segment length in a task's third word
 
 
 def _u16(values: torch.Tensor) -> torch.Tensor:
@@ -94,8 +106,12 @@ class TiledLayout:
     stage_ptr: torch.Tensor    # int32 [ctas+1]: stages of CTA c
     stage_block: torch.Tensor  # int32 [stages]: column block of each stage
     task_ptr: torch.Tensor     # int32 [ctas+1]: tasks of CTA c
-    tasks: torch.Tensor        # int32 [T, 4]: first slot, chunks, stage | split << 16, first scale pair
-    task_rows: torch.Tensor    # int32 [T, 32]: row | phase << 28 (row ROW_NONE: padding lane)
+    # int32 [T, 4]: first slot, chunks, stage | split << 16 | segment chunks << 26
+    # (0: one segment), then fp32: first row group, NVFP4: first scale pair
+    tasks: torch.Tensor
+    # int32, row ROW_NONE: padding lane.  fp32 [groups, 32]: segment k of task
+    # q takes row group tasks[q, 3] + k; else [T, 32]: row (NVFP4: | phase << 28)
+    task_rows: torch.Tensor
     col: torch.Tensor          # int16 storage of uint16 [S]
     weight: torch.Tensor       # [S] in the storage format (NVFP4: uint8 [S/2])
     scale_pairs: torch.Tensor | None  # int16 storage of uint16 (NVFP4)
@@ -264,11 +280,15 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
     stage_ptr = torch.zeros(ctas + 1, dtype=torch.int64, device=device)
     torch.cumsum(torch.bincount(stage_cta, minlength=ctas), 0, out=stage_ptr[1:])
 
-    # Non-empty pieces sorted by stage, then by length (longest first).
+    # Non-empty pieces sorted by stage, then by chunk count (longest first),
+    # then by row.  A task's chunk count is that of its first piece, as with a
+    # sort by length, but its 32 rows ascend, so the warp's stores of their
+    # sums into the row-sum plane touch a few lines instead of 32 (166k rows x
+    # 1.33M columns, pieces of ~6.5 edges: 3.8M scattered stores a tick).
     group = stage_of.flatten()
     lengths = piece_len.flatten()
     order = torch.nonzero(lengths).flatten()
-    order = order[torch.sort(-lengths[order], stable=True).indices]
+    order = order[torch.sort(-((lengths[order] + CHUNK - 1) // CHUNK), stable=True).indices]
     order = order[torch.sort(group[order], stable=True).indices]
     sorted_group = group[order]
     group_size = torch.bincount(sorted_group, minlength=n_stages)
@@ -355,22 +375,57 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
         split = 1 << 30
     split = max(1, min(split, 1 << 30))
     splits = max(1, -(-longest // split))
+    unsplit = splits == 1
     split = min(split, max(longest, 1))
-    n_sub = (task_chunks + split - 1) // split
-    sub_task = torch.repeat_interleave(arange(n_tasks), n_sub)
+    # Tasks: runs of consecutive groups of one stage with one chunk count c are
+    # merged, up to MERGE_CHUNKS chunks (and one split) per task, into tasks
+    # of several segments (c chunks each, one group's 32 pieces per segment),
+    # so layouts of short pieces do not hand out a task per 32 pieces.  Only
+    # fp32: the narrower formats keep one group per task (NVFP4's task carries
+    # the group's scale table).  Merging moves no slot: a task's groups are
+    # consecutive in slot order.
+    group_chunks = task_chunks
+    if fmt == native.F32 and n_tasks:
+        target = MERGE_CHUNKS if unsplit else min(split, MERGE_CHUNKS)
+        run_head = torch.ones(n_tasks, dtype=torch.bool, device=device)
+        run_head[1:] = (task_stage[1:] != task_stage[:-1]) | (group_chunks[1:] != group_chunks[:-1])
+        run_first = torch.nonzero(run_head).flatten()
+        position = arange(n_tasks) - run_first[torch.cumsum(run_head.long(), 0) - 1]
+        per_task = torch.where(group_chunks <= MAX_SEGMENT_CHUNKS,
+                               torch.clamp(target // group_chunks.clamp(min=1), min=1), 1)
+        head = position % per_task == 0
+        first_group = torch.nonzero(head).flatten()
+        groups = torch.bincount(torch.cumsum(head.long(), 0) - 1)
+        merged_chunks = group_chunks[first_group] * groups
+        segment = torch.where(groups > 1, group_chunks[first_group], 0)
+        merged_word = first_group                       # the task's first row group
+    else:
+        first_group = arange(n_tasks)
+        merged_chunks = group_chunks
+        segment = torch.zeros_like(group_chunks)
+        merged_word = scale_first                       # NVFP4: the task's scale table
+    n_merged = first_group.numel()
+    if unsplit and n_merged:
+        split = max(split, int(merged_chunks.max()))   # one sub-task per task
+    n_sub = (merged_chunks + split - 1) // split
+    sub_task = torch.repeat_interleave(arange(n_merged), n_sub)
     sub_h = arange(sub_task.numel()) - (torch.cumsum(n_sub, 0) - n_sub)[sub_task]
-    sub_chunks = torch.clamp(task_chunks[sub_task] - sub_h * split, max=split)
+    sub_chunks = torch.clamp(merged_chunks[sub_task] - sub_h * split, max=split)
     # Within a stage: longest sub-tasks first (tasks keep their order otherwise).
-    sub_stage = task_stage[sub_task]
+    sub_group = first_group[sub_task]
+    sub_stage = task_stage[sub_group]
     sub_order = torch.sort(-sub_chunks, stable=True).indices
     sub_order = sub_order[torch.sort(sub_stage[sub_order], stable=True).indices]
     sub_task, sub_h, sub_chunks = sub_task[sub_order], sub_h[sub_order], sub_chunks[sub_order]
-    tasks = torch.stack((task_first[sub_task] + sub_h * split * CHUNK_SLOTS, sub_chunks,
-                         task_stage_local[sub_task] | (sub_h << 16), scale_first[sub_task]), dim=1)
+    sub_group = first_group[sub_task]
+    tasks = torch.stack((task_first[sub_group] + sub_h * split * CHUNK_SLOTS, sub_chunks,
+                         task_stage_local[sub_group] | (sub_h << 16) | (segment[sub_task] << 26),
+                         merged_word[sub_task]), dim=1)
     subs_per_cta = torch.zeros(ctas, dtype=torch.int64, device=device)
-    subs_per_cta.index_add_(0, stage_cta[sub_stage], torch.ones_like(sub_stage))
+    subs_per_cta.index_add_(0, stage_cta[task_stage[sub_group]], torch.ones_like(sub_group))
     torch.cumsum(subs_per_cta, 0, out=task_ptr[1:])
-    task_rows = task_rows[sub_task]
+    if fmt != native.F32:
+        task_rows = task_rows[sub_group]               # one row word per lane of each task
     return TiledLayout(
         neurons=n, n_edges=m, ctas=ctas, blocks=blocks, block_cols=block_cols, buffers=buffers,
         format=fmt, stage_ptr=stage_ptr.to(torch.int32), stage_block=stage_block.to(torch.int32),
@@ -397,13 +452,21 @@ def emulate(layout: TiledLayout, source: torch.Tensor) -> torch.Tensor:
     task = by_slot[torch.searchsorted(first[by_slot], slots, right=True) - 1]
     local = slots - first[task]
     chunk, lane, e = local // CHUNK_SLOTS, (local % CHUNK_SLOTS) // CHUNK, local % CHUNK
-    word = layout.task_rows.long()[task, lane] & 0xFFFFFFFF
+    third = layout.tasks[:, 2].long()
+    if layout.format != native.F32:
+        word = layout.task_rows.long()[task, lane] & 0xFFFFFFFF
+    else:
+        segment = (third >> 26) & 63
+        length = torch.where(segment > 0, segment, layout.tasks[:, 1].long())[task]
+        group = layout.tasks[:, 3].long()[task] + chunk // length
+        word = layout.task_rows.long()[group, lane] & 0xFFFFFFFF
+        chunk = chunk % length
     col = layout.col.long() & 0xFFFF
     cta = torch.searchsorted(layout.task_ptr.long(), torch.arange(layout.n_tasks, device=dev),
                              right=True) - 1
-    stage = layout.stage_ptr.long()[cta] + (layout.tasks[:, 2].long() & 0xFFFF)
+    stage = layout.stage_ptr.long()[cta] + (third & 0xFFFF)
     block = layout.stage_block.long()[stage][task]
-    chunk = chunk + (layout.tasks[:, 2].long() >> 16)[task] * layout.split_chunks
+    chunk = chunk + ((third >> 16) & 0x3FF)[task] * layout.split_chunks
     padded = torch.cat([x, torch.zeros(layout.blocks * layout.block_cols + 1 - x.numel(),
                                        dtype=x.dtype, device=dev)])
     gathered = torch.where(col == layout.block_cols, torch.zeros_like(x[:1]),
