@@ -859,9 +859,12 @@ def run_profile(args, workload: str) -> None:
 
 def run_profile_shard(args, workload: str, device) -> None:
     """``--profile-shard R/W``: rank R's share of a W-way row split of the
-    workload's graph, built and launched on one GPU (the rank's tiled tick with
-    no exchange: what each rank of a W-GPU run launches, minus the peer stores).
-    Only the rank's destination CSR and layout stay on the device."""
+    workload's graph, built and launched on one GPU.  With ``--launch-ticks``
+    above 1, persistent launches with the in-kernel exchange over a world of
+    one (what each rank of a W-GPU run launches, minus the stores to and the
+    wait for the other ranks); else one-tick launches of the rank's kernel
+    without an exchange.  Only the rank's destination CSR and layout stay on
+    the device."""
     from neurosim_gpu_b200.sharded import ShardedDendriticMatrixRuntime
 
     rank, world = (int(v) for v in args.profile_shard.split("/"))
@@ -897,6 +900,7 @@ def run_profile_shard(args, workload: str, device) -> None:
                       "splits": layout.splits if layout is not None else None,
                       "slots": layout.n_slots if layout is not None else None,
                       "padding_fraction": layout.padding_fraction if layout is not None else None,
+                      "tasks": layout.n_tasks if layout is not None else None,
                       "ticks_per_launch": args.launch_ticks,
                       "us_per_tick_diagnostic": us_per_tick,
                       "launches": args.warmup + args.steps,
