@@ -559,6 +559,7 @@ def run_sharded_pels(args) -> dict:
         dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.all_reduce(torch.zeros(1, device=device))  # ranks lined up on the device
         e0.record()
         fn()
         e1.record()
@@ -676,6 +677,7 @@ def strong_scaling_record(args, world: int, rank: int, device) -> dict | None:
                       if runtime.exchange == "peer" else None)
             torch.cuda.synchronize()
             dist.barrier()
+            dist.all_reduce(torch.zeros(1, device=device))  # ranks lined up on the device
             flush.zero_()
             e0.record()
             if launch is not None:
@@ -740,10 +742,17 @@ def run_sharded(args, explicit_workload: bool) -> dict:
     steps = max(args.steps, 1)  # exactly K ticks are timed
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
 
+    align = torch.zeros(1, device=device)
+
     def timed(fn, flush_first: bool = False) -> float:
         dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # A one-float all-reduce on the stream lines the ranks' streams up on
+        # the device (the host barrier releases the ranks tens of us apart); the
+        # flush behind it takes equally long everywhere and gives the host the
+        # time to enqueue the timed work before the stream reaches it.
+        dist.all_reduce(align)
         if flush_first:
             flush.zero_()
         e0.record()

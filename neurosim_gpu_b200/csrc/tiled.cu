@@ -364,13 +364,16 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
 
 // End-of-tick barrier across ranks, for one thread per CTA after a
 // __syncthreads that follows the CTA's peer stores and a system-scope fence by
-// that thread: all CTAs of this rank meet at the local grid
-// barrier, CTA 0 then adds one to every rank's counter, and every CTA waits
-// until its rank's counter shows all ranks' arrivals for this tick.  Bounded:
-// on timeout it records code 6.
+// that thread: every CTA counts its arrival on the rank's local counter, and
+// the CTA that arrives last (its atomic follows every other CTA's arrival,
+// each made after that CTA's fence) fences and adds one to every rank's
+// counter.  Every CTA then waits until its rank's counter shows all ranks'
+// arrivals for this tick; none waits on the local counter, so the signal
+// leaves as soon as the rank's last CTA is done.  The local counter still
+// grows by the grid size per tick.  Bounded: on timeout it records code 6.
 __device__ void peer_barrier(const Peers& px, unsigned long long* local, int tick, int* st) {
-  grid_arrive_wait(local, st);
-  if (blockIdx.x == 0) {
+  const unsigned long long arrival = atomicAdd(local, 1ull);
+  if (arrival % gridDim.x == gridDim.x - 1) {
     __threadfence_system();
     for (int p = 0; p < px.world; ++p) atomicAdd_system(px.counters[p], 1ull);
   }
