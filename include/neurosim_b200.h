@@ -131,8 +131,10 @@ typedef struct nsb_out_csr {
  *   s' = clamp(alpha*s + (1-alpha)*gain*tanh((1-c)*j + c*d' - k*a + u), 0, 1)
  *   a' = ra*a + (1-ra)*s'
  * `width` is the number of lanes that share one destination row: 4, 8, 16 or 32
- * (the reference accepts 8/16/32), or 0 to let the library choose from the
- * mean degree.  One launch; edges are streamed once for every 8 batch rows. */
+ * (the reference accepts 8/16/32; B >= 2 runs 8, 16 or 32, a smaller width
+ * meaning 8), or 0 to let the library choose from the mean degree.  The width
+ * fixes the order of a row's sum.  One launch; edges are streamed once for
+ * every 8 batch rows. */
 NSB_API int nsb_dendritic_step(const nsb_tick* tick, const nsb_csr* csr, int32_t width,
                        const nsb_tick_out* out, void* stream);
 

@@ -311,28 +311,37 @@ cudaError_t launch_batch_variant(const TickArgs& t, const View& x, const Csr& cs
 
 template <int BT, bool UPDATE, typename W>
 cudaError_t dispatch_batch_tile(const TickArgs& t, const View& x, const Csr& csr, const W& w,
-                                const TickOut& out, const Out& product, cudaStream_t stream) {
+                                int width, const TickOut& out, const Out& product,
+                                cudaStream_t stream) {
   // One vector load per (edge, batch tile) needs every tile full and its BT
   // floats contiguous and BT * 4-byte aligned.
   const bool vec = x.sb == 1 && x.sn % BT == 0 && t.batch % BT == 0 &&
                    aligned(x.data, static_cast<uintptr_t>(BT) * 4);
-  // Lanes per row from the mean degree: each lane takes two edges per step.
+  // Lanes per row: the caller's width (8 / 16 / 32; smaller means 8), else
+  // from the mean degree (each lane takes two edges per step).  The lanes fix
+  // a row's summation order, so the row blocks of a sharded graph pass the
+  // whole graph's choice.
   const double degree = static_cast<double>(csr.n_edges) / static_cast<double>(std::max<int64_t>(t.neurons, 1));
+  const int lanes = width > 0 ? (width <= 8 ? 8 : width <= 16 ? 16 : 32)
+                              : degree <= 24.0 ? 8 : degree <= 64.0 ? 16 : 32;
 #define NSB_BATCH(G)                                                                          \
   return vec ? launch_batch_variant<BT, G, UPDATE, true>(t, x, csr, w, out, product, stream)  \
              : launch_batch_variant<BT, G, UPDATE, false>(t, x, csr, w, out, product, stream);
-  if (degree <= 24.0 && BT <= 8) { NSB_BATCH(8) }
-  if (degree <= 64.0) { NSB_BATCH(16) }
+  if (lanes == 8) { NSB_BATCH(8) }
+  if (lanes == 16) { NSB_BATCH(16) }
   NSB_BATCH(32)
 #undef NSB_BATCH
 }
 
 template <bool UPDATE, typename W>
 cudaError_t dispatch_batch(const TickArgs& t, const View& x, const Csr& csr, const W& w,
-                           const TickOut& out, const Out& product, cudaStream_t stream) {
-  if (t.batch <= 2) return dispatch_batch_tile<2, UPDATE>(t, x, csr, w, out, product, stream);
-  if (t.batch <= 4) return dispatch_batch_tile<4, UPDATE>(t, x, csr, w, out, product, stream);
-  return dispatch_batch_tile<8, UPDATE>(t, x, csr, w, out, product, stream);
+                           int width, const TickOut& out, const Out& product,
+                           cudaStream_t stream) {
+  if (t.batch <= 2)
+    return dispatch_batch_tile<2, UPDATE>(t, x, csr, w, width, out, product, stream);
+  if (t.batch <= 4)
+    return dispatch_batch_tile<4, UPDATE>(t, x, csr, w, width, out, product, stream);
+  return dispatch_batch_tile<8, UPDATE>(t, x, csr, w, width, out, product, stream);
 }
 
 template <bool UPDATE, typename W>
@@ -344,7 +353,7 @@ cudaError_t dispatch_group(const TickArgs& t, const View& x, const Csr& csr, con
   // summation order (and the result) does not depend on the state's layout.
   // With the [N, B] layout (batch stride 1) its gathers are one sector per edge.
   if (batch >= 2 && x.data)
-    return dispatch_batch<UPDATE>(t, x, csr, w, out, product, stream);
+    return dispatch_batch<UPDATE>(t, x, csr, w, width, out, product, stream);
 #define NSB_BT(G)                                                                      \
   if (batch <= 1) return launch_variant<G, 1, UPDATE>(t, x, csr, w, vec, out, product, stream); \
   if (batch <= 2) return launch_variant<G, 2, UPDATE>(t, x, csr, w, vec, out, product, stream); \

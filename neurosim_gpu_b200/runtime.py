@@ -182,6 +182,10 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
         # Lanes per row; each lane reads 4-edge chunks, so 32 lanes cover 128 edges.
         self.threads_per_row = threads_per_row or (8 if degree <= 16 else 16 if degree <= 48
                                                    else 32)
+        # B >= 2: the batch kernel's lanes per row, the caller's or the
+        # library's own choice from the mean degree.
+        self._batch_width = threads_per_row or (8 if degree <= 24 else 16 if degree <= 64
+                                                else 32)
         self.weight_dtype = weight_dtype
         self.weight_format = weight_format
         self.precision = "fp32"
@@ -281,9 +285,10 @@ class NativeDendriticMatrixRuntime(_NativeCompartments):
             raise ValueError("the CSR path runs one tick per launch")
         weight, scales, scale, _ = self._weights()
         topology = self.topology
+        width = self.threads_per_row if s.shape[0] == 1 else self._batch_width
         return self.extension.prepare_step(s, d, a, self._parameters(), topology.in_rowptr,
                                            topology.in_col, weight, u, us, v, vs,
-                                           self.threads_per_row, scales, scale, out=out)
+                                           width, scales, scale, out=out)
 
     @property
     def checkpoint_precision(self) -> str:

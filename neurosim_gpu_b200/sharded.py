@@ -1,25 +1,26 @@
 """Row-sharded matrix tick across the GPUs of one node (one process per GPU).
 
-Destination rows are cut into ``world`` equal ranges: rank r owns rows
-``[r*R, min(N, (r+1)*R))`` with ``R = ceil(N / world)`` rounded up to a
-multiple of 4.  Every tick each rank
+Destination rows are cut into ``world`` contiguous ranges (:func:`row_bounds`):
+by default where the prefix sum of ``in_rowptr`` reaches equal shares of the
+edges, each range starting on a multiple of 4 rows.  Every tick each rank
 
 1. runs the native tick on its own rows, gathering from the full soma vector
-   ``x`` (all N neurons, laid out ``[world*R, B]`` so neuron n sits at row n on
-   every rank) and writing its new soma values straight into its own slice of
+   ``x`` (all N neurons in global row order, so neuron n sits at row n on
+   every rank) and writing its new soma values straight into its own rows of
    the next buffer;
-2. all-gathers the slices in place over NCCL (``all_gather_into_tensor``,
-   ``N*B*4`` bytes per tick), so every rank holds the next full soma vector.
+2. exchanges the rows: stores into every other rank's buffer inside the tick
+   kernel (the fused exchange), or an NCCL all-gather (``N*B*4`` bytes per
+   tick; in place when the ranges are equal slices, else through a staging
+   buffer of equal slices and one index_select back into row order).
 
 Per-row sums are the same as on one GPU with the same kernel, so sharded
-states are bit-identical to the single-GPU runtime's.  Each rank keeps its own
-dendrite / adaptation slices and parameter views.  ``run`` captures ticks and
-collectives together in one CUDA graph.
+states are bit-identical to the single-GPU runtime's, whatever the partition.
+Each rank keeps its own dendrite / adaptation slices and parameter views.
+``run`` captures ticks and collectives together in one CUDA graph.
 
 The partition and exchange logic lives in :class:`RowShard`, which runs on any
 device and backend (the CPU tests drive it over gloo with the oracle tick).
 """
-
 from __future__ import annotations
 
 import math
@@ -34,26 +35,67 @@ from .dynamics import DendriticDynamics
 from .precision import encode_sparse_weights
 
 
+def row_bounds(neurons: int, world: int, rowptr: torch.Tensor | None = None) -> list[int]:
+    """First rows of the ranks' row ranges (``world + 1`` bounds, 0 and N last).
+
+    With ``rowptr`` (the destination CSR's ``in_rowptr``) the ranges hold
+    about equal numbers of edges: bound r is the row where the prefix sum of
+    edges reaches r / world of them, rounded to a multiple of 4.  Without it
+    they hold equal numbers of rows (a multiple of 4 per rank).  A multiple of
+    4 keeps every rank's first row, and with it its slices of the state,
+    16-byte aligned (bulk copies in the tick kernel).
+    """
+    per = 4 * math.ceil(neurons / world / 4)
+    if rowptr is None or world == 1:
+        return [min(neurons, r * per) for r in range(world)] + [neurons]
+    prefix = rowptr.to(torch.int64)
+    edges = int(prefix[-1])
+    targets = torch.tensor([r * edges // world for r in range(1, world)], dtype=torch.int64,
+                           device=prefix.device)
+    rows = torch.searchsorted(prefix, targets).tolist()
+    bounds = [0]
+    for row in rows:
+        bounds.append(min(max(4 * ((row + 2) // 4), bounds[-1]), 4 * (neurons // 4)))
+    return bounds + [neurons]
+
+
 @dataclass
 class RowShard:
-    """Rows of one rank and the double-buffered full soma vector."""
+    """Rows of one rank and the double-buffered full soma vector.
+
+    ``bounds`` (from :func:`row_bounds`) are every rank's row ranges; the
+    gathered buffers hold the soma vector in global row order, so rank r's
+    rows sit at ``bounds[r]`` in every rank's buffer whatever the partition.
+    """
 
     neurons: int
     batch: int
     rank: int
     world: int
     device: torch.device
+    bounds: list[int] | None = None
 
     def __post_init__(self) -> None:
-        # A multiple of 4 rows per rank keeps every rank's first row and its
-        # slices of the state 16-byte aligned (bulk copies in the tick kernel).
-        self.rows_per_rank = 4 * math.ceil(self.neurons / self.world / 4)
-        self.lo = min(self.neurons, self.rank * self.rows_per_rank)
-        self.hi = min(self.neurons, self.lo + self.rows_per_rank)
-        self.cols = self.world * self.rows_per_rank
+        if self.bounds is None:
+            self.bounds = row_bounds(self.neurons, self.world)
+        if (len(self.bounds) != self.world + 1 or self.bounds[0] != 0
+                or self.bounds[-1] != self.neurons
+                or any(a > b for a, b in zip(self.bounds, self.bounds[1:]))
+                or any(b % 4 and b != self.neurons for b in self.bounds[:-1])):
+            raise ValueError("row bounds must rise from 0 to N in multiples of 4")
+        self.lo, self.hi = self.bounds[self.rank], self.bounds[self.rank + 1]
+        sizes = [b - a for a, b in zip(self.bounds, self.bounds[1:])]
+        # The NCCL exchange gathers slices of rows_per_rank rows from every rank.
+        self.rows_per_rank = 4 * math.ceil(max(sizes) / 4)
+        # Equal slices at r * rows_per_rank: the buffer itself is gathered in place.
+        self.in_place = all(self.bounds[r] == min(self.neurons, r * self.rows_per_rank)
+                            for r in range(self.world))
+        self.cols = (self.world * self.rows_per_rank if self.in_place
+                     else 4 * math.ceil(self.neurons / 4))
         shape = (self.cols, self.batch)
         self.buffers = [torch.zeros(shape, device=self.device) for _ in range(2)]
         self.current = 0
+        self._staging = self._pad = self._order = None
 
     @property
     def rows(self) -> int:
@@ -72,11 +114,38 @@ class RowShard:
         return self.buffers[index][self.lo: self.hi].t()
 
     def exchange(self, index: int, group=None) -> None:
-        """All-gather every rank's slice of buffer ``index`` in place."""
-        flat = self.buffers[index].view(-1)
+        """All-gather every rank's slice of buffer ``index`` in place.
+
+        Unequal slices go through a staging buffer of ``world`` equal slices
+        (this rank's rows padded to ``rows_per_rank``) and are put back in
+        global row order by one index_select.
+        """
         chunk = self.rows_per_rank * self.batch
-        dist.all_gather_into_tensor(flat, flat[self.rank * chunk: (self.rank + 1) * chunk],
-                                    group=group)
+        if self.in_place:
+            flat = self.buffers[index].view(-1)
+            dist.all_gather_into_tensor(flat, flat[self.rank * chunk: (self.rank + 1) * chunk],
+                                        group=group)
+            return
+        if self._staging is None:
+            self._staging = torch.zeros((self.world * self.rows_per_rank, self.batch),
+                                        device=self.device)
+            self._pad = torch.zeros((self.rows_per_rank, self.batch), device=self.device)
+            self._order = torch.cat([torch.arange(r * self.rows_per_rank,
+                                                  r * self.rows_per_rank + b - a)
+                                     for r, (a, b) in enumerate(zip(self.bounds, self.bounds[1:]))]
+                                    ).to(self.device)
+        self._pad[: self.rows].copy_(self.buffers[index][self.lo: self.hi])
+        dist.all_gather_into_tensor(self._staging.view(-1), self._pad.view(-1), group=group)
+        torch.index_select(self._staging, 0, self._order, out=self.buffers[index][: self.neurons])
+
+    def gather_rows(self, local: torch.Tensor, group=None) -> torch.Tensor:
+        """Every rank's [B, rows] values assembled into the full [B, N] (an all-gather)."""
+        padded = torch.zeros(self.batch, self.rows_per_rank, device=local.device)
+        padded[:, : local.shape[1]] = local
+        parts = [torch.empty_like(padded) for _ in range(self.world)]
+        dist.all_gather(parts, padded.contiguous(), group=group)
+        sizes = [b - a for a, b in zip(self.bounds, self.bounds[1:])]
+        return torch.cat([part[:, :size] for part, size in zip(parts, sizes)], dim=1)
 
     def state(self) -> torch.Tensor:
         """The full soma state [B, N] (a view of the current buffer)."""
@@ -106,14 +175,18 @@ class ShardedDendriticMatrixRuntime:
     ``(in_rowptr, in_col, in_weight)`` of the full destination CSR on this
     rank's device; ``dynamics`` and ``initial_state`` ([B, N]) are the full ones.
     ``state`` is the full soma state on every rank; ``dendritic_state`` and
-    ``adaptation_state`` are this rank's rows.
+    ``adaptation_state`` are this rank's rows.  ``partition="edges"`` (the
+    default) cuts the rows where the prefix sum of ``in_rowptr`` reaches equal
+    shares of the edges, so a degree-skewed graph still gives every rank the
+    same work per tick; ``"rows"`` gives every rank the same number of rows.
+    The states do not depend on the partition (bit for bit).
     """
 
     def __init__(self, graph, dynamics: DendriticDynamics, initial_state: torch.Tensor, *,
                  group=None, precision: str = "fp32", kernel: str = "auto",
                  threads_per_row: int | None = None, extension=None,
                  rank: int | None = None, world: int | None = None,
-                 exchange: str = "auto") -> None:
+                 exchange: str = "auto", partition: str = "edges") -> None:
         if isinstance(graph, tuple):
             in_rowptr, in_col, in_weight = graph
         else:
@@ -124,6 +197,8 @@ class ShardedDendriticMatrixRuntime:
             raise ValueError("kernel must be 'auto', 'csr' or 'tiled'")
         if exchange not in ("auto", "nccl", "peer"):
             raise ValueError("exchange must be 'auto', 'nccl' or 'peer'")
+        if partition not in ("edges", "rows"):
+            raise ValueError("partition must be 'edges' or 'rows'")
         self.group = group
         # rank / world may be given explicitly to build one rank's share without a
         # process group (the exchange is then up to the caller).
@@ -133,7 +208,9 @@ class ShardedDendriticMatrixRuntime:
         batch, neurons = initial_state.shape
         self.neurons, self.batch = neurons, batch
         self.extension = extension if extension is not None else _native.load_native_extension()
-        self.shard = RowShard(neurons, batch, self.rank, self.world, device)
+        self.shard = RowShard(neurons, batch, self.rank, self.world, device,
+                              row_bounds(neurons, self.world,
+                                         in_rowptr if partition == "edges" else None))
         lo, hi = self.shard.lo, self.shard.hi
         self.compartment_dynamics = dynamics
         self._source_csr = (in_rowptr, in_col, in_weight.detach())
@@ -160,20 +237,30 @@ class ShardedDendriticMatrixRuntime:
             full, scales, scale = encode_sparse_weights(in_weight.detach(), precision)
         self.layout = None
         if batch == 1 and kernel != "csr" and self.local_edges > 0:
+            fmt = {"fp32": _native.F32, "fp16": _native.F16, "fp8": _native.E4M3,
+                   "nvfp4": _native.NVFP4}[precision]
+            split = _tiled.graph_split(in_rowptr, in_col, fmt, neurons=neurons, cols=neurons,
+                                       ctas=_tiled.sm_count(device),
+                                       smem_limit=_tiled.smem_limit(device))
             if precision == "nvfp4":
                 local = _pack_nibbles(_unpack_nibbles(full, self.n_edges)[e0:e1])
             else:
                 local = full[e0:e1]
             self.layout = _tiled.build_tiled_layout(
                 (rowptr[lo: hi + 1] - e0).to(torch.int32), in_col[e0:e1].contiguous(),
-                local.contiguous(), neurons=hi - lo, cols=self.shard.cols,
+                local.contiguous(), neurons=hi - lo, cols=neurons,
                 ctas=_tiled.sm_count(device), smem_limit=_tiled.smem_limit(device),
-                block_scales=scales, global_scale=scale, scale_offset=e0)
+                block_scales=scales, global_scale=scale, scale_offset=e0, split=split)
         # Row-block CSR for the general kernel: the rows' offsets into the full arrays.
         self.csr = (in_rowptr[lo: hi + 1].contiguous(), in_col, full, scales, scale)
         degree = self.n_edges / max(neurons, 1)
         self.threads_per_row = threads_per_row or (8 if degree <= 16 else 16 if degree <= 48
                                                    else 32)
+        # B >= 2: the batch kernel's lanes per row as the single-GPU runtime's
+        # kernel picks them from the WHOLE graph's mean degree (a row block's
+        # own degree may differ, and the lanes fix a row's summation order).
+        self._batch_width = threads_per_row or (8 if degree <= 24 else 16 if degree <= 64
+                                                else 32)
         # In-kernel peer exchange (run() at B = 1): every rank maps every other
         # rank's gathered buffers and arrival counter through CUDA IPC.
         self._peer = None
@@ -263,10 +350,11 @@ class ShardedDendriticMatrixRuntime:
         if self.layout is not None:
             return self.extension.prepare_step_tiled(
                 s_rows, d, a, self.params, self.layout, u, us, v, vs, out=out,
-                status=self.status, source=shard.buffers[src].view(-1))
+                status=self.status, source=shard.buffers[src].view(-1)[: self.neurons])
         rowptr, col, weight, scales, scale = self.csr
         return self.extension.prepare_step_rows(
-            s_rows, d, a, self.params, rowptr, col, weight, u, us, v, vs, self.threads_per_row,
+            s_rows, d, a, self.params, rowptr, col, weight, u, us, v, vs,
+            self.threads_per_row if self.batch == 1 else self._batch_width,
             scales, scale, source=shard.source(src), out=out)
 
     def _drives(self, drive, dendritic_drive):
@@ -470,12 +558,7 @@ class ShardedDendriticMatrixRuntime:
 
     def gather(self, name: str) -> torch.Tensor:
         """The full [B, N] dendrite or adaptation state (an all-gather)."""
-        local = getattr(self, name)
-        padded = torch.zeros(self.batch, self.shard.rows_per_rank, device=local.device)
-        padded[:, : local.shape[1]] = local
-        parts = [torch.empty_like(padded) for _ in range(self.world)]
-        dist.all_gather(parts, padded.contiguous(), group=self.group)
-        return torch.cat(parts, dim=1)[:, : self.neurons]
+        return self.shard.gather_rows(getattr(self, name), self.group)
 
 
 class _ShardedRolloutPlan:

@@ -2,15 +2,16 @@
 
 The reference's PELS runtime (``native_compartmental.py:134-177``,
 ``csrc/compartmental.cu:142-173``) runs on one GPU.  Here destination rows are
-cut into ``world`` equal ranges as for the sharded matrix tick
-(:class:`~neurosim_gpu_b200.sharded.RowShard`): rank r owns rows
-``[r*R, min(N, (r+1)*R))`` and, for them, the soma / dendrite / adaptation /
-emitted state, theta and the persistent current.  Every tick each rank
+cut into ``world`` contiguous ranges as for the sharded matrix tick
+(:class:`~neurosim_gpu_b200.sharded.RowShard`, by default balanced by edges):
+rank r owns rows ``[lo_r, hi_r)`` and, for them, the soma / dendrite /
+adaptation / emitted state, theta and the persistent current.  Every tick
+each rank
 
 1. advances its rows with j = its current and applies the emit rule; each row's
    delta (the residual where it emits, else 0) goes into the gathered delta
-   buffer ``[world*R, B]`` at its global row;
-2. exchanges the deltas: an in-place NCCL all-gather of the rows' slices
+   buffer (global row order) at its global row;
+2. exchanges the deltas: an NCCL all-gather of the rows' slices
    (``exchange="nccl"``), or peer stores of every delta into every rank's
    buffer inside the advance kernel with a bounded cross-GPU wait at the start
    of the scatter (``exchange="peer"``, CUDA IPC mappings);
@@ -31,7 +32,7 @@ import torch.distributed as dist
 from . import native as _native
 from . import tiled as _tiled
 from .dynamics import DendriticDynamics
-from .sharded import RowShard
+from .sharded import RowShard, row_bounds
 
 
 def filtered_out_csr(in_rowptr: torch.Tensor, in_col: torch.Tensor, in_weight: torch.Tensor,
@@ -70,7 +71,8 @@ class ShardedDendriticPELSRuntime:
 
     def __init__(self, graph, dynamics: DendriticDynamics, initial_state: torch.Tensor, *,
                  theta, group=None, extension=None, rank: int | None = None,
-                 world: int | None = None, exchange: str = "auto") -> None:
+                 world: int | None = None, exchange: str = "auto",
+                 partition: str = "edges") -> None:
         if isinstance(graph, tuple):
             in_rowptr, in_col, in_weight = graph
         else:
@@ -79,6 +81,8 @@ class ShardedDendriticPELSRuntime:
             raise ValueError("native compartment runtime requires CUDA float32")
         if exchange not in ("auto", "nccl", "peer"):
             raise ValueError("exchange must be 'auto', 'nccl' or 'peer'")
+        if partition not in ("edges", "rows"):
+            raise ValueError("partition must be 'edges' or 'rows'")
         self.group = group
         self.rank = dist.get_rank(group) if rank is None else rank
         self.world = dist.get_world_size(group) if world is None else world
@@ -86,7 +90,9 @@ class ShardedDendriticPELSRuntime:
         batch, neurons = initial_state.shape
         self.batch, self.neurons = batch, neurons
         self.extension = extension if extension is not None else _native.load_native_extension()
-        self.shard = RowShard(neurons, batch, self.rank, self.world, device)
+        self.shard = RowShard(neurons, batch, self.rank, self.world, device,
+                              row_bounds(neurons, self.world,
+                                         in_rowptr if partition == "edges" else None))
         lo, hi = self.shard.lo, self.shard.hi
         self.compartment_dynamics = dynamics
         self.params = [p[lo:hi] for p in dynamics.parameters()]
@@ -318,12 +324,7 @@ class ShardedDendriticPELSRuntime:
 
     def gather(self, name: str) -> torch.Tensor:
         """The full [B, N] value of a per-row attribute (an all-gather)."""
-        local = getattr(self, name)
-        padded = torch.zeros(self.batch, self.shard.rows_per_rank, device=local.device)
-        padded[:, : local.shape[1]] = local
-        parts = [torch.empty_like(padded) for _ in range(self.world)]
-        dist.all_gather(parts, padded.contiguous(), group=self.group)
-        return torch.cat(parts, dim=1)[:, : self.neurons]
+        return self.shard.gather_rows(getattr(self, name), self.group)
 
 
 __all__ = ["ShardedDendriticPELSRuntime", "filtered_out_csr"]

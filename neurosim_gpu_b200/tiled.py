@@ -232,10 +232,51 @@ def _stages(piece_len: torch.Tensor, ctas: int) -> tuple[torch.Tensor, torch.Ten
     return stage_cta, stage_block, stage_of
 
 
+def split_length(fmt: int, edges: int, rows: int, blocks: int, longest: int) -> int:
+    """Sub-task split length in chunks for a graph (0: pieces are not split).
+
+    ``longest`` is the longest row piece in chunks.  Splitting only pays when a
+    mean row piece (edges per (row, block)) is longer than one split (166k /
+    25M fp32: 50 edges per piece, 36.9 vs 38.8 us with splits of 9 chunks;
+    166k / 10M: 20 edges, 19.2 unsplit vs 19.7 us); a degree-skewed graph gets
+    longer splits so that blocks x splits stays within MAX_PLANES.
+    """
+    split = SPLIT_CHUNKS.get(fmt, 0)
+    if split > 0 and edges < split * CHUNK * rows * blocks:
+        split = 0
+    if split > 0 and blocks * -(-longest // split) > MAX_PLANES:
+        split = -(-longest // max(1, MAX_PLANES // blocks))
+    return split
+
+
+def graph_split(in_rowptr: torch.Tensor, in_col: torch.Tensor, fmt: int, *, neurons: int,
+                cols: int, ctas: int, smem_limit: int, smem_bytes=None) -> int:
+    """:func:`split_length` of a whole graph, for the layouts of its row blocks.
+
+    A split cuts every row piece at the same edges, so row blocks laid out with
+    the whole graph's split length sum every row as the whole graph's layout
+    does (bit-identical sharded states), however their rows differ in degree.
+    """
+    if smem_bytes is None:
+        lib = native.load_library()
+        smem_bytes = lambda c, bufs: int(lib.nsb_tiled_smem_bytes(c, bufs))  # noqa: E731
+    blocks, block_cols, _ = plan_blocks(cols, ctas, smem_limit, smem_bytes)
+    rowptr = in_rowptr.to(torch.int64)
+    edges = int(rowptr[-1])
+    if edges == 0:
+        return 0
+    degree = rowptr[1:] - rowptr[:-1]
+    rows = torch.repeat_interleave(torch.arange(neurons, dtype=torch.int32,
+                                                device=in_col.device), degree)
+    piece = rows * blocks + (in_col // block_cols).to(torch.int32)
+    longest = -(-int(torch.bincount(piece, minlength=neurons * blocks).max()) // CHUNK)
+    return split_length(fmt, edges, neurons, blocks, longest)
+
+
 def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: torch.Tensor,
                        *, neurons: int, ctas: int, smem_limit: int, block_scales=None,
                        global_scale=None, smem_bytes=None, cols: int | None = None,
-                       scale_offset: int = 0) -> TiledLayout:
+                       scale_offset: int = 0, split: int | None = None) -> TiledLayout:
     """Build the tiled layout of one graph.
 
     ``weight`` is the CSR value array in its storage format (float32 / float16 /
@@ -358,20 +399,13 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
         task_rows[pair_task, pair_lane] = pair_row
         tiled_weight = torch.zeros(slots, dtype=weight.dtype, device=device)
         tiled_weight[slot] = weight
-    # Sub-tasks: chunks [h * split, (h + 1) * split) of a task.  Splitting
-    # only pays when a mean row piece (edges per (row, block)) is longer than
-    # one split (166k / 25M fp32: 50 edges per piece, 36.9 vs 38.8 us with
-    # splits of 9 chunks; 166k / 10M: 20 edges, 19.2 unsplit vs 19.7 us).  The
-    # mean is a property of the graph's density, so the row blocks of a
-    # sharded graph decide as the whole graph does.
+    # Sub-tasks: chunks [h * split, (h + 1) * split) of a task.  The split
+    # length is this graph's (split_length), or the one given: row blocks of a
+    # sharded graph take the whole graph's (graph_split).
     longest = int(task_chunks.max()) if n_tasks else 1
-    split = SPLIT_CHUNKS.get(fmt, 0)
-    if split > 0 and m < split * CHUNK * n * blocks:
-        split = 0
-    if split > 0:
-        if blocks * -(-longest // split) > MAX_PLANES:  # a degree-skewed graph
-            split = -(-longest // max(1, MAX_PLANES // blocks))
-    else:
+    if split is None:
+        split = split_length(fmt, m, n, blocks, longest)
+    if split <= 0:
         split = 1 << 30
     split = max(1, min(split, 1 << 30))
     splits = max(1, -(-longest // split))
