@@ -322,10 +322,14 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long
 // reset, so the critical path is one atomic and the pollers' next read.
 // Every launch that uses a workspace has the same grid size and passes every
 // barrier, so the counter is a multiple of the grid size between launches.
+// The arrival is a release (cumulative over the CTA's writes ordered before
+// it by the __syncthreads) and the poll an acquire, so no full fence is needed
+// on either side: a trailing fence also waited for this thread's own L2
+// prefetches in flight (166k / 25M: 34.85 -> 34.15 us per tick).
 // The wait is bounded: on timeout it records code 4.
 __device__ void grid_arrive_wait(unsigned long long* count, int* st) {
-  __threadfence();
-  const unsigned long long arrival = atomicAdd(count, 1ull);
+  unsigned long long arrival;
+  asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;" : "=l"(arrival) : "l"(count) : "memory");
   const unsigned long long target = (arrival / gridDim.x + 1) * gridDim.x;
   long long polls = 0;
   while (ld_acquire_gpu(count) < target) {
@@ -337,7 +341,6 @@ __device__ void grid_arrive_wait(unsigned long long* count, int* st) {
       __nanosleep(256);
     }
   }
-  __threadfence();
 }
 
 // The same barrier for the whole CTA.
