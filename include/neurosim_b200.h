@@ -45,7 +45,7 @@ extern "C" {
 #define NSB_API
 #endif
 
-#define NSB_ABI_VERSION 12
+#define NSB_ABI_VERSION 13
 
 enum nsb_status {
   NSB_OK = 0,
@@ -213,26 +213,27 @@ NSB_API int nsb_dendritic_event_noalloc(const nsb_tick* tick, float* current,
  *    stage_ptr[c+1]-1 (block stage_block[s]) with `buffers` (1 or 2) state
  *    blocks in shared memory.
  *  - Tasks of CTA c are task_ptr[c] .. task_ptr[c+1]-1.  tasks[4q..4q+3] =
- *    first slot, chunks C, stage (index among the CTA's stages) | h << 16 |
- *    S << 26, and a fourth word.  A task is split h (h < splits) of 32 rows'
- *    pieces in the stage's block: the lanes' edges 16*split_chunks*h + j,
- *    j < 4C, lane i's edge 16*split_chunks*h + j at slot
- *    first + 128*(j/4) + 4*i + j%4.  With S > 0 (h = 0) the task is C/S such
- *    segments of S chunks one after the other, each for its own 32 rows.
+ *    first slot, chunks n, stage (index among the CTA's stages) | h << 16 |
+ *    S << 26, and a fourth word.  With `chunk` = C slots per lane per chunk,
+ *    a task is split h (h < splits) of 32 rows' pieces in the stage's block:
+ *    the lanes' edges C*split_chunks*h + j, j < C*n, lane i's edge
+ *    C*split_chunks*h + j at slot first + 32C*(j/C) + C*i + j%C.  With S > 0
+ *    (h = 0) the task is n/S such segments of S chunks one after the other,
+ *    each for its own 32 rows.
  *    fp32: the fourth word is a row group g, and lane i of segment k owns row
  *    task_rows[32(g+k)+i] & 0x0FFFFFFF (0x0FFFFFFF: no row; S = 0: k = 0).
  *    Other formats (S = 0): lane i owns row task_rows[32q+i] & 0x0FFFFFFF and
  *    the fourth word is the first scale pair (NVFP4).
  *  - col[slot] is the column minus the block start (uint16); padding slots
- *    hold block_cols and weight 0.  n_slots is a multiple of 128.
+ *    hold block_cols and weight 0.  n_slots is a multiple of 32C.
  *  - NVFP4: codes are packed two per byte by slot (even slot in the low
  *    nibble).  If lane i's first edge in the block is at CSR position o, its
  *    edge j takes the E4M3 scale of CSR block (o + j) / 16; bits 28..31 of
  *    task_rows[32q+i] hold o % 16, and scale_pairs[first scale pair + 32*b + i]
  *    holds the scales of CSR blocks o/16 + b (low byte) and o/16 + b + 1 (high
  *    byte); past the lane's last edge both are 0.
- *  - Pointer alignment: tasks 16 B; col 8 B; weight 16 B (f32), 8 B (f16),
- *    4 B (E4M3), 2 B (NVFP4).
+ *  - Pointer alignment (C = 4 / 8): tasks 16 B; col 8 / 16 B; weight 16 / 32 B
+ *    (f32), 8 / 16 B (f16), 4 / 8 B (E4M3), 2 / 4 B (NVFP4).
  *  - The kernels trust the layout's contents (offsets, lengths, rows): pass
  *    layouts made by the builder.  `ctas` must not exceed the SM count: the
  *    tick is a cooperative launch with one CTA per SM. */
@@ -240,7 +241,7 @@ typedef struct nsb_tiled_layout {
   int32_t ctas, blocks, block_cols, buffers, format;
   int32_t splits;              /* sub-task splits per block (row-sum planes per block) */
   int32_t split_chunks;        /* chunks of one sub-task                    */
-  int32_t reserved;
+  int32_t chunk;               /* slots of one lane per chunk: 4 or 8 (C below) */
   int64_t n_stages, n_tasks, n_slots, n_scale_pairs;
   int64_t rows;                /* destination rows                          */
   int64_t cols;                /* length of the gathered source vector      */

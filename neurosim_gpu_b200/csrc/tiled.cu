@@ -63,8 +63,6 @@ constexpr int kProducerWarp = kTiledThreads / 32 - 1;
 constexpr long long kWaitLimit = 1ll << 24;  // try_wait polls before giving up
 constexpr long long kGridWaitLimit = 1ll << 24;  // polls of the grid barrier
 constexpr int kTiledHeader = 64;             // mbarriers + task counter
-constexpr int kChunk = 4;                    // slots of one lane per vector load
-constexpr int kChunkSlots = 32 * kChunk;     // slots of one warp-wide chunk
 // L2 prefetch of task data by the producer warp: bytes of tasks a CTA keeps
 // prefetched beyond the hand-out counter.  Only the narrower weight formats
 // use it: an fp32 tick streams more bytes than L2 holds, and prefetched lines
@@ -196,94 +194,183 @@ __device__ __forceinline__ void e2m1x4_to_float(uint32_t four, float (&v)[4]) {
   v[3] = b.y;
 }
 
-// Chunk readers: load(slot, scale_entry) fetches the weights of one lane's
-// four slots; decode() turns them into the four float32 weights, equal bit for
-// bit to the reference quantizer's dequantized values (precision.py:102-109):
-// fp8 -> e4m3(code) * g, nvfp4 -> e2m1(code) * (e4m3(block scale) * g).
-struct ChunkF32 {
+// 256-bit streaming load (eight 32-bit words).
+struct Words8 {
+  uint32_t v[8];
+};
+
+__device__ __forceinline__ Words8 ld_stream_v8(const void* p, uint64_t pol) {
+  Words8 r;
+  asm volatile(
+      "ld.global.nc.L1::no_allocate.L2::cache_hint.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8], %9;"
+      : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3]), "=r"(r.v[4]), "=r"(r.v[5]),
+        "=r"(r.v[6]), "=r"(r.v[7])
+      : "l"(p), "l"(pol));
+  return r;
+}
+
+// The K 16-bit block-relative columns of one lane's chunk: one 8-byte (K = 4)
+// or 16-byte (K = 8) load.
+template <int K>
+struct ChunkCols;
+
+template <>
+struct ChunkCols<4> {
+  using Raw = uint2;
+  static __device__ __forceinline__ Raw load(const uint16_t* col, int64_t slot, uint64_t pol) {
+    return ld_stream_v2(col + slot, pol);
+  }
+  static __device__ __forceinline__ uint32_t at(const Raw& r, int e) {
+    const uint32_t word = e < 2 ? r.x : r.y;
+    return (e & 1) ? word >> 16 : word & 0xFFFFu;
+  }
+};
+
+template <>
+struct ChunkCols<8> {
   using Raw = uint4;
+  static __device__ __forceinline__ Raw load(const uint16_t* col, int64_t slot, uint64_t pol) {
+    return ld_stream_v4(col + slot, pol);
+  }
+  static __device__ __forceinline__ uint32_t at(const Raw& r, int e) {
+    const uint32_t word = e < 2 ? r.x : e < 4 ? r.y : e < 6 ? r.z : r.w;
+    return (e & 1) ? word >> 16 : word & 0xFFFFu;
+  }
+};
+
+// Chunk readers, for K slots per lane (one lane's chunk): load(slot,
+// scale_entry) fetches the K weights; decode() turns them into K float32
+// weights, equal bit for bit to the reference quantizer's dequantized values
+// (precision.py:102-109): fp8 -> e4m3(code) * g, nvfp4 -> e2m1(code) *
+// (e4m3(block scale) * g).
+template <int K>
+struct ChunkF32 {
+  static constexpr int kSlots = K;
+  static constexpr bool kF32 = true;
+  using Raw = typename std::conditional<K == 4, uint4, Words8>::type;
   const float* w;
   __device__ __forceinline__ void prefetch(int first, int chunks, int, int) const {
-    prefetch_l2(w + first, static_cast<uint32_t>(chunks) * kChunkSlots * 4u);
+    prefetch_l2(w + first, static_cast<uint32_t>(chunks) * 32u * K * 4u);
   }
   __device__ __forceinline__ void set_scale(float) {}
   __device__ __forceinline__ Raw load(int64_t slot, int64_t, uint64_t pol) const {
-    return ld_stream_v4(w + slot, pol);
+    if constexpr (K == 4) return ld_stream_v4(w + slot, pol);
+    else return ld_stream_v8(w + slot, pol);
   }
-  __device__ __forceinline__ void decode(const Raw& r, uint32_t, float (&v)[4]) const {
-    v[0] = __uint_as_float(r.x);
-    v[1] = __uint_as_float(r.y);
-    v[2] = __uint_as_float(r.z);
-    v[3] = __uint_as_float(r.w);
+  __device__ __forceinline__ void decode(const Raw& r, uint32_t, float (&v)[K]) const {
+    if constexpr (K == 4) {
+      v[0] = __uint_as_float(r.x);
+      v[1] = __uint_as_float(r.y);
+      v[2] = __uint_as_float(r.z);
+      v[3] = __uint_as_float(r.w);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r.v[e]);
+    }
   }
 };
 
+template <int K>
 struct ChunkF16 {
-  using Raw = uint2;
+  static constexpr int kSlots = K;
+  static constexpr bool kF32 = false;
+  using Raw = typename std::conditional<K == 4, uint2, uint4>::type;
   const __half* w;
   __device__ __forceinline__ void prefetch(int first, int chunks, int, int) const {
-    prefetch_l2(w + first, static_cast<uint32_t>(chunks) * kChunkSlots * 2u);
+    prefetch_l2(w + first, static_cast<uint32_t>(chunks) * 32u * K * 2u);
   }
   __device__ __forceinline__ void set_scale(float) {}
   __device__ __forceinline__ Raw load(int64_t slot, int64_t, uint64_t pol) const {
-    return ld_stream_v2(w + slot, pol);
+    if constexpr (K == 4) return ld_stream_v2(w + slot, pol);
+    else return ld_stream_v4(w + slot, pol);
   }
-  __device__ __forceinline__ void decode(const Raw& r, uint32_t, float (&v)[4]) const {
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
-    v[0] = a.x;
-    v[1] = a.y;
-    v[2] = b.x;
-    v[3] = b.y;
+  __device__ __forceinline__ void decode(const Raw& r, uint32_t, float (&v)[K]) const {
+    const uint32_t* words = reinterpret_cast<const uint32_t*>(&r);
+#pragma unroll
+    for (int i = 0; i < K / 2; ++i) {
+      const float2 h = __half22float2(*reinterpret_cast<const __half2*>(words + i));
+      v[2 * i] = h.x;
+      v[2 * i + 1] = h.y;
+    }
   }
 };
 
+template <int K>
 struct ChunkE4M3 {
-  using Raw = uint32_t;
+  static constexpr int kSlots = K;
+  static constexpr bool kF32 = false;
+  using Raw = typename std::conditional<K == 4, uint32_t, uint2>::type;
   const uint8_t* codes;
   float g;
   __device__ __forceinline__ void prefetch(int first, int chunks, int, int) const {
-    prefetch_l2(codes + first, static_cast<uint32_t>(chunks) * kChunkSlots);
+    prefetch_l2(codes + first, static_cast<uint32_t>(chunks) * 32u * K);
   }
   __device__ __forceinline__ void set_scale(float s) { g = s; }
   __device__ __forceinline__ Raw load(int64_t slot, int64_t, uint64_t pol) const {
-    return ld_stream_u32(codes + slot, pol);
+    if constexpr (K == 4) return ld_stream_u32(codes + slot, pol);
+    else return ld_stream_v2(codes + slot, pol);
   }
-  __device__ __forceinline__ void decode(Raw r, uint32_t, float (&v)[4]) const {
-    const float2 a = e4m3x2_to_float2(r & 0xFFFFu);
-    const float2 b = e4m3x2_to_float2(r >> 16);
-    v[0] = __fmul_rn(a.x, g);
-    v[1] = __fmul_rn(a.y, g);
-    v[2] = __fmul_rn(b.x, g);
-    v[3] = __fmul_rn(b.y, g);
+  __device__ __forceinline__ void decode(const Raw& r, uint32_t, float (&v)[K]) const {
+    const uint32_t* words = reinterpret_cast<const uint32_t*>(&r);
+#pragma unroll
+    for (int i = 0; i < K / 4; ++i) {
+      const float2 a = e4m3x2_to_float2(words[i] & 0xFFFFu);
+      const float2 b = e4m3x2_to_float2(words[i] >> 16);
+      v[4 * i] = __fmul_rn(a.x, g);
+      v[4 * i + 1] = __fmul_rn(a.y, g);
+      v[4 * i + 2] = __fmul_rn(b.x, g);
+      v[4 * i + 3] = __fmul_rn(b.y, g);
+    }
   }
 };
 
+template <int K>
 struct ChunkNVFP4 {
-  using Raw = uint32_t;  // four codes (low 16 bits) | scale pair << 16
+  static constexpr int kSlots = K;
+  static constexpr bool kF32 = false;
+  // K = 4: four codes (low 16 bits) | scale pair << 16; K = 8: eight codes, scale pair.
+  using Raw = typename std::conditional<K == 4, uint32_t, uint2>::type;
   const uint8_t* codes;
   const uint16_t* pairs;
   float g;
   // Codes and the scale-table rows a split of C chunks starting at chunk c0
-  // of the lanes' pieces reads: rows (4 c0) / 16 .. (4 (c0 + C) + 11) / 16.
+  // of the lanes' pieces reads: rows (K c0) / 16 .. (K (c0 + C) + 15 - K) / 16.
   __device__ __forceinline__ void prefetch(int first, int chunks, int entry, int c0) const {
-    prefetch_l2(codes + (first >> 1), static_cast<uint32_t>(chunks) * (kChunkSlots / 2));
-    const int r0 = (kChunk * c0) >> 4;
-    const int r1 = (kChunk * (c0 + chunks) + 11) >> 4;
+    prefetch_l2(codes + (first >> 1), static_cast<uint32_t>(chunks) * 16u * K);
+    const int r0 = (K * c0) >> 4;
+    const int r1 = (K * (c0 + chunks) + 15 - K) >> 4;
     prefetch_l2(pairs + entry + r0 * 32, static_cast<uint32_t>(r1 - r0 + 1) * 64u);
   }
   __device__ __forceinline__ void set_scale(float s) { g = s; }
   __device__ __forceinline__ Raw load(int64_t slot, int64_t entry, uint64_t pol) const {
-    return ld_stream_u16(codes + (slot >> 1), pol) | (static_cast<uint32_t>(__ldg(pairs + entry)) << 16);
+    if constexpr (K == 4) {
+      return ld_stream_u16(codes + (slot >> 1), pol) | (static_cast<uint32_t>(__ldg(pairs + entry)) << 16);
+    } else {
+      return make_uint2(ld_stream_u32(codes + (slot >> 1), pol), __ldg(pairs + entry));
+    }
   }
-  __device__ __forceinline__ void decode(Raw r, uint32_t tag, float (&v)[4]) const {
-    const float2 scale = e4m3x2_to_float2(r >> 16);
+  __device__ __forceinline__ void decode(const Raw& r, uint32_t tag, float (&v)[K]) const {
+    uint32_t codes4[K / 4];
+    uint32_t pair;
+    if constexpr (K == 4) {
+      codes4[0] = r & 0xFFFFu;
+      pair = r >> 16;
+    } else {
+      codes4[0] = r.x & 0xFFFFu;
+      codes4[1] = r.x >> 16;
+      pair = r.y;
+    }
+    const float2 scale = e4m3x2_to_float2(pair);
     const float f0 = __fmul_rn(scale.x, g), f1 = __fmul_rn(scale.y, g);
     const int phase = (tag >> kTagPhase) & 15;  // edge e is in the next block iff phase + e >= 16
-    float q[4];
-    e2m1x4_to_float(r & 0xFFFFu, q);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = __fmul_rn(q[e], phase + e >= 16 ? f1 : f0);
+    for (int i = 0; i < K / 4; ++i) {
+      float q[4];
+      e2m1x4_to_float(codes4[i], q);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        v[4 * i + e] = __fmul_rn(q[e], phase + 4 * i + e >= 16 ? f1 : f0);
+    }
   }
 };
 
@@ -403,6 +490,9 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
                   Out product, bool update, int ticks, int* status, Peers px,
                   const unsigned long long* gate_count, unsigned long long gate_min) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
+  constexpr int kK = W::kSlots;              // slots of one lane per chunk
+  constexpr int kChunkSlots = 32 * kK;       // slots of one warp-wide chunk
+  using Cols = ChunkCols<kK>;
   const int nbuf = L.buffers;
   const int cb_pad = L.block_cols + 4;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);            // [2]
@@ -588,7 +678,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
       // formats keep one segment per task with its row word (NVFP4: and the
       // lane's decode phase) read with the task: their kernels have fewer
       // registers to spare (fp16 at 166k / 25M: 30.6 -> 32.9 us segmented).
-      constexpr bool kPhased = !std::is_same<W, ChunkF32>::value;
+      constexpr bool kPhased = !W::kF32;
       auto grab = [&]() {
         int q = 0;
         if (lane == 0) q = atomicAdd(next_task, 1);
@@ -616,7 +706,8 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
       int group = 0;         // row group of the current segment
       uint32_t tag_base = 0;
       // Issue the loads of the next chunk into one ring entry (tag 0: none left).
-      auto issue = [&](typename W::Raw& raw, uint2& cols, uint32_t& tag, uint32_t& tag_row) {
+      auto issue = [&](typename W::Raw& raw, typename Cols::Raw& cols, uint32_t& tag,
+                       uint32_t& tag_row) {
         // On a task switch the next task (already fetched) becomes current and
         // the look-ahead is refilled: a shared-counter grab, then the metadata
         // load, which waits for the grab.  For fp32 the refill comes after
@@ -624,7 +715,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
         // 37.4 -> 36.1 us, 1.33M / 200M 653 -> 629 us per tick); the narrower
         // formats refill first, which keeps the hand-out counter, and with it
         // the producer's prefetch window, ahead (NVFP4 33.7 vs 36.5 us).
-        constexpr bool kLoadsFirst = std::is_same<W, ChunkF32>::value;
+        constexpr bool kLoadsFirst = W::kF32;
         bool refill = false;
         while (left == 0) {  // warp-uniform
           if (refill) {  // a task without chunks: take the next one now
@@ -635,7 +726,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
             tag = 0;
             return;
           }
-          slot = next_meta.x + lane * kChunk;
+          slot = next_meta.x + lane * kK;
           left = next_meta.y;
           if (kPhased) {
             chunk = ((next_meta.z >> 16) & 0x3FF) * L.split_chunks;  // chunk index within the piece
@@ -657,9 +748,9 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
             refill = false;
           }
         }
-        const int p = kPhased ? phase + chunk * kChunk : 0;
+        const int p = kPhased ? phase + chunk * kK : 0;
         raw = w.load(slot, entry + (p >> 4) * 32, pol);
-        cols = ld_stream_v2(L.col + slot, pol);
+        cols = Cols::load(L.col, slot, pol);
         if (refill) {
           next_q = grab();
           fetch();
@@ -683,7 +774,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
 
       // ---- the ring ---------------------------------------------------------
       typename W::Raw raw[D];
-      uint2 cols[D];
+      typename Cols::Raw cols[D];
       uint32_t tag[D], rows[D];
 #pragma unroll
       for (int u = 0; u < D; ++u) issue(raw[u], cols[u], tag[u], rows[u]);
@@ -706,12 +797,10 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
               part = L.part + static_cast<int64_t>(__ldg(L.stage_block + stage_first + s)) *
                                   L.splits * L.rows;
             }
-            float v[4];
+            float v[kK];
             w.decode(raw[u], g, v);
-            acc = fmaf(v[0], sb[cols[u].x & 0xFFFFu], acc);
-            acc = fmaf(v[1], sb[cols[u].x >> 16], acc);
-            acc = fmaf(v[2], sb[cols[u].y & 0xFFFFu], acc);
-            acc = fmaf(v[3], sb[cols[u].y >> 16], acc);
+#pragma unroll
+            for (int e = 0; e < kK; ++e) acc = fmaf(v[e], sb[Cols::at(cols[u], e)], acc);
             if (g & kTagLast) {
               if (rows[u] != kRowMask) part[(g >> kTagSplit) * L.rows + rows[u]] = acc;
               acc = -0.0f;
@@ -926,6 +1015,38 @@ size_t tiled_workspace_bytes(const nsb_tiled_layout& layout) {
                    static_cast<size_t>(layout.rows) * 4;
 }
 
+// The kernel for the layout's weight format at K slots per lane per chunk,
+// with a ring of D chunks (K * D = 16 slots of loads in flight per lane).
+template <int K, int D>
+cudaError_t launch_tiled_format(const nsb_tiled_layout& layout, const TiledArgs& L,
+                                const TickArgs& t, const float* x, bool update, int ticks,
+                                const TickOut& out, const Out& product, int* status, int ctas,
+                                cudaStream_t stream, const Peers& px, const TiledGate& gate) {
+  if (gate.count) {  // the hybrid PELS propagate: float32 weights only (checked by the caller)
+    return launch_tiled_kernel<ChunkF32<K>, D, false, true>(
+        L, ChunkF32<K>{static_cast<const float*>(layout.weight)}, t, x, out, product, update,
+        ticks, status, ctas, stream, Peers{}, gate);
+  }
+  switch (layout.format) {
+    case NSB_WEIGHT_F16:
+      return launch_tiled_variant<ChunkF16<K>, D>(
+          L, ChunkF16<K>{static_cast<const __half*>(layout.weight)}, t, x, out, product, update,
+          ticks, status, ctas, stream, px);
+    case NSB_WEIGHT_E4M3:
+      return launch_tiled_variant<ChunkE4M3<K>, D>(
+          L, ChunkE4M3<K>{static_cast<const uint8_t*>(layout.weight), 0.0f}, t, x, out, product,
+          update, ticks, status, ctas, stream, px);
+    case NSB_WEIGHT_NVFP4:
+      return launch_tiled_variant<ChunkNVFP4<K>, D>(
+          L, ChunkNVFP4<K>{static_cast<const uint8_t*>(layout.weight), layout.scale_pairs, 0.0f},
+          t, x, out, product, update, ticks, status, ctas, stream, px);
+    default:
+      return launch_tiled_variant<ChunkF32<K>, D>(
+          L, ChunkF32<K>{static_cast<const float*>(layout.weight)}, t, x, out, product, update,
+          ticks, status, ctas, stream, px);
+  }
+}
+
 cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, const float* x,
                          bool update, int ticks, const TickOut& out, const Out& product,
                          void* workspace, int* status, cudaStream_t stream,
@@ -993,29 +1114,11 @@ cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, cons
     if (staged && cap >= 64) L.stage_rows = static_cast<int32_t>(std::min<int64_t>(cap, 1 << 20));
   }
   const int ctas = layout.ctas;
-  if (gate.count) {  // the hybrid PELS propagate: float32 weights only (checked by the caller)
-    return launch_tiled_kernel<ChunkF32, 4, false, true>(
-        L, ChunkF32{static_cast<const float*>(layout.weight)}, t, x, out, product, update, ticks,
-        status, ctas, stream, Peers{}, gate);
-  }
-  switch (layout.format) {
-    case NSB_WEIGHT_F16:
-      return launch_tiled_variant<ChunkF16, 4>(L, ChunkF16{static_cast<const __half*>(layout.weight)},
-                                               t, x, out, product, update, ticks, status, ctas,
-                                               stream, px);
-    case NSB_WEIGHT_E4M3:
-      return launch_tiled_variant<ChunkE4M3, 4>(
-          L, ChunkE4M3{static_cast<const uint8_t*>(layout.weight), 0.0f}, t, x, out, product,
-          update, ticks, status, ctas, stream, px);
-    case NSB_WEIGHT_NVFP4:
-      return launch_tiled_variant<ChunkNVFP4, 4>(
-          L, ChunkNVFP4{static_cast<const uint8_t*>(layout.weight), layout.scale_pairs, 0.0f}, t,
-          x, out, product, update, ticks, status, ctas, stream, px);
-    default:
-      return launch_tiled_variant<ChunkF32, 4>(L, ChunkF32{static_cast<const float*>(layout.weight)},
-                                               t, x, out, product, update, ticks, status, ctas,
-                                               stream, px);
-  }
+  return layout.chunk == 8
+             ? launch_tiled_format<8, 2>(layout, L, t, x, update, ticks, out, product, status,
+                                         ctas, stream, px, gate)
+             : launch_tiled_format<4, 4>(layout, L, t, x, update, ticks, out, product, status,
+                                         ctas, stream, px, gate);
 }
 
 }  // namespace nsb

@@ -77,7 +77,7 @@ class _TiledLayout(ctypes.Structure):
     _fields_ = [("ctas", ctypes.c_int32), ("blocks", ctypes.c_int32),
                 ("block_cols", ctypes.c_int32), ("buffers", ctypes.c_int32),
                 ("format", ctypes.c_int32), ("splits", ctypes.c_int32),
-                ("split_chunks", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("split_chunks", ctypes.c_int32), ("chunk", ctypes.c_int32),
                 ("n_stages", ctypes.c_int64), ("n_tasks", ctypes.c_int64),
                 ("n_slots", ctypes.c_int64), ("n_scale_pairs", ctypes.c_int64),
                 ("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
@@ -217,7 +217,7 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
         getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
-    if lib.nsb_abi_version() != 12:
+    if lib.nsb_abi_version() != 13:
         raise RuntimeError("libneurosim_b200.so ABI version mismatch")
     return lib
 

@@ -15,19 +15,22 @@ and streams the edges with vector loads:
   runs the full-row stages of blocks ``c, c + ctas, ...``, double-buffered.)
 * For each stage, the rows' non-empty pieces (their edges inside the block, a
   contiguous run of the original CSR row) are sorted by chunk count (then by
-  row) and grouped 32 at a time into tasks.  A task has ``chunks`` chunks;
-  lane ``i`` owns one row
-  and its edge ``j`` sits at slot ``first + 128 * (j // 4) + 4 * i + j % 4``,
-  so one lane reads four edges with one vector load and a warp's loads cover
-  128 consecutive slots.  Shorter pieces are padded with column ``block_cols``
-  (a zero in shared memory) and weight 0.  Consecutive groups of one stage
-  with the same chunk count are merged into tasks of several such segments
-  (up to ``MERGE_CHUNKS`` chunks; fp32 only), each segment's 32 rows being
-  one row group of ``task_rows``.
+  row) and grouped 32 at a time into tasks.  A chunk is ``K`` slots per lane
+  (``chunk``: 4, or 8 when the pieces average at least WIDE_CHUNK_MIN_EDGES
+  edges); a task has ``chunks`` chunks, lane ``i`` owns one row and its edge
+  ``j`` sits at slot ``first + 32K * (j // K) + K * i + j % K``, so one lane
+  reads K edges with one vector load of columns and one of weights and a
+  warp's loads cover 32K consecutive slots.  Shorter pieces are padded with
+  column ``block_cols`` (a zero in shared memory) and weight 0.  A lane sums
+  its piece in CSR order whatever K is.  Consecutive groups of one stage with
+  the same chunk count are merged into tasks of several such segments (up to
+  MERGE_SLOTS slots per lane; fp32 only), each segment's 32 rows being one
+  row group of ``task_rows``.
 * Columns are stored relative to their block as uint16 (2 bytes per edge
   instead of the CSR's 4).
 * A task is cut into sub-tasks of ``split_chunks`` chunks (edges
-  ``16 * split_chunks * h ...`` of every lane's piece form split ``h``), so the
+  ``K * split_chunks * h ...`` of every lane's piece form split ``h``; the
+  split is a whole number of edges, SPLIT_EDGES, for either K), so the
   CTA's work comes in pieces small enough to balance over its warps.  Each
   sub-task's per-row sums go to a workspace plane ``part[block][h][row]``;
   after a grid-wide barrier every CTA adds the planes of its share of the rows
@@ -57,28 +60,36 @@ import torch
 from . import native
 
 LANES = 32
-CHUNK = 4                     # slots of one lane per vector load
-CHUNK_SLOTS = LANES * CHUNK   # slots of one warp-wide chunk
+CHUNK = 4                     # slots of one lane per chunk (the narrow width)
+WIDE_CHUNK = 8                # the wide width: one 16-byte column load per lane
+# A layout whose row pieces average at least this many edges uses wide chunks:
+# half the loads, tags and ring steps per edge, for ~3.5 slots of padding per
+# piece instead of ~1.5.  Measured (fp32, us per tick, 4 -> 8 slots): 166k /
+# 25M 35.4 -> 32.0 (fp16 28.9 -> 24.2, fp8 29.8 -> 23.3, NVFP4 33.0 -> 27.6),
+# 166k / 10M 18.2 -> 17.2, one rank of the 1.33M / 200M graph on 8 GPUs (6.5
+# edges per piece) 56.5 -> 53.4, that graph on one GPU 478 -> 451.
+WIDE_CHUNK_MIN_EDGES = 4
 MAX_BLOCK_COLS = 65504        # 16-bit block-relative columns, block_cols = padding
 MAX_ROWS = (1 << 28) - 1      # 28-bit rows in task_rows; ROW_NONE marks a padding lane
 ROW_NONE = MAX_ROWS
 WARPS = 31                    # consumer warps of a CTA
-# Split length of sub-tasks in chunks (4 edges), by weight format (0: tasks
-# are not split).  Splitting shortens the tail of a tick but adds row-sum
-# planes that the update reads; measured at 166k / 25M it pays off for fp32
-# (36.9 vs 38.8 us with splits of 9 chunks) and costs the narrower formats
-# (fp16 32.1 vs 30.5 us, NVFP4 38.5 vs 33.8 us).  A constant length cuts every
-# row at the same edges whatever rows a layout holds, so sharded sums stay
-# bit-identical.
-SPLIT_CHUNKS = {native.F32: 9, native.F16: 0, native.E4M3: 0, native.NVFP4: 0}
+# Split length of sub-tasks in edges (a multiple of both chunk widths), by
+# weight format (0: tasks are not split).  Splitting shortens the tail of a
+# tick but adds row-sum planes that the update reads; measured at 166k / 25M it
+# pays off for fp32 (8-slot chunks, 2,000 ticks: splits of 16 / 24 / 32 / 40 /
+# 48 / 64 edges 47.5 / 36.6 / 31.0 / 31.9 / 32.1 / 32.7 us) and, with 4-slot
+# chunks, costs the narrower formats (fp16 32.1 vs 30.5 us, NVFP4 38.5 vs
+# 33.8 us).  A constant length cuts every row at the same edges whatever rows
+# or chunk width a layout has, so sharded sums stay bit-identical.
+SPLIT_EDGES = {native.F32: 32, native.F16: 0, native.E4M3: 0, native.NVFP4: 0}
 MAX_PLANES = 32               # cap on blocks x splits (only degree-skewed graphs reach it)
-# Chunks a task of several 32-piece segments holds at most (unsplit layouts;
-# split layouts merge up to one split).  Layouts of short pieces otherwise
-# hand out one task per ~2 chunks.  Measured on one rank's share of the 1.33M /
-# 200M graph (166k rows x 1.33M columns, 23 blocks, 1-4 chunk pieces): 74.3 us
-# per tick unmerged, 56.0 / 54.9 / 54.6 / 54.9 us with tasks of up to
-# 6 / 7 / 8 / 10 chunks.
-MERGE_CHUNKS = 8
+# Slots per lane a task of several 32-piece segments holds at most (unsplit
+# layouts; split layouts merge up to one split).  Layouts of short pieces
+# otherwise hand out one task per ~2 chunks.  Measured on one rank's share of
+# the 1.33M / 200M graph (166k rows x 1.33M columns, 23 blocks, 1-4 chunk
+# pieces of 4 slots): 74.3 us per tick unmerged, 56.0 / 54.9 / 54.6 / 54.9 us
+# with tasks of up to 24 / 28 / 32 / 40 slots per lane.
+MERGE_SLOTS = 32
 MAX_SEGMENT_CHUNKS = 63       # 6-bit segment length in a task's third word
 
 
@@ -119,6 +130,7 @@ class TiledLayout:
     cols: int = 0         # length of the gathered source vector (0: same as neurons)
     splits: int = 1       # sub-task planes per block
     split_chunks: int = 1 << 20  # chunks of one sub-task
+    chunk: int = CHUNK    # slots of one lane per chunk (4 or 8)
     _workspace: torch.Tensor | None = field(default=None, repr=False)
 
     def __post_init__(self) -> None:
@@ -165,7 +177,7 @@ class TiledLayout:
             return t.data_ptr() if t is not None and t.numel() else None
         return native._TiledLayout(
             self.ctas, self.blocks, self.block_cols, self.buffers, self.format, self.splits,
-            self.split_chunks, 0, self.n_stages, self.n_tasks, self.n_slots,
+            self.split_chunks, self.chunk, self.n_stages, self.n_tasks, self.n_slots,
             self.scale_pairs.numel() if self.scale_pairs is not None else 0,
             self.neurons, self.cols,
             ptr(self.stage_ptr), ptr(self.stage_block), ptr(self.task_ptr), ptr(self.tasks),
@@ -233,20 +245,27 @@ def _stages(piece_len: torch.Tensor, ctas: int) -> tuple[torch.Tensor, torch.Ten
 
 
 def split_length(fmt: int, edges: int, rows: int, blocks: int, longest: int) -> int:
-    """Sub-task split length in chunks for a graph (0: pieces are not split).
+    """Sub-task split length in edges for a graph (0: pieces are not split).
 
-    ``longest`` is the longest row piece in chunks.  Splitting only pays when a
+    ``longest`` is the longest row piece in edges.  Splitting only pays when a
     mean row piece (edges per (row, block)) is longer than one split (166k /
-    25M fp32: 50 edges per piece, 36.9 vs 38.8 us with splits of 9 chunks;
+    25M fp32: 50 edges per piece, 36.9 vs 38.8 us with splits of 36 edges;
     166k / 10M: 20 edges, 19.2 unsplit vs 19.7 us); a degree-skewed graph gets
-    longer splits so that blocks x splits stays within MAX_PLANES.
+    longer splits so that blocks x splits stays within MAX_PLANES.  Always a
+    multiple of WIDE_CHUNK, so both chunk widths cut a piece at the same edges.
     """
-    split = SPLIT_CHUNKS.get(fmt, 0)
-    if split > 0 and edges < split * CHUNK * rows * blocks:
+    split = SPLIT_EDGES.get(fmt, 0)
+    if split > 0 and edges < split * rows * blocks:
         split = 0
     if split > 0 and blocks * -(-longest // split) > MAX_PLANES:
         split = -(-longest // max(1, MAX_PLANES // blocks))
+        split = -(-split // WIDE_CHUNK) * WIDE_CHUNK
     return split
+
+
+def chunk_width(edges: int, pieces: int) -> int:
+    """Slots per lane per chunk for a layout with ``pieces`` non-empty row pieces."""
+    return WIDE_CHUNK if edges >= WIDE_CHUNK_MIN_EDGES * max(pieces, 1) else CHUNK
 
 
 def graph_split(in_rowptr: torch.Tensor, in_col: torch.Tensor, fmt: int, *, neurons: int,
@@ -269,14 +288,15 @@ def graph_split(in_rowptr: torch.Tensor, in_col: torch.Tensor, fmt: int, *, neur
     rows = torch.repeat_interleave(torch.arange(neurons, dtype=torch.int32,
                                                 device=in_col.device), degree)
     piece = rows * blocks + (in_col // block_cols).to(torch.int32)
-    longest = -(-int(torch.bincount(piece, minlength=neurons * blocks).max()) // CHUNK)
+    longest = int(torch.bincount(piece, minlength=neurons * blocks).max())
     return split_length(fmt, edges, neurons, blocks, longest)
 
 
 def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: torch.Tensor,
                        *, neurons: int, ctas: int, smem_limit: int, block_scales=None,
                        global_scale=None, smem_bytes=None, cols: int | None = None,
-                       scale_offset: int = 0, split: int | None = None) -> TiledLayout:
+                       scale_offset: int = 0, split: int | None = None,
+                       chunk: int | None = None) -> TiledLayout:
     """Build the tiled layout of one graph.
 
     ``weight`` is the CSR value array in its storage format (float32 / float16 /
@@ -329,7 +349,11 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
     group = stage_of.flatten()
     lengths = piece_len.flatten()
     order = torch.nonzero(lengths).flatten()
-    order = order[torch.sort(-((lengths[order] + CHUNK - 1) // CHUNK), stable=True).indices]
+    K = chunk if chunk is not None else chunk_width(m, order.numel())
+    if K not in (CHUNK, WIDE_CHUNK):
+        raise ValueError("chunk must be 4 or 8")
+    K_SLOTS = LANES * K
+    order = order[torch.sort(-((lengths[order] + K - 1) // K), stable=True).indices]
     order = order[torch.sort(group[order], stable=True).indices]
     sorted_group = group[order]
     group_size = torch.bincount(sorted_group, minlength=n_stages)
@@ -346,9 +370,9 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
     torch.cumsum(tasks_per_cta, 0, out=task_ptr[1:])
     task_len = torch.zeros(n_tasks, dtype=torch.int64, device=device)
     task_len.scatter_reduce_(0, pair_task, lengths[order], reduce="amax")
-    task_chunks = (task_len + CHUNK - 1) // CHUNK
-    task_first = torch.cumsum(task_chunks * CHUNK_SLOTS, 0) - task_chunks * CHUNK_SLOTS
-    slots = int((task_chunks * CHUNK_SLOTS).sum())
+    task_chunks = (task_len + K - 1) // K
+    task_first = torch.cumsum(task_chunks * K_SLOTS, 0) - task_chunks * K_SLOTS
+    slots = int((task_chunks * K_SLOTS).sum())
     if slots >= 2**31:
         raise ValueError("tiled layout exceeds 2^31 slots")
     task_stage = torch.repeat_interleave(arange(n_stages), tasks_per_stage)
@@ -360,8 +384,8 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
     rank_of_pair[order] = arange(order.numel())
     r = rank_of_pair[piece]
     within = arange(m) - piece_start[piece]
-    slot = (task_first[pair_task[r]] + (within // CHUNK) * CHUNK_SLOTS + pair_lane[r] * CHUNK
-            + within % CHUNK)
+    slot = (task_first[pair_task[r]] + (within // K) * K_SLOTS + pair_lane[r] * K
+            + within % K)
     col = torch.full((slots,), block_cols, dtype=torch.int64, device=device)
     col[slot] = col64 - block_of_edge * block_cols
 
@@ -376,7 +400,7 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
         codes[slot] = nibbles
         tiled_weight = (codes[0::2] | (codes[1::2] << 4)).contiguous()
         # Chunk c of a lane with phase p reads pair row (p + 4c) // 16 <= (11 + 4C) // 16.
-        table_rows = ((11 + CHUNK * task_chunks) >> 4) + 1
+        table_rows = ((15 - K + K * task_chunks) >> 4) + 1
         entries = table_rows * LANES
         scale_first = torch.cumsum(entries, 0) - entries
         n_pairs = int(entries.sum())
@@ -402,17 +426,16 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
     # Sub-tasks: chunks [h * split, (h + 1) * split) of a task.  The split
     # length is this graph's (split_length), or the one given: row blocks of a
     # sharded graph take the whole graph's (graph_split).
-    longest = int(task_chunks.max()) if n_tasks else 1
     if split is None:
-        split = split_length(fmt, m, n, blocks, longest)
-    if split <= 0:
-        split = 1 << 30
+        split = split_length(fmt, m, n, blocks, int(task_len.max()) if n_tasks else 1)
+    longest = int(task_chunks.max()) if n_tasks else 1   # in chunks from here on
+    split = split // K if split > 0 else 1 << 30
     split = max(1, min(split, 1 << 30))
     splits = max(1, -(-longest // split))
     unsplit = splits == 1
     split = min(split, max(longest, 1))
     # Tasks: runs of consecutive groups of one stage with one chunk count c are
-    # merged, up to MERGE_CHUNKS chunks (and one split) per task, into tasks
+    # merged, up to MERGE_SLOTS slots per lane (and one split) per task, into tasks
     # of several segments (c chunks each, one group's 32 pieces per segment),
     # so layouts of short pieces do not hand out a task per 32 pieces.  Only
     # fp32: the narrower formats keep one group per task (NVFP4's task carries
@@ -420,7 +443,7 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
     # consecutive in slot order.
     group_chunks = task_chunks
     if fmt == native.F32 and n_tasks:
-        target = MERGE_CHUNKS if unsplit else min(split, MERGE_CHUNKS)
+        target = MERGE_SLOTS // K if unsplit else min(split, MERGE_SLOTS // K)
         run_head = torch.ones(n_tasks, dtype=torch.bool, device=device)
         run_head[1:] = (task_stage[1:] != task_stage[:-1]) | (group_chunks[1:] != group_chunks[:-1])
         run_first = torch.nonzero(run_head).flatten()
@@ -452,7 +475,7 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
     sub_order = sub_order[torch.sort(sub_stage[sub_order], stable=True).indices]
     sub_task, sub_h, sub_chunks = sub_task[sub_order], sub_h[sub_order], sub_chunks[sub_order]
     sub_group = first_group[sub_task]
-    tasks = torch.stack((task_first[sub_group] + sub_h * split * CHUNK_SLOTS, sub_chunks,
+    tasks = torch.stack((task_first[sub_group] + sub_h * split * K_SLOTS, sub_chunks,
                          task_stage_local[sub_group] | (sub_h << 16) | (segment[sub_task] << 26),
                          merged_word[sub_task]), dim=1)
     subs_per_cta = torch.zeros(ctas, dtype=torch.int64, device=device)
@@ -466,7 +489,7 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
         task_ptr=task_ptr.to(torch.int32), tasks=tasks.to(torch.int32).contiguous(),
         task_rows=_i32(task_rows).contiguous(), col=_u16(col), weight=tiled_weight,
         scale_pairs=scale_pairs, global_scale=global_scale, cols=cols, splits=splits,
-        split_chunks=split)
+        split_chunks=split, chunk=K)
 
 
 def emulate(layout: TiledLayout, source: torch.Tensor) -> torch.Tensor:
@@ -485,7 +508,8 @@ def emulate(layout: TiledLayout, source: torch.Tensor) -> torch.Tensor:
     by_slot = torch.argsort(first)           # (sub-)tasks are not stored in slot order
     task = by_slot[torch.searchsorted(first[by_slot], slots, right=True) - 1]
     local = slots - first[task]
-    chunk, lane, e = local // CHUNK_SLOTS, (local % CHUNK_SLOTS) // CHUNK, local % CHUNK
+    K = layout.chunk
+    chunk, lane, e = local // (LANES * K), (local % (LANES * K)) // K, local % K
     third = layout.tasks[:, 2].long()
     if layout.format != native.F32:
         word = layout.task_rows.long()[task, lane] & 0xFFFFFFFF
@@ -520,7 +544,7 @@ def _decoded_slots(layout: TiledLayout, task, chunk, lane, e, word) -> torch.Ten
     if layout.format == native.E4M3:
         return e4m3_to_float(layout.weight) * g
     codes = torch.stack((layout.weight & 15, layout.weight >> 4), dim=1).flatten()
-    p = (word >> 28) + CHUNK * chunk
+    p = (word >> 28) + layout.chunk * chunk
     entry = layout.tasks[:, 3].long()[task] + (p >> 4) * LANES + lane
     pair = layout.scale_pairs.long()[entry] & 0xFFFF
     scale = torch.where((p & 15) + e >= 16, pair >> 8, pair & 0xFF).to(torch.uint8)

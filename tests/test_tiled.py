@@ -28,18 +28,22 @@ def _smem_bytes():
     return lambda cols, bufs: int(lib.nsb_tiled_smem_bytes(cols, bufs))
 
 
+@pytest.mark.parametrize("chunk", [None, 4, 8])
 @pytest.mark.parametrize("fmt", ["fp32", "fp16", "fp8", "nvfp4"])
 @pytest.mark.parametrize("n,m,ctas,smem", [(97, 600, 4, 232448), (2000, 60000, 8, 8000),
                                            (5000, 100000, 16, 6000), (3001, 40001, 5, 232448),
                                            (5000, 100000, 2, 6000), (1, 0, 3, 232448),
-                                           (300, 9000, 148, 232448)])
-def test_layout_emulation_matches_oracle_cpu(fmt, n, m, ctas, smem):
-    """The layout builder alone, emulated on CPU (no GPU needed)."""
+                                           (300, 9000, 148, 232448), (2000, 200000, 8, 232448)])
+def test_layout_emulation_matches_oracle_cpu(fmt, n, m, ctas, smem, chunk):
+    """The layout builder alone, emulated on CPU (no GPU needed), at either
+    chunk width (None: the builder's choice from the mean piece length)."""
     graph = random_topology(n, m, device="cpu", seed=3)
     weight, scales, scale, decoded = _packed(graph, fmt)
     layout = build_tiled_layout(graph.in_rowptr, graph.in_col, weight, neurons=n, ctas=ctas,
                                 smem_limit=smem, block_scales=scales, global_scale=scale,
-                                smem_bytes=_smem_bytes())
+                                smem_bytes=_smem_bytes(), chunk=chunk)
+    assert chunk is None or layout.chunk == chunk
+    assert layout.n_slots % (32 * layout.chunk) == 0
     x = torch.rand(1, n, generator=torch.Generator().manual_seed(1))
     want = oracle.spmv(csr_of(graph, decoded), npy(x))[0]
     np.testing.assert_allclose(emulate(layout, x).numpy(), want, atol=1e-6, rtol=0)
@@ -47,16 +51,19 @@ def test_layout_emulation_matches_oracle_cpu(fmt, n, m, ctas, smem):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("chunk", [4, 8])
 @pytest.mark.parametrize("fmt", ["fp32", "fp16", "fp8", "nvfp4"])
 @pytest.mark.parametrize("n,m,ctas,smem", [(97, 600, 4, 232448), (2000, 60000, 8, 8000),
                                            (5000, 100000, 16, 6000), (3001, 40001, 5, 232448),
-                                           (20000, 400000, 148, 24000), (5000, 100000, 2, 6000)])
-def test_tiled_tick_matches_oracle(fmt, n, m, ctas, smem):
+                                           (20000, 400000, 148, 24000), (5000, 100000, 2, 6000),
+                                           (2000, 200000, 8, 232448)])
+def test_tiled_tick_matches_oracle(fmt, n, m, ctas, smem, chunk):
     ext = load_native_extension()
     graph = random_topology(n, m, device="cpu", seed=3).to("cuda")
     weight, scales, scale, decoded = _packed(graph, fmt)
     layout = build_tiled_layout(graph.in_rowptr, graph.in_col, weight, neurons=n, ctas=ctas,
-                                smem_limit=smem, block_scales=scales, global_scale=scale)
+                                smem_limit=smem, block_scales=scales, global_scale=scale,
+                                chunk=chunk)
     model = bench_model(n)
     state = torch.rand(1, n, generator=torch.Generator().manual_seed(2)).cuda()
     dendrite = torch.rand(1, n, generator=torch.Generator().manual_seed(4)).cuda() - 0.5
@@ -284,3 +291,32 @@ def test_staged_update_equals_direct_update_bitwise(fmt, rows_per_cta):
         results.append(out)
     for got, want in zip(*results):
         assert torch.equal(got, want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["fp32", "fp16", "fp8", "nvfp4"])
+@pytest.mark.parametrize("n,m,smem", [(6000, 400000, 232448), (6000, 150000, 12000)])
+def test_chunk_widths_tick_bit_identically(fmt, n, m, smem):
+    """A lane sums its piece in CSR order whatever the chunk width, and splits
+    cut pieces at the same edges, so 4- and 8-slot layouts tick bit for bit
+    alike (20 ticks in one persistent launch)."""
+    ext = load_native_extension()
+    graph = random_topology(n, m, device="cpu", seed=12).to("cuda")
+    weight, scales, scale, _ = _packed(graph, fmt)
+    model = bench_model(n)
+    s0 = torch.rand(1, n, generator=torch.Generator().manual_seed(2)).cuda()
+    results = []
+    for chunk in (4, 8):
+        layout = build_tiled_layout(graph.in_rowptr, graph.in_col, weight, neurons=n, ctas=24,
+                                    smem_limit=smem, block_scales=scales, global_scale=scale,
+                                    chunk=chunk)
+        assert layout.chunk == chunk
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        out = [torch.empty_like(s0) for _ in range(3)]
+        ext.prepare_step_tiled(s0, torch.zeros_like(s0), torch.zeros_like(s0), model.parameters(),
+                               layout, None, 0.2, None, 0.1, out=out, status=status, ticks=20)()
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        results.append(out)
+    for a, b in zip(*results):
+        assert torch.equal(a, b)
