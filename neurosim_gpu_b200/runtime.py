@@ -568,9 +568,7 @@ class _RolloutPlan:
     def run(self, runtime: "NativeDendriticMatrixRuntime", drives, out, chunks):
         compute = torch.cuda.current_stream(self.device)
         upload, download = self.upload, self.download
-        for target, value in zip(self.running, (runtime.state, runtime.dendritic_state,
-                                                runtime.adaptation_state)):
-            target.copy_(value)
+        # The rings were last used by work on the compute stream.
         upload.wait_stream(compute)
         download.wait_stream(compute)
         lo = 0
@@ -581,6 +579,8 @@ class _RolloutPlan:
                     upload.wait_event(self.consumed[k])
                 self.drive_ring[k][:length].copy_(drives[lo:hi], non_blocking=True)
                 self.uploaded[k].record(upload)
+            if c == 0:  # the first upload is under way; now the state goes in
+                self._load_state(runtime)
             compute.wait_event(self.uploaded[k])
             if c >= 2:
                 compute.wait_event(self.saved[k])
@@ -595,6 +595,21 @@ class _RolloutPlan:
         compute.wait_stream(upload)
         block = self.block.clone()
         return tuple(block[i] for i in range(3))
+
+    def _load_state(self, runtime: "NativeDendriticMatrixRuntime") -> None:
+        """Copy the runtime's s, d, a into the running block: one copy when
+        they are the three rows of one block (what stream() and run() hand
+        out), else three."""
+        s, d, a = runtime.state, runtime.dendritic_state, runtime.adaptation_state
+        n = s.numel()
+        if (all(t.is_contiguous() and t.numel() == n for t in (s, d, a))
+                and d.data_ptr() == s.data_ptr() + 4 * n and a.data_ptr() == d.data_ptr() + 4 * n
+                and s.untyped_storage().data_ptr() == a.untyped_storage().data_ptr()):
+            self.block.copy_(s.as_strided(self.block.shape, self.block.stride(),
+                                          s.storage_offset()))
+            return
+        for target, value in zip(self.running, (s, d, a)):
+            target.copy_(value)
 
 
 class _TickGraph:
