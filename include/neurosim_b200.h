@@ -232,8 +232,8 @@ NSB_API int nsb_dendritic_event_noalloc(const nsb_tick* tick, float* current,
  *    task_rows[32q+i] hold o % 16, and scale_pairs[first scale pair + 32*b + i]
  *    holds the scales of CSR blocks o/16 + b (low byte) and o/16 + b + 1 (high
  *    byte); past the lane's last edge both are 0.
- *  - Pointer alignment (C = 4 / 8): tasks 16 B; col 8 / 16 B; weight 16 / 32 B
- *    (f32), 8 / 16 B (f16), 4 / 8 B (E4M3), 2 / 4 B (NVFP4).
+ *  - Pointer alignment: tasks 16 B; col 2C B; weight 4C B (f32), 2C B (f16),
+ *    C B (E4M3), C/2 B (NVFP4).
  *  - The kernels trust the layout's contents (offsets, lengths, rows): pass
  *    layouts made by the builder.  `ctas` must not exceed the SM count: the
  *    tick is a cooperative launch with one CTA per SM. */
@@ -241,7 +241,7 @@ typedef struct nsb_tiled_layout {
   int32_t ctas, blocks, block_cols, buffers, format;
   int32_t splits;              /* sub-task splits per block (row-sum planes per block) */
   int32_t split_chunks;        /* chunks of one sub-task                    */
-  int32_t chunk;               /* slots of one lane per chunk: 4 or 8 (C below) */
+  int32_t chunk;               /* slots of one lane per chunk: 4, 8, or 16 for E4M3 / NVFP4 (C below) */
   int64_t n_stages, n_tasks, n_slots, n_scale_pairs;
   int64_t rows;                /* destination rows                          */
   int64_t cols;                /* length of the gathered source vector      */

@@ -184,7 +184,9 @@ bool check_tiled(const nsb_tiled_layout* L) {
       L->block_cols > 65504 || (L->buffers != 1 && L->buffers != 2) || L->splits < 1 ||
       L->splits > 1023 || L->split_chunks < 1 || L->n_stages < 0 ||
       L->n_stages >= (int64_t{1} << 24) || L->n_tasks < 0 || L->n_slots < 0 ||
-      (L->chunk != 4 && L->chunk != 8) || L->n_slots % (32 * L->chunk) != 0 ||
+      (L->chunk != 4 && L->chunk != 8 && L->chunk != 16) ||
+      (L->chunk == 16 && L->format != NSB_WEIGHT_E4M3 && L->format != NSB_WEIGHT_NVFP4) ||
+      L->n_slots % (32 * L->chunk) != 0 ||
       L->n_slots >= (int64_t{1} << 31) || L->rows <= 0 ||
       L->rows >= (int64_t{1} << 28) - 1 || L->cols <= 0 ||
       static_cast<int64_t>(L->blocks) * L->block_cols < L->cols ||
@@ -194,10 +196,10 @@ bool check_tiled(const nsb_tiled_layout* L) {
       (L->n_tasks > 0 && (!L->tasks || !L->task_rows)) ||
       (L->n_slots > 0 && (!L->col || !L->weight)))
     return fail(NSB_ERR_ARGUMENT, "tiled layout arrays are required"), false;
-  static const uintptr_t weight_alignment[4] = {16, 8, 4, 2};  // at chunk 4; twice at 8
+  static const uintptr_t weight_alignment[4] = {16, 8, 4, 2};  // at chunk 4; x chunk / 4
   if (L->format < 0 || L->format > 3)
     return fail(NSB_ERR_ARGUMENT, "unknown CSR weight format"), false;
-  const uintptr_t wide = L->chunk == 8 ? 2 : 1;
+  const uintptr_t wide = static_cast<uintptr_t>(L->chunk / 4);
   if (!aligned(L->tasks, 16) || !aligned(L->col, 8 * wide) ||
       !aligned(L->weight, weight_alignment[L->format] * wide))
     return fail(NSB_ERR_ARGUMENT, "tiled layout arrays are misaligned"), false;

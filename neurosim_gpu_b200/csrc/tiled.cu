@@ -238,6 +238,18 @@ struct ChunkCols<8> {
   }
 };
 
+template <>
+struct ChunkCols<16> {
+  using Raw = Words8;
+  static __device__ __forceinline__ Raw load(const uint16_t* col, int64_t slot, uint64_t pol) {
+    return ld_stream_v8(col + slot, pol);
+  }
+  static __device__ __forceinline__ uint32_t at(const Raw& r, int e) {
+    const uint32_t word = r.v[e >> 1];
+    return (e & 1) ? word >> 16 : word & 0xFFFFu;
+  }
+};
+
 // Chunk readers, for K slots per lane (one lane's chunk): load(slot,
 // scale_entry) fetches the K weights; decode() turns them into K float32
 // weights, equal bit for bit to the reference quantizer's dequantized values
@@ -274,7 +286,8 @@ template <int K>
 struct ChunkF16 {
   static constexpr int kSlots = K;
   static constexpr bool kF32 = false;
-  using Raw = typename std::conditional<K == 4, uint2, uint4>::type;
+  using Raw = typename std::conditional<K == 4, uint2,
+                                       typename std::conditional<K == 8, uint4, Words8>::type>::type;
   const __half* w;
   __device__ __forceinline__ void prefetch(int first, int chunks, int, int) const {
     prefetch_l2(w + first, static_cast<uint32_t>(chunks) * 32u * K * 2u);
@@ -282,7 +295,8 @@ struct ChunkF16 {
   __device__ __forceinline__ void set_scale(float) {}
   __device__ __forceinline__ Raw load(int64_t slot, int64_t, uint64_t pol) const {
     if constexpr (K == 4) return ld_stream_v2(w + slot, pol);
-    else return ld_stream_v4(w + slot, pol);
+    else if constexpr (K == 8) return ld_stream_v4(w + slot, pol);
+    else return ld_stream_v8(w + slot, pol);
   }
   __device__ __forceinline__ void decode(const Raw& r, uint32_t, float (&v)[K]) const {
     const uint32_t* words = reinterpret_cast<const uint32_t*>(&r);
@@ -299,7 +313,8 @@ template <int K>
 struct ChunkE4M3 {
   static constexpr int kSlots = K;
   static constexpr bool kF32 = false;
-  using Raw = typename std::conditional<K == 4, uint32_t, uint2>::type;
+  using Raw = typename std::conditional<K == 4, uint32_t,
+                                       typename std::conditional<K == 8, uint2, uint4>::type>::type;
   const uint8_t* codes;
   float g;
   __device__ __forceinline__ void prefetch(int first, int chunks, int, int) const {
@@ -308,7 +323,8 @@ struct ChunkE4M3 {
   __device__ __forceinline__ void set_scale(float s) { g = s; }
   __device__ __forceinline__ Raw load(int64_t slot, int64_t, uint64_t pol) const {
     if constexpr (K == 4) return ld_stream_u32(codes + slot, pol);
-    else return ld_stream_v2(codes + slot, pol);
+    else if constexpr (K == 8) return ld_stream_v2(codes + slot, pol);
+    else return ld_stream_v4(codes + slot, pol);
   }
   __device__ __forceinline__ void decode(const Raw& r, uint32_t, float (&v)[K]) const {
     const uint32_t* words = reinterpret_cast<const uint32_t*>(&r);
@@ -328,8 +344,10 @@ template <int K>
 struct ChunkNVFP4 {
   static constexpr int kSlots = K;
   static constexpr bool kF32 = false;
-  // K = 4: four codes (low 16 bits) | scale pair << 16; K = 8: eight codes, scale pair.
-  using Raw = typename std::conditional<K == 4, uint32_t, uint2>::type;
+  // K = 4: four codes (low 16 bits) | scale pair << 16; K = 8: eight codes,
+  // scale pair; K = 16: sixteen codes (x, y), scale pair (z).
+  using Raw = typename std::conditional<K == 4, uint32_t,
+                                       typename std::conditional<K == 8, uint2, uint4>::type>::type;
   const uint8_t* codes;
   const uint16_t* pairs;
   float g;
@@ -345,8 +363,11 @@ struct ChunkNVFP4 {
   __device__ __forceinline__ Raw load(int64_t slot, int64_t entry, uint64_t pol) const {
     if constexpr (K == 4) {
       return ld_stream_u16(codes + (slot >> 1), pol) | (static_cast<uint32_t>(__ldg(pairs + entry)) << 16);
-    } else {
+    } else if constexpr (K == 8) {
       return make_uint2(ld_stream_u32(codes + (slot >> 1), pol), __ldg(pairs + entry));
+    } else {
+      const uint2 c = ld_stream_v2(codes + (slot >> 1), pol);
+      return make_uint4(c.x, c.y, __ldg(pairs + entry), 0u);
     }
   }
   __device__ __forceinline__ void decode(const Raw& r, uint32_t tag, float (&v)[K]) const {
@@ -355,10 +376,16 @@ struct ChunkNVFP4 {
     if constexpr (K == 4) {
       codes4[0] = r & 0xFFFFu;
       pair = r >> 16;
-    } else {
+    } else if constexpr (K == 8) {
       codes4[0] = r.x & 0xFFFFu;
       codes4[1] = r.x >> 16;
       pair = r.y;
+    } else {
+      codes4[0] = r.x & 0xFFFFu;
+      codes4[1] = r.x >> 16;
+      codes4[2] = r.y & 0xFFFFu;
+      codes4[3] = r.y >> 16;
+      pair = r.z;
     }
     const float2 scale = e4m3x2_to_float2(pair);
     const float f0 = __fmul_rn(scale.x, g), f1 = __fmul_rn(scale.y, g);
@@ -1114,6 +1141,18 @@ cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, cons
     if (staged && cap >= 64) L.stage_rows = static_cast<int32_t>(std::min<int64_t>(cap, 1 << 20));
   }
   const int ctas = layout.ctas;
+  if (layout.chunk == 16) {  // E4M3 / NVFP4 only (checked with the layout)
+    switch (layout.format) {
+      case NSB_WEIGHT_E4M3:
+        return launch_tiled_variant<ChunkE4M3<16>, 2>(
+            L, ChunkE4M3<16>{static_cast<const uint8_t*>(layout.weight), 0.0f}, t, x, out,
+            product, update, ticks, status, ctas, stream, px);
+      default:
+        return launch_tiled_variant<ChunkNVFP4<16>, 2>(
+            L, ChunkNVFP4<16>{static_cast<const uint8_t*>(layout.weight), layout.scale_pairs, 0.0f},
+            t, x, out, product, update, ticks, status, ctas, stream, px);
+    }
+  }
   return layout.chunk == 8
              ? launch_tiled_format<8, 2>(layout, L, t, x, update, ticks, out, product, status,
                                          ctas, stream, px, gate)

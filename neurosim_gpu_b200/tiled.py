@@ -69,6 +69,13 @@ WIDE_CHUNK = 8                # the wide width: one 16-byte column load per lane
 # 166k / 10M 18.2 -> 17.2, one rank of the 1.33M / 200M graph on 8 GPUs (6.5
 # edges per piece) 56.5 -> 53.4, that graph on one GPU 478 -> 451.
 WIDE_CHUNK_MIN_EDGES = 4
+# E4M3 / NVFP4 layouts whose pieces average at least this many edges use
+# 16-slot chunks (their weights are 1 / 0.5 bytes, so the extra padding costs
+# little; fp16 would spill registers at that width).  166k / 25M (50-edge
+# pieces): NVFP4 27.6 -> 26.0 us per tick, fp8 23.4 -> 23.3; 166k / 10M
+# (20-edge pieces, 30 % padding at 16 slots): 21.5 -> 21.7, 18.1 -> 18.8.
+WIDEST_CHUNK = 16
+WIDEST_CHUNK_MIN_EDGES = 32
 MAX_BLOCK_COLS = 65504        # 16-bit block-relative columns, block_cols = padding
 MAX_ROWS = (1 << 28) - 1      # 28-bit rows in task_rows; ROW_NONE marks a padding lane
 ROW_NONE = MAX_ROWS
@@ -263,8 +270,10 @@ def split_length(fmt: int, edges: int, rows: int, blocks: int, longest: int) -> 
     return split
 
 
-def chunk_width(edges: int, pieces: int) -> int:
+def chunk_width(edges: int, pieces: int, fmt: int = native.F32) -> int:
     """Slots per lane per chunk for a layout with ``pieces`` non-empty row pieces."""
+    if fmt in (native.E4M3, native.NVFP4) and edges >= WIDEST_CHUNK_MIN_EDGES * max(pieces, 1):
+        return WIDEST_CHUNK
     return WIDE_CHUNK if edges >= WIDE_CHUNK_MIN_EDGES * max(pieces, 1) else CHUNK
 
 
@@ -349,9 +358,10 @@ def build_tiled_layout(in_rowptr: torch.Tensor, in_col: torch.Tensor, weight: to
     group = stage_of.flatten()
     lengths = piece_len.flatten()
     order = torch.nonzero(lengths).flatten()
-    K = chunk if chunk is not None else chunk_width(m, order.numel())
-    if K not in (CHUNK, WIDE_CHUNK):
-        raise ValueError("chunk must be 4 or 8")
+    K = chunk if chunk is not None else chunk_width(m, order.numel(), fmt)
+    if K not in (CHUNK, WIDE_CHUNK, WIDEST_CHUNK) or (
+            K == WIDEST_CHUNK and fmt not in (native.E4M3, native.NVFP4)):
+        raise ValueError("chunk must be 4 or 8 (16 for E4M3 / NVFP4 weights)")
     K_SLOTS = LANES * K
     order = order[torch.sort(-((lengths[order] + K - 1) // K), stable=True).indices]
     order = order[torch.sort(group[order], stable=True).indices]

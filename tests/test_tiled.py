@@ -28,15 +28,18 @@ def _smem_bytes():
     return lambda cols, bufs: int(lib.nsb_tiled_smem_bytes(cols, bufs))
 
 
-@pytest.mark.parametrize("chunk", [None, 4, 8])
+@pytest.mark.parametrize("chunk", [None, 4, 8, 16])
 @pytest.mark.parametrize("fmt", ["fp32", "fp16", "fp8", "nvfp4"])
 @pytest.mark.parametrize("n,m,ctas,smem", [(97, 600, 4, 232448), (2000, 60000, 8, 8000),
                                            (5000, 100000, 16, 6000), (3001, 40001, 5, 232448),
                                            (5000, 100000, 2, 6000), (1, 0, 3, 232448),
                                            (300, 9000, 148, 232448), (2000, 200000, 8, 232448)])
 def test_layout_emulation_matches_oracle_cpu(fmt, n, m, ctas, smem, chunk):
-    """The layout builder alone, emulated on CPU (no GPU needed), at either
-    chunk width (None: the builder's choice from the mean piece length)."""
+    """The layout builder alone, emulated on CPU (no GPU needed), at each
+    chunk width (None: the builder's choice from the mean piece length; 16
+    slots only for the 1-byte and half-byte weight formats)."""
+    if chunk == 16 and fmt not in ("fp8", "nvfp4"):
+        pytest.skip("16-slot chunks are for E4M3 / NVFP4 weights")
     graph = random_topology(n, m, device="cpu", seed=3)
     weight, scales, scale, decoded = _packed(graph, fmt)
     layout = build_tiled_layout(graph.in_rowptr, graph.in_col, weight, neurons=n, ctas=ctas,
@@ -51,13 +54,15 @@ def test_layout_emulation_matches_oracle_cpu(fmt, n, m, ctas, smem, chunk):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("chunk", [4, 8])
+@pytest.mark.parametrize("chunk", [4, 8, 16])
 @pytest.mark.parametrize("fmt", ["fp32", "fp16", "fp8", "nvfp4"])
 @pytest.mark.parametrize("n,m,ctas,smem", [(97, 600, 4, 232448), (2000, 60000, 8, 8000),
                                            (5000, 100000, 16, 6000), (3001, 40001, 5, 232448),
                                            (20000, 400000, 148, 24000), (5000, 100000, 2, 6000),
                                            (2000, 200000, 8, 232448)])
 def test_tiled_tick_matches_oracle(fmt, n, m, ctas, smem, chunk):
+    if chunk == 16 and fmt not in ("fp8", "nvfp4"):
+        pytest.skip("16-slot chunks are for E4M3 / NVFP4 weights")
     ext = load_native_extension()
     graph = random_topology(n, m, device="cpu", seed=3).to("cuda")
     weight, scales, scale, decoded = _packed(graph, fmt)
@@ -306,7 +311,7 @@ def test_chunk_widths_tick_bit_identically(fmt, n, m, smem):
     model = bench_model(n)
     s0 = torch.rand(1, n, generator=torch.Generator().manual_seed(2)).cuda()
     results = []
-    for chunk in (4, 8):
+    for chunk in (4, 8, 16) if fmt in ("fp8", "nvfp4") else (4, 8):
         layout = build_tiled_layout(graph.in_rowptr, graph.in_col, weight, neurons=n, ctas=24,
                                     smem_limit=smem, block_scales=scales, global_scale=scale,
                                     chunk=chunk)
@@ -318,5 +323,6 @@ def test_chunk_widths_tick_bit_identically(fmt, n, m, smem):
         torch.cuda.synchronize()
         assert int(status.item()) == 0
         results.append(out)
-    for a, b in zip(*results):
-        assert torch.equal(a, b)
+    for other in results[1:]:
+        for a, b in zip(results[0], other):
+            assert torch.equal(a, b)
