@@ -328,7 +328,7 @@ def run_pels(args, workload: str) -> dict:
                                                  .manual_seed(0)) * 0.4 - 0.2).to(device))
     drive = [offset + 0.2 + 0.1 * math.sin(0.11 * t) for t in range(chunk)]
     runtime = NativeDendriticPELSRuntime(graph, model, torch.zeros(batch, neurons, device=device),
-                                         theta=PELS_THETA)
+                                         theta=PELS_THETA, propagation=args.propagation)
     steps = max(args.steps - args.steps % chunk, chunk)
     with torch.inference_mode():
         runtime.run(max(args.warmup, chunk), drive, dendritic_drive=0.1, graph_ticks=chunk)
@@ -558,7 +558,8 @@ def run_sharded_pels(args) -> dict:
                                                  .manual_seed(0)) * 0.4 - 0.2).to(device))
     drive = [offset + 0.2 + 0.1 * math.sin(0.11 * t) for t in range(chunk)]
     runtime = ShardedDendriticPELSRuntime(graph, model, torch.zeros(batch, neurons, device=device),
-                                          theta=PELS_THETA, exchange=args.exchange)
+                                          theta=PELS_THETA, exchange=args.exchange,
+                                          propagation=args.propagation)
     steps = max(args.steps - args.steps % chunk, chunk)
 
     def timed(fn) -> float:
@@ -612,14 +613,15 @@ def run_sharded_pels(args) -> dict:
                    "parallelism": f"row-sharded x{world}, " + (
                        "deltas exchanged by peer stores inside the advance kernel (NVLink)"
                        if runtime.exchange == "peer" else "NCCL all-gather of deltas"),
-                   "kernel_path": "pels-rows", "ticks_per_graph": chunk},
+                   "kernel_path": "pels-rows-" + runtime.propagation, "ticks_per_graph": chunk},
         "roofline": {"bound": "hbm", "achieved": None, "peak": hbm_peak()[0], "unit": "GB/s",
                      "frac": None, "traffic": None, "per_gpu": True,
-                     "kernel": "event_rows_kernel + event_scatter_rows_kernel"},
+                     "kernel": "event_rows_kernel + event_scatter_rows_kernel"
+                     + (" + tiled_tick_kernel (gated)" if runtime.propagation == "hybrid" else "")},
         "e2e": {"value": m * batch / (e2e_ms * 1e-3), "unit": "synapse-updates/s",
                 "h2d_bytes_per_step": 4 * batch * neurons,
                 "d2h_bytes_per_step": 4 * batch * neurons, "ms_per_step": e2e_ms},
-        "gpu_launches": 2 * steps * world,
+        "gpu_launches": (3 if runtime.propagation == "hybrid" else 2) * steps * world,
         "clocks": sampler.summary() if sampler else None,
     }
     runtime.release_graphs()
@@ -1037,6 +1039,9 @@ def main() -> None:
                         help="matrix tick path (auto: cluster for small graphs, tiled at B = 1)")
     parser.add_argument("--exchange", choices=("auto", "nccl", "peer"), default="auto",
                         help="row-sharded runs: soma / delta exchange (auto: peer stores)")
+    parser.add_argument("--propagation", choices=("auto", "event", "hybrid"), default="auto",
+                        help="PELS workloads: propagation of the emitted deltas (auto: the "
+                             "hybrid tick at B = 1 for graphs of >= 2^20 edges)")
     parser.add_argument("--profile", action="store_true",
                         help="eager launches only, for ncu captures (prints no bench line)")
     parser.add_argument("--profile-suite", action="store_true",

@@ -45,7 +45,7 @@ extern "C" {
 #define NSB_API
 #endif
 
-#define NSB_ABI_VERSION 13
+#define NSB_ABI_VERSION 14
 
 enum nsb_status {
   NSB_OK = 0,
@@ -474,6 +474,41 @@ NSB_API int nsb_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows,
                                    const float* delta, const nsb_scatter_rows* csr,
                                    float* current, const nsb_delta_exchange* exchange,
                                    void* workspace, int* status, void* stream);
+
+/* Hybrid row-sharded PELS tick (B = 1, peer exchange; no counterpart in the
+ * reference): the row-sharded tick above with the propagation of the emitted
+ * deltas chosen on the device from the tick's activity over ALL ranks, as
+ * nsb_dendritic_event_hybrid does on one GPU.  Three calls per tick, on one
+ * stream, with the same row-event workspace:
+ * 1. nsb_dendritic_event_rows_gated: nsb_dendritic_event_rows with an
+ *    exchange, which also sums `out_degree[r]` (the whole graph's out-degree
+ *    of the rank's row r) over the rows that emit and adds the rank's sum into
+ *    every rank's count of this tick (words 2 + parity of each rank's counter
+ *    array: the arrival counter is word 0 of a zero-filled array of at least 4
+ *    u64) before it signals its arrival.
+ * 2. nsb_event_scatter_rows_gated: after its wait, the scatter returns at once
+ *    when the ranks' emitting sources have >= gate_edges (>= 1) out-edges;
+ *    else it scatters as nsb_event_scatter_rows does.  It leaves the count and
+ *    the address of the tick's gathered delta buffer in the workspace.
+ * 3. nsb_tiled_propagate_rows_gated: below the gate it returns at once; at or
+ *    above it, current[rows] += W[rows, :] @ delta by the tiled kernel
+ *    (`layout`: the float32 tiled layout of the rank's rows x all N columns,
+ *    with its workspace; no atomics).
+ * All three are always enqueued, so a tick can be captured into a CUDA graph.
+ * Every rank must use the same gate_edges. */
+NSB_API int nsb_dendritic_event_rows_gated(const nsb_tick* tick, const nsb_event_rows* ev,
+                                           const nsb_delta_exchange* exchange,
+                                           const int32_t* out_degree, const nsb_tick_out* out,
+                                           const nsb_out* out_emitted, void* workspace,
+                                           void* stream);
+NSB_API int nsb_event_scatter_rows_gated(int64_t neurons, int64_t rows,
+                                         const nsb_scatter_rows* csr, float* current,
+                                         const nsb_delta_exchange* exchange, uint64_t gate_edges,
+                                         void* workspace, int* status, void* stream);
+NSB_API int nsb_tiled_propagate_rows_gated(const nsb_tiled_layout* layout, void* tiled_workspace,
+                                           size_t tiled_workspace_bytes, float* current,
+                                           uint64_t gate_edges, void* workspace, int* status,
+                                           void* stream);
 
 /* Weight encoder (replaces encode_sparse_weights, src/neurosim_gpu/precision.py:76-90,
  * for weights in device memory; bit-exact to it).  `format` is NSB_WEIGHT_E4M3

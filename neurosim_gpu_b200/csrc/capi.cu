@@ -665,9 +665,11 @@ bool check_rows_workspace(void* workspace) {
 }
 }  // namespace
 
-int nsb_dendritic_event_rows(const nsb_tick* tick, const nsb_event_rows* ev, float* delta,
-                             const nsb_delta_exchange* exchange, const nsb_tick_out* out,
-                             const nsb_out* out_emitted, void* workspace, void* stream) {
+namespace {
+int event_rows(const nsb_tick* tick, const nsb_event_rows* ev, float* delta,
+               const nsb_delta_exchange* exchange, const int32_t* out_degree,
+               const nsb_tick_out* out, const nsb_out* out_emitted, void* workspace,
+               void* stream, const char* name) {
   nsb::TickArgs t;
   if (!check_tick(tick, &t)) return NSB_ERR_ARGUMENT;
   if (!ev) return fail(NSB_ERR_ARGUMENT, "row-event arguments are required");
@@ -695,12 +697,32 @@ int nsb_dendritic_event_rows(const nsb_tick* tick, const nsb_event_rows* ev, flo
   e.theta = ev->theta;
   e.theta_stride = ev->theta_stride;
   e.delta = delta;
+  e.out_degree = out_degree;
   const nsb::TickOut o{to_out(out->state), to_out(out->dendrite), to_out(out->adaptation)};
   const cudaError_t err = nsb::launch_event_rows(
       t, e, o, to_out(*out_emitted), exchange ? &px : nullptr,
       static_cast<nsb::EventRowsState*>(workspace), static_cast<cudaStream_t>(stream));
-  if (err != cudaSuccess) return cuda_fail(err, "nsb_dendritic_event_rows launch");
+  if (err != cudaSuccess) return cuda_fail(err, name);
   return NSB_OK;
+}
+}  // namespace
+
+int nsb_dendritic_event_rows(const nsb_tick* tick, const nsb_event_rows* ev, float* delta,
+                             const nsb_delta_exchange* exchange, const nsb_tick_out* out,
+                             const nsb_out* out_emitted, void* workspace, void* stream) {
+  return event_rows(tick, ev, delta, exchange, nullptr, out, out_emitted, workspace, stream,
+                    "nsb_dendritic_event_rows launch");
+}
+
+int nsb_dendritic_event_rows_gated(const nsb_tick* tick, const nsb_event_rows* ev,
+                                   const nsb_delta_exchange* exchange, const int32_t* out_degree,
+                                   const nsb_tick_out* out, const nsb_out* out_emitted,
+                                   void* workspace, void* stream) {
+  if (!tick || tick->batch != 1) return fail(NSB_ERR_ARGUMENT, "the gated row tick takes B = 1");
+  if (!exchange) return fail(NSB_ERR_ARGUMENT, "the gated row tick needs a peer exchange");
+  if (!out_degree) return fail(NSB_ERR_ARGUMENT, "the gated row tick needs the rows' out-degrees");
+  return event_rows(tick, ev, nullptr, exchange, out_degree, out, out_emitted, workspace, stream,
+                    "nsb_dendritic_event_rows_gated launch");
 }
 
 int nsb_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows, const float* delta,
@@ -722,9 +744,61 @@ int nsb_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows, const f
   const nsb::ScatterRowsArgs c{csr->rowptr, csr->dst, csr->weight, csr->n_edges};
   const cudaError_t err = nsb::launch_event_scatter_rows(
       batch, neurons, rows, delta, c, current, exchange ? &px : nullptr,
-      static_cast<const nsb::EventRowsState*>(workspace), status,
+      static_cast<nsb::EventRowsState*>(workspace), status,
       static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "nsb_event_scatter_rows launch");
+  return NSB_OK;
+}
+
+int nsb_event_scatter_rows_gated(int64_t neurons, int64_t rows, const nsb_scatter_rows* csr,
+                                 float* current, const nsb_delta_exchange* exchange,
+                                 uint64_t gate_edges, void* workspace, int* status, void* stream) {
+  if (neurons <= 0 || rows < 0 || rows > neurons || neurons >= (int64_t(1) << 40))
+    return fail(NSB_ERR_ARGUMENT, "scatter geometry: N > 0, 0 <= rows <= N");
+  if (!csr || !csr->rowptr || csr->n_edges < 0 || csr->n_edges >= (int64_t(1) << 31) ||
+      (csr->n_edges > 0 && (!csr->dst || !csr->weight)))
+    return fail(NSB_ERR_ARGUMENT, "invalid row-scatter topology geometry");
+  if (rows > 0 && !current) return fail(NSB_ERR_ARGUMENT, "current is required");
+  if (!exchange) return fail(NSB_ERR_ARGUMENT, "the gated scatter needs a peer exchange");
+  if (gate_edges < 1) return fail(NSB_ERR_ARGUMENT, "gate_edges must be at least 1");
+  nsb::DeltaPeers px{};
+  if (!check_delta_exchange(exchange, &px)) return NSB_ERR_ARGUMENT;
+  if (!check_rows_workspace(workspace)) return NSB_ERR_WORKSPACE;
+  g_error.clear();
+  const nsb::ScatterRowsArgs c{csr->rowptr, csr->dst, csr->weight, csr->n_edges};
+  const cudaError_t err = nsb::launch_event_scatter_rows(
+      1, neurons, rows, nullptr, c, current, &px, static_cast<nsb::EventRowsState*>(workspace),
+      status, static_cast<cudaStream_t>(stream), gate_edges);
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_event_scatter_rows_gated launch");
+  return NSB_OK;
+}
+
+int nsb_tiled_propagate_rows_gated(const nsb_tiled_layout* layout, void* tiled_workspace,
+                                   size_t tiled_workspace_bytes, float* current,
+                                   uint64_t gate_edges, void* workspace, int* status,
+                                   void* stream) {
+  if (!check_tiled(layout)) return tiled_status(NSB_ERR_ARGUMENT);
+  if (layout->format != NSB_WEIGHT_F32)
+    return fail(NSB_ERR_ARGUMENT, "the gated propagate takes a float32 layout");
+  if (!check_workspace(layout, tiled_workspace, tiled_workspace_bytes))
+    return tiled_status(NSB_ERR_WORKSPACE);
+  if (!current) return fail(NSB_ERR_ARGUMENT, "current is required");
+  if (gate_edges < 1) return fail(NSB_ERR_ARGUMENT, "gate_edges must be at least 1");
+  if (!check_rows_workspace(workspace)) return NSB_ERR_WORKSPACE;
+  g_error.clear();
+  const auto* state = static_cast<const nsb::EventRowsState*>(workspace);
+  nsb::TiledGate gate;
+  gate.count = &state->gate_count;
+  gate.min = gate_edges;
+  gate.accumulate = true;
+  gate.source = &state->gate_source;
+  nsb::TickArgs none{};
+  none.batch = 1;
+  none.neurons = layout->rows;
+  const cudaError_t err = nsb::launch_tiled(*layout, none, current, false, 1, nsb::TickOut{},
+                                            nsb::Out{current, 0, 1}, tiled_workspace, status,
+                                            static_cast<cudaStream_t>(stream), nullptr, gate);
+  if (err != cudaSuccess) return cuda_fail(err, "nsb_tiled_propagate_rows_gated launch");
   return NSB_OK;
 }
 

@@ -56,10 +56,13 @@ size_t tiled_smem_bytes(int block_cols, int buffers);
 size_t tiled_workspace_bytes(const nsb_tiled_layout& layout);
 // Gate of a propagate-only launch (the hybrid PELS tick): the kernel returns at
 // once unless *count >= min, and with `accumulate` adds W @ x into `product`.
+// With `source`, the launch reads its x pointer from device memory at *source
+// (written by an earlier launch on the stream) instead of the argument.
 struct TiledGate {
   const unsigned long long* count = nullptr;
   unsigned long long min = 0;
   bool accumulate = false;
+  const unsigned long long* source = nullptr;
 };
 
 cudaError_t launch_tiled(const nsb_tiled_layout& layout, const TickArgs& t, const float* x,
@@ -86,6 +89,7 @@ struct EventRowsArgs {
   const float* theta;    // the rank's rows
   int64_t theta_stride;
   float* delta;          // local mode: the gathered delta buffer [cols, B]
+  const int32_t* out_degree = nullptr;  // peer mode: the rows' out-degrees (gated ticks), or null
 };
 
 // Every rank's two gathered delta buffers and arrival counters (peer mode).
@@ -100,6 +104,9 @@ struct EventRowsState {
   unsigned long long ticks;  // peer-mode ticks this rank has signalled
   unsigned int done;         // CTAs of the current advance launch that finished
   unsigned int reserved;
+  unsigned long long count;         // gated ticks: this launch's emitting out-edges so far
+  unsigned long long gate_count;    // gated ticks: all ranks' emitting out-edges of the tick
+  unsigned long long gate_source;   // gated ticks: address of the tick's gathered deltas
 };
 
 // The source-major out-CSR restricted to the rank's destination rows.
@@ -113,11 +120,14 @@ struct ScatterRowsArgs {
 cudaError_t launch_event_rows(const TickArgs& t, const EventRowsArgs& e, const TickOut& out,
                               const Out& out_emitted, const DeltaPeers* px,
                               EventRowsState* state, cudaStream_t stream);
+// With gate_edges > 0 (peer mode), the scatter returns after its wait when all
+// ranks' emitting sources have >= gate_edges out-edges, and CTA 0 leaves that
+// count and the tick's delta buffer in `state` for a gated tiled propagate.
 cudaError_t launch_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows,
                                       const float* delta, const ScatterRowsArgs& c,
                                       float* current, const DeltaPeers* px,
-                                      const EventRowsState* state, int* status,
-                                      cudaStream_t stream);
+                                      EventRowsState* state, int* status,
+                                      cudaStream_t stream, unsigned long long gate_edges = 0);
 
 // fp8 / NVFP4 weight encoders (encode.cu); workspace: 4 bytes (the amax word).
 cudaError_t launch_encode(int format, const float* weight, int64_t n, uint8_t* codes,

@@ -55,6 +55,7 @@ event_rows_kernel(TickArgs t, EventRowsArgs e, TickOut out, Out out_emitted, Del
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   int parity = 0;
   if (X) parity = static_cast<int>(*reinterpret_cast<volatile unsigned long long*>(&state->ticks) & 1);
+  unsigned long long emitting = 0;  // gated ticks: out-edges of this thread's emitting rows
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
        i += stride) {
     const int64_t b = i / rows;
@@ -68,6 +69,7 @@ event_rows_kernel(TickArgs t, EventRowsArgs e, TickOut out, Out out_emitted, Del
     const bool active = fabsf(residual) >= __ldg(e.theta + r * e.theta_stride);
     out_emitted.put(b, r, active ? q.s : previous);
     const float delta = active ? residual : 0.0f;
+    if (X && e.out_degree && active) emitting += static_cast<unsigned long long>(__ldg(e.out_degree + r));
     const int64_t at = (e.row_offset + r) * batch + b;
     if (X) {
       for (int p = 0; p < px.world; ++p) px.delta[p][parity][at] = delta;
@@ -80,12 +82,26 @@ event_rows_kernel(TickArgs t, EventRowsArgs e, TickOut out, Out out_emitted, Del
     // fence after it (cumulative over the barrier) orders them all before the
     // CTA counts itself done.  A fence per thread costs ~ one NVLink round trip
     // each and stalls behind copies in flight.
+    if (e.out_degree) {  // one atomic per warp into the launch's count
+      for (int o = 16; o > 0; o >>= 1) emitting += __shfl_down_sync(0xffffffffu, emitting, o);
+      if ((threadIdx.x & 31) == 0 && emitting) atomicAdd(&state->count, emitting);
+    }
     __syncthreads();
     if (threadIdx.x == 0) __threadfence_system();
     if (threadIdx.x == 0 && atomicAdd(&state->done, 1u) == gridDim.x - 1) {
       // The last CTA of this tick: every CTA has counted itself, so the count
       // can start over for the next tick.
       state->done = 0;
+      if (e.out_degree) {
+        // Every CTA's count preceded its arrival above.  This rank's slot of
+        // the next tick's parity starts over (no rank adds to it before this
+        // rank's arrival below), and every rank's slot of this tick's parity
+        // (words 2 and 3 after its arrival counter) gets this rank's total.
+        __threadfence();
+        const unsigned long long total = atomicExch(&state->count, 0ull);
+        *reinterpret_cast<volatile unsigned long long*>(px.counters[px.rank] + 2 + (parity ^ 1)) = 0ull;
+        for (int p = 0; p < px.world; ++p) atomicAdd_system(px.counters[p] + 2 + parity, total);
+      }
       __threadfence_system();
       for (int p = 0; p < px.world; ++p) atomicAdd_system(px.counters[p], 1ull);
       atomicAdd(&state->ticks, 1ull);
@@ -97,7 +113,7 @@ template <bool X, int G>
 __global__ void __launch_bounds__(kRowThreads)
 event_scatter_rows_kernel(int64_t batch, int64_t neurons, int64_t rows, const float* delta,
                           ScatterRowsArgs c, float* current, DeltaPeers px,
-                          const EventRowsState* state, int* status) {
+                          EventRowsState* state, int* status, unsigned long long gate_edges) {
   if (X) {
     // Tick k was counted by the advance launch just before this one, so this
     // rank's tick count is k + 1: wait for world * (k + 1) arrivals.
@@ -117,6 +133,16 @@ event_scatter_rows_kernel(int64_t batch, int64_t neurons, int64_t rows, const fl
       }
     }
     __syncthreads();
+    if (gate_edges) {
+      // All ranks counted this tick's emitting out-edges before they arrived.
+      const unsigned long long active = *reinterpret_cast<const volatile unsigned long long*>(
+          px.counters[px.rank] + 2 + ((ticks - 1) & 1));
+      if (blockIdx.x == 0 && threadIdx.x == 0) {
+        state->gate_count = active;
+        state->gate_source = reinterpret_cast<unsigned long long>(delta);
+      }
+      if (active >= gate_edges) return;  // the gated tiled propagate takes this tick
+    }
   }
   constexpr int kGroups = 32 / G;  // active sources a warp scatters at once
   const int lane = threadIdx.x & 31;
@@ -188,49 +214,49 @@ namespace {
 template <bool X, int G>
 cudaError_t scatter_rows_variant(int sm_count, int64_t batch, int64_t neurons, int64_t rows,
                                  const float* delta, const ScatterRowsArgs& c, float* current,
-                                 const DeltaPeers& px, const EventRowsState* state, int* status,
-                                 cudaStream_t stream) {
+                                 const DeltaPeers& px, EventRowsState* state, int* status,
+                                 cudaStream_t stream, unsigned long long gate_edges) {
   static int occupancy = 0;
   if (occupancy == 0) occupancy = resident(event_scatter_rows_kernel<X, G>);
   const int64_t warps = (batch * neurons + 31) / 32;
   const int64_t needed = std::max<int64_t>(1, (warps * 32 + kRowThreads - 1) / kRowThreads);
   const int64_t blocks = std::min<int64_t>(needed, int64_t{sm_count} * occupancy);
   event_scatter_rows_kernel<X, G><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(
-      batch, neurons, rows, delta, c, current, px, state, status);
+      batch, neurons, rows, delta, c, current, px, state, status, gate_edges);
   return cudaGetLastError();
 }
 
 template <bool X>
 cudaError_t scatter_rows_width(int sm_count, int64_t n_edges, int64_t batch, int64_t neurons,
                                int64_t rows, const float* delta, const ScatterRowsArgs& c,
-                               float* current, const DeltaPeers& px,
-                               const EventRowsState* state, int* status, cudaStream_t stream) {
+                               float* current, const DeltaPeers& px, EventRowsState* state,
+                               int* status, cudaStream_t stream, unsigned long long gate_edges) {
   // Lanes per emitting source from the mean out-degree into this rank's rows.
   const double degree = static_cast<double>(n_edges) / static_cast<double>(std::max<int64_t>(neurons, 1));
   if (degree <= 12)
     return scatter_rows_variant<X, 8>(sm_count, batch, neurons, rows, delta, c, current, px, state,
-                                      status, stream);
+                                      status, stream, gate_edges);
   if (degree <= 24)
     return scatter_rows_variant<X, 16>(sm_count, batch, neurons, rows, delta, c, current, px,
-                                       state, status, stream);
+                                       state, status, stream, gate_edges);
   return scatter_rows_variant<X, 32>(sm_count, batch, neurons, rows, delta, c, current, px, state,
-                                     status, stream);
+                                     status, stream, gate_edges);
 }
 }  // namespace
 
 cudaError_t launch_event_scatter_rows(int64_t batch, int64_t neurons, int64_t rows,
                                       const float* delta, const ScatterRowsArgs& c,
                                       float* current, const DeltaPeers* px,
-                                      const EventRowsState* state, int* status,
-                                      cudaStream_t stream) {
+                                      EventRowsState* state, int* status,
+                                      cudaStream_t stream, unsigned long long gate_edges) {
   DeviceInfo info;
   cudaError_t err = device_info(&info);
   if (err != cudaSuccess) return err;
   if (px)
     return scatter_rows_width<true>(info.sm_count, c.n_edges, batch, neurons, rows, delta, c,
-                                    current, *px, state, status, stream);
+                                    current, *px, state, status, stream, gate_edges);
   return scatter_rows_width<false>(info.sm_count, c.n_edges, batch, neurons, rows, delta, c,
-                                   current, DeltaPeers{}, state, status, stream);
+                                   current, DeltaPeers{}, state, status, stream, 0);
 }
 
 }  // namespace nsb

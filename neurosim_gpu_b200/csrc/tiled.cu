@@ -515,7 +515,8 @@ template <typename W, int D, bool X, bool G>
 __global__ void __launch_bounds__(kTiledThreads, 1)
 tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ x0, TickOut out,
                   Out product, bool update, int ticks, int* status, Peers px,
-                  const unsigned long long* gate_count, unsigned long long gate_min) {
+                  const unsigned long long* gate_count, unsigned long long gate_min,
+                  const unsigned long long* gate_source) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   constexpr int kK = W::kSlots;              // slots of one lane per chunk
   constexpr int kChunkSlots = 32 * kK;       // slots of one warp-wide chunk
@@ -533,6 +534,11 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
   // before any barrier.
   if (G && *reinterpret_cast<const volatile unsigned long long*>(gate_count) < gate_min)
     return;
+  // A gated launch may take its source vector from a pointer an earlier launch left.
+  const float* const xin =
+      G && gate_source
+          ? reinterpret_cast<const float*>(*reinterpret_cast<const volatile unsigned long long*>(gate_source))
+          : x0;
 
   const int c = blockIdx.x;
   const int warp = threadIdx.x >> 5;
@@ -602,7 +608,7 @@ tiled_tick_kernel(TiledArgs L, W weights, TickArgs t, const float* __restrict__ 
 
   for (int tick = 0; tick < ticks; ++tick) {
     const bool exchange = X && px.world > 0;
-    const float* x = exchange ? px.gathered[px.rank][tick & 1] : tick == 0 ? x0 : out.s.data;
+    const float* x = exchange ? px.gathered[px.rank][tick & 1] : tick == 0 ? xin : out.s.data;
     const int use0 = tick * stages;
     if (warp == kProducerWarp) {
       // All 32 lanes prefetch tasks (each lane one task's metadata load and
@@ -1016,7 +1022,7 @@ cudaError_t launch_tiled_kernel(const TiledArgs& L, const W& w, const TickArgs& 
   config.attrs = attribute;
   config.numAttrs = 1;
   return cudaLaunchKernelEx(&config, kernel, L, w, t, x, out, product, update, ticks, status, px,
-                            gate.count, gate.min);
+                            gate.count, gate.min, gate.source);
 }
 
 template <typename W, int D>

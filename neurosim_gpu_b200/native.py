@@ -137,7 +137,8 @@ EXPORTED_SYMBOLS = ("nsb_dendritic_step", "nsb_csr_propagate",
                     "nsb_dendritic_event_rows", "nsb_event_scatter_rows", "nsb_encode_weights",
                     "nsb_dendritic_event_hybrid", "nsb_dendritic_rollout_tiled",
                     "nsb_dendritic_rollout_tiled_peers", "nsb_dendritic_rollout_cluster",
-                    "nsb_last_error", "nsb_abi_version")
+                    "nsb_dendritic_event_rows_gated", "nsb_event_scatter_rows_gated",
+                    "nsb_tiled_propagate_rows_gated", "nsb_last_error", "nsb_abi_version")
 
 
 @functools.lru_cache(maxsize=1)
@@ -206,6 +207,17 @@ def load_library() -> ctypes.CDLL:
                                            ctypes.c_void_p, p(_ScatterRows), ctypes.c_void_p,
                                            p(_DeltaExchange), ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_void_p]
+    lib.nsb_dendritic_event_rows_gated.argtypes = [p(_Tick), p(_EventRows), p(_DeltaExchange),
+                                                   ctypes.c_void_p, p(_TickOut), p(_Out),
+                                                   ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_event_scatter_rows_gated.argtypes = [ctypes.c_int64, ctypes.c_int64, p(_ScatterRows),
+                                                 ctypes.c_void_p, p(_DeltaExchange),
+                                                 ctypes.c_uint64, ctypes.c_void_p,
+                                                 ctypes.c_void_p, ctypes.c_void_p]
+    lib.nsb_tiled_propagate_rows_gated.argtypes = [p(_TiledLayout), ctypes.c_void_p,
+                                                   ctypes.c_size_t, ctypes.c_void_p,
+                                                   ctypes.c_uint64, ctypes.c_void_p,
+                                                   ctypes.c_void_p, ctypes.c_void_p]
     lib.nsb_encode_weights.argtypes = [ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_void_p, ctypes.c_void_p]
@@ -217,7 +229,7 @@ def load_library() -> ctypes.CDLL:
     lib.nsb_abi_version.restype = ctypes.c_int
     for name in EXPORTED_SYMBOLS:
         getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
-    if lib.nsb_abi_version() != 13:
+    if lib.nsb_abi_version() != 14:
         raise RuntimeError("libneurosim_b200.so ABI version mismatch")
     return lib
 
@@ -566,12 +578,15 @@ class DendriticExtension:
     # -- row-sharded PELS --------------------------------------------------------
     def prepare_event_rows(self, state, dendrite, adaptation, params, current, emitted, theta,
                            input, input_scalar, dendritic_input, dendritic_scalar, *,
-                           row_offset, cols, delta, exchange, out, workspace):
+                           row_offset, cols, delta, exchange, out, workspace, out_degree=None):
         """A launch callable for the advance + emit half of a row-sharded PELS tick.
 
         ``state`` ... ``theta`` are this rank's rows ([B, rows] / [rows]);
         ``delta`` is the gathered [cols, B] delta buffer (None with an
         ``exchange``, a :class:`_DeltaExchange`); ``out`` is (s, d, a, emitted).
+        ``out_degree`` (int32 [rows], with an exchange, B = 1): also count the
+        emitting rows' out-edges for a gated tick
+        (``nsb_dendritic_event_rows_gated``).
         """
         _check_state(state)
         tick = _tick(state, dendrite, adaptation, params, input, input_scalar,
@@ -600,22 +615,39 @@ class DendriticExtension:
         x = ctypes.byref(exchange) if exchange is not None else None
         lib, device = self.lib, state.device
         keep = (state, dendrite, adaptation, params, current, emitted, theta, input,
-                dendritic_input, delta, exchange, out, workspace)
+                dendritic_input, delta, exchange, out, workspace, out_degree)
+        if out_degree is not None:
+            _check(exchange is not None and state.size(0) == 1,
+                   "a gated row tick needs B = 1 and an exchange")
+            _check(out_degree.device == state.device and out_degree.dtype == torch.int32
+                   and out_degree.is_contiguous() and out_degree.numel() == state.size(1),
+                   "out_degree must be a contiguous int32 [rows]")
 
         def launch() -> None:
             assert keep is not None
             with torch.cuda.device(device):
-                code = lib.nsb_dendritic_event_rows(ctypes.byref(tick), ctypes.byref(ev),
-                                                    delta_ptr, x, ctypes.byref(result),
-                                                    ctypes.byref(out_emitted),
-                                                    workspace.data_ptr(), _stream(device))
+                if out_degree is not None:
+                    code = lib.nsb_dendritic_event_rows_gated(
+                        ctypes.byref(tick), ctypes.byref(ev), x, out_degree.data_ptr(),
+                        ctypes.byref(result), ctypes.byref(out_emitted), workspace.data_ptr(),
+                        _stream(device))
+                else:
+                    code = lib.nsb_dendritic_event_rows(ctypes.byref(tick), ctypes.byref(ev),
+                                                        delta_ptr, x, ctypes.byref(result),
+                                                        ctypes.byref(out_emitted),
+                                                        workspace.data_ptr(), _stream(device))
             _raise_on_status(lib, code)
 
         return launch
 
     def prepare_scatter_rows(self, batch, neurons, rows, delta, rowptr, dst, weight, current, *,
-                             exchange, workspace, status=None):
-        """A launch callable for the scatter half of a row-sharded PELS tick."""
+                             exchange, workspace, status=None, gate_edges=0):
+        """A launch callable for the scatter half of a row-sharded PELS tick.
+
+        ``gate_edges`` > 0 (B = 1, with an exchange): the gated scatter of a
+        hybrid tick (``nsb_event_scatter_rows_gated``), which returns after its
+        wait when the ranks' emitting sources have >= gate_edges out-edges.
+        """
         _check(current.is_cuda and current.dtype == torch.float32 and current.is_contiguous()
                and tuple(current.shape) == (batch, rows), "current must be a contiguous [B, rows]")
         for array in (rowptr, dst):
@@ -637,10 +669,42 @@ class DendriticExtension:
         def launch() -> None:
             assert keep is not None
             with torch.cuda.device(device):
-                code = lib.nsb_event_scatter_rows(int(batch), int(neurons), int(rows), delta_ptr,
-                                                  ctypes.byref(csr), current.data_ptr(), x,
-                                                  workspace.data_ptr(), status_ptr,
-                                                  _stream(device))
+                if gate_edges:
+                    code = lib.nsb_event_scatter_rows_gated(
+                        int(neurons), int(rows), ctypes.byref(csr), current.data_ptr(), x,
+                        int(gate_edges), workspace.data_ptr(), status_ptr, _stream(device))
+                else:
+                    code = lib.nsb_event_scatter_rows(int(batch), int(neurons), int(rows),
+                                                      delta_ptr, ctypes.byref(csr),
+                                                      current.data_ptr(), x,
+                                                      workspace.data_ptr(), status_ptr,
+                                                      _stream(device))
+            _raise_on_status(lib, code)
+
+        return launch
+
+    def prepare_propagate_rows_gated(self, layout, current, gate_edges, *, workspace,
+                                     status=None):
+        """A launch callable for the gated tiled propagate of a hybrid row-sharded
+        tick (``nsb_tiled_propagate_rows_gated``): at or above the gate,
+        ``current`` ([1, rows]) += W[rows, :] @ the tick's gathered deltas."""
+        _check(current.is_cuda and current.dtype == torch.float32 and current.is_contiguous()
+               and current.numel() == layout.neurons, "current must be a contiguous [1, rows]")
+        _check(layout.format == F32, "the gated propagate takes a float32 layout")
+        _check(int(gate_edges) >= 1, "gate_edges must be at least 1")
+        c_layout = layout.c_struct()
+        tiled_workspace = layout.workspace()
+        status_ptr = status.data_ptr() if status is not None else None
+        lib, device = self.lib, current.device
+        keep = (layout, current, workspace, status, tiled_workspace)
+
+        def launch() -> None:
+            assert keep is not None
+            with torch.cuda.device(device):
+                code = lib.nsb_tiled_propagate_rows_gated(
+                    ctypes.byref(c_layout), tiled_workspace.data_ptr(), tiled_workspace.numel(),
+                    current.data_ptr(), int(gate_edges), workspace.data_ptr(), status_ptr,
+                    _stream(device))
             _raise_on_status(lib, code)
 
         return launch

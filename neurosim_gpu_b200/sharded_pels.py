@@ -67,12 +67,21 @@ class ShardedDendriticPELSRuntime:
     ``emitted_state`` and ``persistent_current`` are this rank's rows
     ([B, rows]).  ``rank`` / ``world`` may be given to build one rank's share
     without a process group (the caller then moves the deltas).
+
+    ``propagation``: ``'event'`` scatters every tick's emitted deltas;
+    ``'hybrid'`` (B = 1, peer exchange) propagates a tick whose emitting
+    sources have at least ``hybrid_gate`` x M out-edges over ALL ranks with the
+    tiled kernel over the rank's rows (W[rows, :] @ deltas, no atomics) and
+    scatters the others, chosen on the device every tick as the single-GPU
+    hybrid tick does; ``'auto'`` is the hybrid at B = 1 with the peer exchange
+    for graphs of at least 2^20 edges, else the event tick.
     """
 
     def __init__(self, graph, dynamics: DendriticDynamics, initial_state: torch.Tensor, *,
                  theta, group=None, extension=None, rank: int | None = None,
                  world: int | None = None, exchange: str = "auto",
-                 partition: str = "edges") -> None:
+                 partition: str = "edges", propagation: str = "auto",
+                 hybrid_gate: float = 0.15) -> None:
         if isinstance(graph, tuple):
             in_rowptr, in_col, in_weight = graph
         else:
@@ -83,6 +92,10 @@ class ShardedDendriticPELSRuntime:
             raise ValueError("exchange must be 'auto', 'nccl' or 'peer'")
         if partition not in ("edges", "rows"):
             raise ValueError("partition must be 'edges' or 'rows'")
+        if propagation not in ("auto", "event", "hybrid"):
+            raise ValueError("propagation must be 'auto', 'event' or 'hybrid'")
+        if not 0.0 < hybrid_gate <= 1.0:
+            raise ValueError("hybrid_gate must be in (0, 1]")
         self.group = group
         self.rank = dist.get_rank(group) if rank is None else rank
         self.world = dist.get_world_size(group) if world is None else world
@@ -116,10 +129,29 @@ class ShardedDendriticPELSRuntime:
         self._peer = None
         self._peer_bases: list[int] = []
         wants_peer = exchange == "peer" or (exchange == "auto" and rank is None)
-        if wants_peer and 1 < self.world <= _native.MAX_PEERS and dist.is_initialized():
+        # exchange="peer" also runs on a process group of one rank (the fused
+        # kernels with the rank's own buffers: tests of the peer path on one GPU).
+        if (wants_peer and dist.is_initialized() and self.world <= _native.MAX_PEERS
+                and (self.world > 1 or exchange == "peer")):
             self._setup_peer_exchange()
-        elif exchange == "peer" and self.world > 1:
+        elif exchange == "peer":
             raise ValueError("the peer exchange needs <= 8 ranks and a process group")
+        # Hybrid ticks: the rows' tiled layout over all N columns and the rows'
+        # out-degrees (whose emitting sum over all ranks sets the gate).
+        self._hybrid = None
+        wanted = propagation == "hybrid" or (propagation == "auto" and self.n_edges >= (1 << 20))
+        if propagation == "hybrid" and (batch != 1 or self._peer is None):
+            raise ValueError("the hybrid row tick takes B = 1 and the peer exchange")
+        if wanted and batch == 1 and self._peer is not None and hi > lo:
+            rowptr = in_rowptr.to(torch.int64)
+            e0, e1 = int(rowptr[lo]), int(rowptr[hi])
+            layout = _tiled.build_tiled_layout(
+                (rowptr[lo: hi + 1] - e0).to(torch.int32), in_col[e0:e1].contiguous(),
+                in_weight.detach()[e0:e1].float().contiguous(), neurons=hi - lo, cols=neurons,
+                ctas=_tiled.sm_count(device), smem_limit=_tiled.smem_limit(device))
+            out_degree = torch.bincount(in_col.to(torch.int64), minlength=neurons)[lo:hi]
+            gate = max(1, int(hybrid_gate * self.n_edges))
+            self._hybrid = (layout, out_degree.to(torch.int32).contiguous(), gate)
 
     @staticmethod
     def _validate_theta(theta, in_col, neurons, device) -> torch.Tensor:
@@ -165,6 +197,11 @@ class ShardedDendriticPELSRuntime:
         dist.barrier(group=self.group)
 
     @property
+    def propagation(self) -> str:
+        """'hybrid' (scatter or tiled propagate, chosen per tick on the device) or 'event'."""
+        return "hybrid" if self._hybrid is not None else "event"
+
+    @property
     def exchange(self) -> str:
         """'peer' (deltas exchanged inside the kernels), 'nccl' or 'none' (one rank)."""
         if self._peer is not None:
@@ -198,15 +235,26 @@ class ShardedDendriticPELSRuntime:
         s, d, a, e = inputs
         peer = self._peer
         delta = None if peer is not None else self.shard.buffers[0].view(-1)
+        hybrid = self._hybrid
         advance = self.extension.prepare_event_rows(
             s, d, a, self.params, self.persistent_current, e, self.theta, u, us, v, vs,
             row_offset=self.shard.lo, cols=self.shard.cols, delta=delta, exchange=peer,
-            out=outputs, workspace=self.workspace)
+            out=outputs, workspace=self.workspace,
+            out_degree=hybrid[1] if hybrid is not None else None)
         rowptr, dst, weight = self.csr
         scatter = self.extension.prepare_scatter_rows(
             self.batch, self.neurons, self.shard.rows, delta, rowptr, dst, weight,
             self.persistent_current, exchange=peer, workspace=self.workspace,
-            status=self.status)
+            status=self.status, gate_edges=hybrid[2] if hybrid is not None else 0)
+        if hybrid is not None:
+            propagate = self.extension.prepare_propagate_rows_gated(
+                hybrid[0], self.persistent_current, hybrid[2], workspace=self.workspace,
+                status=self.status)
+            gated_scatter = scatter
+
+            def scatter() -> None:  # below the gate the first returns, else the second
+                gated_scatter()
+                propagate()
         exchange = None
         if peer is None and self.world > 1:
             exchange = lambda: self.shard.exchange(0, self.group)  # noqa: E731

@@ -10,8 +10,9 @@ Modes (argv[1]):
            for bit like the original: prints "CHECKPOINT <case> <bool>".
   pels     row-sharded PELS with the peer and the NCCL delta exchange: 4 ticks
            against the single-GPU PELS runtime, then a CUDA-graph run; theta = 0
-           against the matrix tick and the current against W @ emitted: prints
-           "PELS <exchange>-<theta> <bool> ...".
+           against the matrix tick and the current against W @ emitted; then
+           B = 1 hybrid ticks over the peer exchange: prints
+           "PELS <exchange>-<theta> <bool> ..." and "PELS hybrid-peer <bool> ...".
   pels_timeout  rank 1 stays alive but does not launch; rank 0's scatter must
            end its bounded cross-GPU wait with status code 6: prints "STATUS <code>".
   stream   sharded stream() (per-tick drives of the rank's rows, every tick's
@@ -181,6 +182,37 @@ def pels(device, rank):
                 print(f"PELS {exchange}-{theta} {ok} diff={diff:.3g} drift={drift:.3g} "
                       f"status={status}{extra}", flush=True)
             dist.barrier()
+    # B = 1 hybrid ticks over the peer exchange: the activity of all ranks picks
+    # the scatter or the tiled propagate (gate 5 % of M: both occur).
+    init1 = init[:1].contiguous()
+    rt = ShardedDendriticPELSRuntime(graph, dyn, init1, theta=0.02, exchange="peer",
+                                     propagation="hybrid", hybrid_gate=0.05)
+    with torch.inference_mode():
+        for t in range(4):
+            rt.step(0.2 + 0.1 * t, dendritic_drive=0.1)
+        early = {name: rt.gather(name) for name in names}
+        rt.run(16, 0.3, dendritic_drive=0.1, graph_ticks=8)
+        late = {name: rt.gather(name) for name in names}
+    torch.cuda.synchronize()
+    status = int(rt.status.item())
+    mode = rt.propagation
+    rt.release_graphs()
+    rt.close()
+    if rank == 0:
+        topo = random_topology(n, m, device="cpu", seed=4, build_device=device)
+        single = NativeDendriticPELSRuntime(topo, dyn, init1.clone(), theta=0.02,
+                                            propagation="event")
+        with torch.inference_mode():
+            for t in range(4):
+                single.step(0.2 + 0.1 * t, dendritic_drive=0.1)
+        diff = max(float((early[k] - getattr(single, k)).abs().max()) for k in names)
+        product = ext.csr_propagate(topo.in_rowptr, topo.in_col, topo.in_weight,
+                                    late["emitted_state"].contiguous())
+        drift = float((late["persistent_current"] - product).abs().max())
+        ok = mode == "hybrid" and status == 0 and diff <= 2e-6 and drift <= 2e-5
+        print(f"PELS hybrid-peer {ok} diff={diff:.3g} drift={drift:.3g} status={status}",
+              flush=True)
+    dist.barrier()
 
 
 def pels_timeout(device, rank):

@@ -74,7 +74,7 @@ def test_sharded_checkpoint_restores_sharded_and_single_gpu():
 def test_sharded_pels_peer_and_nccl_exchanges_match_one_gpu():
     out = _run("pels")
     lines = [line.split() for line in out.splitlines() if line.startswith("PELS")]
-    assert len(lines) == 4, out
+    assert len(lines) == 5, out
     for _, case, ok, *diffs in lines:
         assert ok == "True", (case, diffs)
 

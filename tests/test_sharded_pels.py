@@ -193,3 +193,53 @@ def test_sharded_pels_matches_one_gpu_and_keeps_the_current_consistent(world):
     np.testing.assert_allclose(npy(_full(ranks, "persistent_current")), want, atol=2e-5, rtol=0)
     for rt in ranks:
         rt.check_status()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("gate", [1e-6, 0.15, 1.0])
+def test_hybrid_row_tick_on_a_one_rank_group_matches_one_gpu(gate):
+    """The hybrid row tick (gated scatter or tiled propagate, chosen on the
+    device from the activity counted over all ranks) with the peer exchange,
+    on a process group of one rank: it tracks the single-GPU event tick and
+    keeps current == W @ emitted, through step() and through run()'s graph.
+    gate 1e-6: every tick propagates; 1.0: every tick scatters; 0.15: both."""
+    n = 6000
+    graph = random_topology(n, 200000, device="cpu", seed=8).to("cuda")
+    model = bench_model(n)
+    initial = torch.rand(1, n, generator=torch.Generator().manual_seed(5)).cuda()
+    single = NativeDendriticPELSRuntime(graph, model, initial.clone(), theta=0.02,
+                                        propagation="event")
+    dist.init_process_group("gloo", store=dist.HashStore(), rank=0, world_size=1)
+    try:
+        rt = ShardedDendriticPELSRuntime(graph, model, initial.clone(), theta=0.02,
+                                         exchange="peer", propagation="hybrid",
+                                         hybrid_gate=gate)
+        assert rt.exchange == "peer" and rt.propagation == "hybrid"
+        drives = [0.2 + 0.1 * np.sin(0.3 * t) for t in range(4)]
+        taken = []
+        with torch.inference_mode():
+            for t in range(4):
+                rt.step(drives[t], dendritic_drive=0.1)
+                single.step(drives[t], dendritic_drive=0.1)
+                counts = rt.workspace[16:40].view(torch.int64)  # count, gate_count, gate_source
+                taken.append(int(counts[1]) >= rt._hybrid[2])
+        torch.cuda.synchronize()
+        if gate == 1e-6:
+            assert all(taken)
+        if gate == 1.0:
+            assert not any(taken)
+        for name in ("state", "dendritic_state", "adaptation_state", "emitted_state",
+                     "persistent_current"):
+            np.testing.assert_allclose(npy(getattr(rt, name)), npy(getattr(single, name)),
+                                       atol=2e-6, rtol=0, err_msg=name)
+        with torch.inference_mode():
+            for _ in range(10):
+                rt.step(0.25, dendritic_drive=0.1)
+            rt.run(32, 0.25, dendritic_drive=0.1, graph_ticks=16)
+        want = oracle.spmv(csr_of(graph), npy(rt.emitted_state))
+        np.testing.assert_allclose(npy(rt.persistent_current), want, atol=2e-5, rtol=0)
+        rt.check_status()
+        rt.release_graphs()
+        rt.close()
+    finally:
+        dist.destroy_process_group()
