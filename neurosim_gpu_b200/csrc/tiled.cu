@@ -12,10 +12,12 @@
 //   * CTA c runs stages stage_ptr[c] .. stage_ptr[c+1]-1 (normally one).
 //   * A segment is 32 rows x the stage's block: lane i owns one row, and its
 //     edges in the block form a contiguous run of its CSR row (the "piece").
-//     A segment has C chunks; chunk c of lane i holds the lane's edges
-//     4c..4c+3 at slots first + 128c + 4i + (0..3), so one 8-byte load of the
-//     16-bit columns and one vector load of the weights serve four edges, and
-//     a warp's loads cover 128 consecutive slots.  Padding slots hold column
+//     A segment has C chunks of K slots per lane (K = 4, 8, or 16 for E4M3 /
+//     NVFP4; one K per layout); chunk c of lane i holds the lane's edges
+//     Kc..Kc+K-1 at slots first + 32Kc + Ki + (0..K-1), so one load of the
+//     K 16-bit columns (8, 16 or 32 bytes) and one vector load of the
+//     weights serve K edges, and a warp's loads cover 32K consecutive slots.
+//     A lane sums its piece in CSR order whatever K is.  Padding slots hold column
 //     `block_cols` (a shared-memory zero) and weight 0.  A task is one
 //     segment (lane i's row: task_rows[32q+i] & 0x0FFFFFFF), or, for fp32,
 //     several equal segments one after the other (segment k's rows: row group
@@ -73,7 +75,7 @@ constexpr uint32_t kRowMask = 0x0FFFFFFFu;   // task_rows: row bits; kRowMask = 
 // Tag of a chunk in a consumer's ring (one 32-bit word per lane).
 constexpr uint32_t kTagValid = 1u;
 constexpr uint32_t kTagLast = 2u;   // last chunk of its task
-constexpr int kTagPhase = 2;        // NVFP4: (phase + 4c) % 16, 4 bits
+constexpr int kTagPhase = 2;        // NVFP4: (phase + K c) % 16, 4 bits
 constexpr int kTagStage = 6;        // CTA-local stage, 16 bits
 constexpr int kTagSplit = 22;       // split of the sub-task, 10 bits
 
