@@ -398,3 +398,48 @@ def test_stream_calls_reuse_their_plan(ext, kernel, n, m):
     for name in ("state", "dendritic_state", "adaptation_state"):
         assert torch.equal(getattr(streamed, name), getattr(stepped, name)), name
     streamed.check_status()
+
+
+@pytest.mark.parametrize("kernel,n,m", [("tiled", 6000, 150000), ("cluster", 1000, 20000)])
+def test_stream_replays_a_graph_for_repeated_host_buffers(ext, kernel, n, m):
+    """stream() calls that reuse the same pinned drive and output buffers (refilled
+    in place) replay one captured CUDA graph from the second such call on; a
+    call with other buffers in between runs without it.  Every call equals
+    step() bit for bit."""
+    graph = random_topology(n, m, device="cpu", seed=7).to("cuda")
+    model = bench_model(n)
+    initial = torch.rand(1, n, generator=torch.Generator().manual_seed(5)).cuda()
+    ticks = 20
+    gen = torch.Generator().manual_seed(6)
+    drives = torch.empty(ticks, 1, n).pin_memory()
+    out = torch.empty(ticks, 1, n).pin_memory()
+    stepped = NativeDendriticMatrixRuntime(graph, model, initial.clone(), kernel=kernel)
+    streamed = NativeDendriticMatrixRuntime(graph, model, initial.clone(), kernel=kernel)
+    captured = None
+    with torch.inference_mode():
+        for call in range(5):
+            fresh = call == 3  # other buffers: no graph for this call
+            values = torch.rand(ticks, 1, n, generator=gen) * 0.4
+            if fresh:
+                result = streamed.stream(values.pin_memory(), dendritic_drive=0.1)
+            else:
+                drives.copy_(values)
+                result = streamed.stream(drives, out, dendritic_drive=0.1)
+            torch.cuda.synchronize()
+            plan = streamed._rollout_plan
+            if call == 0:
+                assert plan.graph is None
+            elif call >= 1:
+                assert plan.graph is not None
+                captured = plan.graph if captured is None else captured
+                assert plan.graph is captured  # captured once, then replayed
+            got = result.clone()
+            for t in range(ticks):
+                want = stepped.step(values[t].cuda(), dendritic_drive=0.1)
+                assert torch.equal(got[t], want.cpu()), (call, t)
+            if call == 2:  # step() and run() between calls
+                streamed.step(0.3, dendritic_drive=0.1)
+                stepped.step(0.3, dendritic_drive=0.1)
+    for name in ("state", "dendritic_state", "adaptation_state"):
+        assert torch.equal(getattr(streamed, name), getattr(stepped, name)), name
+    streamed.check_status()
