@@ -583,11 +583,14 @@ ROLLOUT_CAP = 32  # longest launch of a streamed rollout on the tiled path
 
 
 def rollout_chunks(ticks: int, cap: int = ROLLOUT_CAP, first: int = 2) -> list[int]:
-    """Launch lengths of a streamed rollout of ``ticks`` ticks: ``first``, then
-    doubling up to ``cap``-tick launches, then halving back down, so that the
-    upload before the first launch and the download after the last one are
-    short and every launch's drives upload while the launch before it runs
-    (the next launch is at most twice as long)."""
+    """Launch lengths of a streamed rollout of ``ticks`` ticks: a head of
+    ``first``, 2 * ``first``, ... (doubling while the head and its mirror fit
+    and below ``cap``), the rest of the ticks in near-equal launches of at
+    most ``cap``, then the head in reverse.  The upload before the first
+    launch and the download after the last one are short, and along the head
+    each launch's drives (twice as many ticks) upload while the launch before
+    it runs.  The middle launches are not bounded by the last head launch
+    (20 ticks from 1: 1-2-4-6-4-2-1; 13: 1-2-7-2-1)."""
     head, size = [], first
     while size < cap and 2 * (sum(head) + size) <= ticks:
         head.append(size)

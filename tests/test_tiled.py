@@ -264,6 +264,29 @@ def test_sharded_layouts_split_rows_like_the_whole_graph_cpu():
             (whole.blocks, whole.block_cols, whole.split_chunks)
 
 
+
+@pytest.mark.parametrize("first,cap", [(1, 32), (2, 32), (128, 128)])
+def test_rollout_chunks_cover_the_ticks_and_ramp_cpu(first, cap):
+    """Streamed-rollout launch lengths add up to the ticks and none exceeds the
+    cap; a head doubling from ``first`` (while below the cap) opens the
+    rollout, the same head in reverse closes it, and the middle launches
+    differ by at most one tick."""
+    from neurosim_gpu_b200.tiled import rollout_chunks
+    if first == 1:
+        assert rollout_chunks(20, cap, first) == [1, 2, 4, 6, 4, 2, 1]
+        assert rollout_chunks(512, cap, first)[:6] == [1, 2, 4, 8, 16, 30]
+    for ticks in list(range(1, 200)) + [512, 1000, 4099]:
+        chunks = rollout_chunks(ticks, cap, first)
+        assert sum(chunks) == ticks and all(0 < c <= max(cap, first) for c in chunks)
+        head, size = [], first
+        while size < cap and 2 * (sum(head) + size) <= ticks:
+            head.append(size)
+            size *= 2
+        assert chunks[:len(head)] == head and chunks[len(chunks) - len(head):] == head[::-1]
+        middle = chunks[len(head):len(chunks) - len(head)]
+        assert not middle or max(middle) - min(middle) <= 1, (ticks, chunks)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("fmt", ["fp32", "nvfp4"])
 @pytest.mark.parametrize("rows_per_cta", [None, 40])
