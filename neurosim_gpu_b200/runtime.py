@@ -598,11 +598,12 @@ class _RolloutPlan:
 
     def _graph_key(self, drives, out, chunks):
         """What a captured rollout depends on, or None when the call's buffers
-        cannot be captured (pageable or non-contiguous host memory)."""
+        cannot be captured (pageable or non-contiguous host memory, or drives
+        that need a dtype conversion)."""
         if self.capture_failed:
             return None
         for t in (drives, out):
-            if not t.is_contiguous():
+            if not t.is_contiguous() or t.dtype != torch.float32:
                 return None
             if t.device.type == "cpu":
                 if not t.is_pinned():
